@@ -1,0 +1,342 @@
+"""ctypes binding of ``libdmoe_b200.so`` (the C ABI declared in ``include/dmoe_b200.h``) and
+thin torch-tensor wrappers around it.
+
+The shared library is the product's compute path.  There is no fallback: if the library is
+missing or a call fails, these functions raise.  Tensors only supply device pointers,
+sizes and the current CUDA stream; the kernels run inside the library.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Dict, Optional, Sequence, Tuple
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("DMOE_LIB", os.path.join(_PKG, "libdmoe_b200.so"))
+
+F32, F16, BF16 = 0, 1, 2
+ACT_RELU, ACT_SILU = 0, 1
+ROUTER_SOFTMAX, ROUTER_SIGMOID_GROUP = 0, 1
+
+DEVERR_NAMES = {
+    0x1: "grouped GEMM producer wait timed out",
+    0x2: "grouped GEMM MMA wait timed out",
+    0x4: "grouped GEMM epilogue wait timed out",
+    0x8: "grouped GEMM teardown wait timed out",
+    0x10: "completion flag wait timed out",
+    0x20: "invalid segment table (clamped)",
+}
+
+_DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/dmoe_b200.h
+SIGNATURES = {
+    "dmoe_version": (ctypes.c_char_p, []),
+    "dmoe_last_error": (ctypes.c_char_p, []),
+    "dmoe_launch_count": (_u64, []),
+    "dmoe_router": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32, ctypes.c_int, ctypes.c_int, _vp,
+                                   _vp, _vp, ctypes.c_int, _vp]),
+    "dmoe_route_plan_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "dmoe_route_plan": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
+                                       _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "dmoe_permute_rows": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, ctypes.c_int, _vp]),
+    "dmoe_grouped_mlp_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "dmoe_grouped_gated_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, _vp, _vp, _sz, _vp, _vp]),
+    "dmoe_combine": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, _vp, _vp]),
+    "dmoe_ipc_export": (ctypes.c_int, [_vp, _vp]),
+    "dmoe_ipc_open": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "dmoe_ipc_close": (ctypes.c_int, [_vp]),
+    "dmoe_enable_peer_access": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
+    "dmoe_copy": (ctypes.c_int, [_vp, _vp, _sz, _vp]),
+    "dmoe_flag_signal": (ctypes.c_int, [_vp, _u64, _vp]),
+    "dmoe_flag_wait": (ctypes.c_int, [_vp, _u64, _u64, _vp, _vp]),
+}
+
+_lib: Optional[ctypes.CDLL] = None
+_lib_lock = threading.Lock()
+
+
+class DMoEError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library once; raise if it is absent (the product has no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        with _lib_lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise DMoEError(f"{LIB_PATH} is missing: build it with `python -m distributedmoe_b200._build`")
+                handle = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().dmoe_last_error().decode(errors="replace")
+        raise DMoEError(f"{what} failed (status {rc}): {msg}")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise DMoEError(f"unsupported dtype {dt}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise DMoEError("dmoe kernels take CUDA tensors only (no CPU fallback)")
+        if not t.is_contiguous():
+            raise DMoEError("dmoe kernels take contiguous tensors")
+        dev = t.device if dev is None else dev
+    return dev
+
+
+# ----------------------------------------------------------------------------- scratch
+class _Scratch:
+    """Per-(device, stream) growable scratch buffers and a per-device status word."""
+
+    def __init__(self):
+        self._bufs: Dict[Tuple[int, int, str], torch.Tensor] = {}
+        self._status: Dict[int, torch.Tensor] = {}
+        self._lock = threading.Lock()
+
+    def get(self, device: torch.device, name: str, nbytes: int) -> torch.Tensor:
+        key = (device.index, _stream(device), name)
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
+
+    def status(self, device: torch.device) -> torch.Tensor:
+        with self._lock:
+            st = self._status.get(device.index)
+            if st is None:
+                st = torch.zeros(1, dtype=torch.int32, device=device)
+                self._status[device.index] = st
+            return st
+
+
+scratch = _Scratch()
+
+
+def check_device_status(device: torch.device, reset: bool = True) -> None:
+    """Raise if a kernel on `device` reported a timed-out wait or a bad segment table.
+    Synchronises with the device status word (a 4-byte read)."""
+    st = scratch.status(device)
+    v = int(st.item())
+    if v:
+        if reset:
+            st.zero_()
+        names = [n for bit, n in DEVERR_NAMES.items() if v & bit]
+        raise DMoEError(f"device reported error 0x{v:x}: {', '.join(names)}")
+
+
+# ----------------------------------------------------------------------------- ops
+def router(x: Optional[torch.Tensor], w_r: Optional[torch.Tensor], top_k: int, *, num_experts: Optional[int] = None,
+           mode: int = ROUTER_SOFTMAX, renormalize: bool = False, scale: float = 1.0,
+           logit_bias: Optional[torch.Tensor] = None, score_bias: Optional[torch.Tensor] = None, n_group: int = 1,
+           topk_group: int = 1, logits_in: Optional[torch.Tensor] = None, want_logits: bool = False,
+           w_dtype: Optional[torch.dtype] = None, out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+    """Router kernel: returns (selected [T,k] int64, weights [T,k], logits [T,E] fp32 or None)."""
+    if logits_in is not None:
+        dev = _require_cuda(logits_in)
+        T, E = logits_in.shape
+        x_dtype = torch.float32
+        d = 0
+    else:
+        dev = _require_cuda(x, w_r)
+        T, d = x.shape
+        E = w_r.shape[0]
+        x_dtype = x.dtype
+        if w_r.dtype != x.dtype or w_r.shape[1] != d:
+            raise DMoEError("router weight must be [E, d] in the dtype of x")
+    if num_experts is not None and num_experts != E:
+        raise DMoEError("num_experts mismatch")
+    w_dtype = w_dtype or (x_dtype if logits_in is None else torch.float32)
+    if out is not None:
+        idx, w = out
+    else:
+        idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
+        w = torch.empty(T, top_k, dtype=w_dtype, device=dev)
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if (want_logits and logits_in is None) else None
+    for b in (logit_bias, score_bias):
+        if b is not None and (b.dtype != torch.float32 or b.numel() != E):
+            raise DMoEError("router biases must be fp32 [E]")
+    rc = lib().dmoe_router(_ptr(x) if logits_in is None else None, _ptr(w_r) if logits_in is None else None,
+                           dtype_code(x_dtype), _ptr(logit_bias), _ptr(score_bias), _ptr(logits_in), T, d, E, top_k,
+                           mode, int(renormalize), float(scale), n_group, topk_group, _ptr(logits), idx.data_ptr(),
+                           w.data_ptr(), dtype_code(w.dtype), _stream(dev))
+    _check(rc, "dmoe_router")
+    return idx, w, logits
+
+
+def route_plan(idx: torch.Tensor, w: Optional[torch.Tensor], num_experts: int, *, want_slot: bool = True,
+               want_inverse: bool = True, want_weight: bool = True) -> Dict[str, torch.Tensor]:
+    """Routing-plan kernels: counts, offsets, perm_token (+ perm_slot, inverse, perm_weight)."""
+    dev = _require_cuda(idx, w)
+    if idx.dtype != torch.int64:
+        raise DMoEError("selected experts must be int64")
+    T, k = idx.shape
+    n = T * k
+    E = num_experts
+    res = {
+        "counts": torch.empty(E, dtype=torch.int32, device=dev),
+        "offsets": torch.empty(E + 1, dtype=torch.int32, device=dev),
+        "perm_token": torch.empty(n, dtype=torch.int32, device=dev),
+    }
+    if want_slot:
+        res["perm_slot"] = torch.empty(n, dtype=torch.int32, device=dev)
+    if want_inverse:
+        res["inverse"] = torch.empty(n, dtype=torch.int32, device=dev)
+    if want_weight and w is not None:
+        res["perm_weight"] = torch.empty(n, dtype=w.dtype, device=dev)
+    ws_bytes = lib().dmoe_route_plan_workspace_size(T, k, E)
+    ws = scratch.get(dev, "plan", ws_bytes)
+    rc = lib().dmoe_route_plan(idx.data_ptr(), _ptr(w), dtype_code(w.dtype) if w is not None else BF16, T, k, E,
+                               res["counts"].data_ptr(), res["offsets"].data_ptr(), res["perm_token"].data_ptr(),
+                               _ptr(res.get("perm_slot")), _ptr(res.get("inverse")), _ptr(res.get("perm_weight")),
+                               ws.data_ptr(), ws.numel(), _stream(dev))
+    _check(rc, "dmoe_route_plan")
+    return res
+
+
+def _i32_array(vals: Sequence[int]):
+    arr = (ctypes.c_int32 * max(len(vals), 1))(*[int(v) for v in vals])
+    return arr
+
+
+def permute_rows(src: torch.Tensor, dst: torch.Tensor, seg_src: Sequence[int], seg_dst: Sequence[int],
+                 seg_len: Sequence[int], row_map: Optional[torch.Tensor] = None, dst_ptr: Optional[int] = None,
+                 stream: Optional[int] = None) -> None:
+    """dst[seg_dst[i] + r] = src[row_map[seg_src[i] + r] if row_map else seg_src[i] + r].
+    ``dst_ptr`` overrides dst's pointer (a peer GPU buffer), keeping dst for shape/dtype."""
+    dev = _require_cuda(src, row_map)
+    row_bytes = src.shape[-1] * src.element_size()
+    if dst.shape[-1] * dst.element_size() != row_bytes:
+        raise DMoEError("src and dst rows differ in size")
+    n = len(seg_len)
+    rc = lib().dmoe_permute_rows(src.data_ptr(), dst_ptr if dst_ptr is not None else dst.data_ptr(), row_bytes,
+                                 _ptr(row_map), _i32_array(seg_src), _i32_array(seg_dst), _i32_array(seg_len), n,
+                                 stream if stream is not None else _stream(dev))
+    _check(rc, "dmoe_permute_rows")
+
+
+def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
+                      seg_expert, seg_end, act: int, Y: torch.Tensor, m_rows: Optional[int] = None) -> None:
+    """Grouped expert MLP over row segments.  seg_expert/seg_end: Python int sequences (host
+    table) or int32 CUDA tensors (device table)."""
+    dev = _require_cuda(X, w_gate, w_up, w_down, Y)
+    E, I, d = w_gate.shape
+    if w_up.shape != (E, I, d) or w_down.shape != (E, d, I):
+        raise DMoEError("expert stacks must be gate/up [E, I, d] and down [E, d, I]")
+    if X.shape[1] != d or Y.shape[1] != d:
+        raise DMoEError("X and Y must be [rows, d]")
+    if not (X.dtype == w_gate.dtype == w_up.dtype == w_down.dtype == Y.dtype):
+        raise DMoEError("grouped MLP operands must share one dtype")
+    m_rows = X.shape[0] if m_rows is None else m_rows
+    dt = dtype_code(X.dtype)
+    ws = scratch.get(dev, "mlp", lib().dmoe_grouped_mlp_workspace_size(m_rows, I, dt))
+    if isinstance(seg_expert, torch.Tensor):
+        n_seg = seg_expert.numel()
+        se, sn, on_dev = seg_expert.data_ptr(), seg_end.data_ptr(), 1
+        keep = None
+    else:
+        n_seg = len(seg_expert)
+        a1, a2 = _i32_array(seg_expert), _i32_array(seg_end)
+        se, sn, on_dev = ctypes.addressof(a1), ctypes.addressof(a2), 0
+        keep = (a1, a2)
+    rc = lib().dmoe_grouped_gated_mlp(X.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
+                                      se, sn, n_seg, on_dev, m_rows, act, Y.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      scratch.status(dev).data_ptr(), _stream(dev))
+    del keep
+    _check(rc, "dmoe_grouped_gated_mlp")
+
+
+def combine(rows: torch.Tensor, inverse: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
+            accumulate: bool = False) -> None:
+    """out[t] = (out[t] if accumulate) + sum_s w[t,s] * rows[inverse[t*k+s]] (fp32 accumulate)."""
+    dev = _require_cuda(rows, inverse, w, out)
+    T, k = w.shape
+    d = out.shape[-1]
+    if rows.dtype != out.dtype:
+        raise DMoEError("rows and out must share a dtype")
+    rc = lib().dmoe_combine(rows.data_ptr(), inverse.data_ptr(), w.data_ptr(), dtype_code(w.dtype), T, k, d,
+                            dtype_code(out.dtype), int(accumulate), out.data_ptr(), _stream(dev))
+    _check(rc, "dmoe_combine")
+
+
+# ----------------------------------------------------------------------------- transfer
+def ipc_export(t: torch.Tensor) -> bytes:
+    buf = (ctypes.c_uint8 * 64)()
+    _check(lib().dmoe_ipc_export(t.data_ptr(), buf), "dmoe_ipc_export")
+    return bytes(buf)
+
+
+def ipc_open(handle: bytes, device: int) -> int:
+    if len(handle) != 64:
+        raise DMoEError("IPC handle must be 64 bytes")
+    buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+    out = _vp()
+    _check(lib().dmoe_ipc_open(buf, device, ctypes.byref(out)), "dmoe_ipc_open")
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().dmoe_ipc_close(ptr), "dmoe_ipc_close")
+
+
+def enable_peer_access(device: int, peer: int) -> None:
+    _check(lib().dmoe_enable_peer_access(device, peer), "dmoe_enable_peer_access")
+
+
+def copy_bytes(dst_ptr: int, src_ptr: int, nbytes: int, stream: int) -> None:
+    _check(lib().dmoe_copy(dst_ptr, src_ptr, nbytes, stream), "dmoe_copy")
+
+
+def flag_signal(flag_ptr: int, value: int, stream: int) -> None:
+    _check(lib().dmoe_flag_signal(flag_ptr, value, stream), "dmoe_flag_signal")
+
+
+def flag_wait(flag_ptr: int, value: int, timeout_ns: int, status_ptr: int, stream: int) -> None:
+    _check(lib().dmoe_flag_wait(flag_ptr, value, timeout_ns, status_ptr, stream), "dmoe_flag_wait")
+
+
+def launch_count() -> int:
+    return int(lib().dmoe_launch_count())

@@ -1,0 +1,661 @@
+// Grouped expert gated MLP on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the grouped path of ExpertsBlockPipelineTask.run (MoE/PipelineTask.py:478-520):
+//   gate_out = grouped_mm(X, Wg^T, offs); up_out = grouped_mm(X, Wu^T, offs)
+//   h = relu(gate_out) * up_out;           Y = grouped_mm(h, Wd^T, offs)
+// where offs are the cumulative (padded) ends of the per-expert row segments of one buffer.
+// The reference also copies the active experts' weights each run (:511-513); here the
+// kernels index the stacked weights by expert id through a 3-D TMA descriptor instead.
+//
+// Two launches of one persistent, warp-specialised kernel template:
+//   GEMM1 (gated): tile = 128 rows x (128 gate + 128 up) columns, K = d.  The MMA is
+//                  M=128, N=256: the B tile stacks the gate rows and the matching up rows,
+//                  so one accumulator holds both halves and the epilogue writes
+//                  h = act(gate) * up (128 columns) straight from TMEM.
+//   GEMM2 (plain): tile = 128 rows x 256 columns of Y, K = I.
+// Roles per CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [256 x 64] per stage, SW128
+//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma (K=16) per stage
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, activation, 16-byte stores
+// Smem ring of 4 stages (48 KB each); TMEM holds two 256-column fp32 accumulators so the
+// epilogue of tile i overlaps the MMAs of tile i+1.  Every mbarrier wait is bounded by time
+// and reports through the caller's device status word instead of hanging.
+#include <cuda.h>
+
+#include "dmoe_common.cuh"
+
+namespace dmoe {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;    // one 128-byte swizzle atom of 16-bit elements
+constexpr int BN = 256;   // MMA N
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int kThreads = 192;
+constexpr int kMaxSegDev = 1024;
+constexpr int kMaxSegParam = 256;
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+constexpr int kBarBytes = 256;
+constexpr int kSegBytes = 4 * (kMaxSegDev + 1) * 4;
+constexpr int kSmemBytes = 1024 /*align slack*/ + STAGES * STAGE_BYTES + kBarBytes + kSegBytes;
+
+struct GemmSegs {
+  int n_seg;
+  int m_rows;
+  int e_stack;
+  const int32_t* dev_expert;
+  const int32_t* dev_end;
+  int32_t expert[kMaxSegParam];
+  int32_t end[kMaxSegParam];
+};
+
+struct GemmArgs {
+  void* out;
+  int64_t ldo;      // elements between output rows
+  int n_out;        // valid output columns
+  int K;            // reduction length
+  int n_tiles_n;    // output column tiles
+  int raster_n_fast;
+  int act;
+  int32_t* status;
+};
+
+// ------------------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: true once the phase of `parity` completed; false on timeout or when another
+// role of this CTA already gave up (abort flag).
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
+                                       int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      atomicOr(status, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+#define DMOE_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), "=r"(r[b + 4]), "=r"(r[b + 5]), \
+                   "=r"(r[b + 6]), "=r"(r[b + 7])
+#define DMOE_S8(b) "=r"(s[b + 0]), "=r"(s[b + 1]), "=r"(s[b + 2]), "=r"(s[b + 3]), "=r"(s[b + 4]), "=r"(s[b + 5]), \
+                   "=r"(s[b + 6]), "=r"(s[b + 7])
+
+// 32 lanes x 32 consecutive fp32 columns, then wait: the outputs exist only after the wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : DMOE_R8(0), DMOE_R8(8), DMOE_R8(16), DMOE_R8(24)
+      : "r"(taddr)
+      : "memory");
+}
+
+// Two 32-column loads (gate part and up part of the accumulator) and one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, uint32_t (&r)[32], uint32_t (&s)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, "
+      "%46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : DMOE_R8(0), DMOE_R8(8), DMOE_R8(16), DMOE_R8(24), DMOE_S8(0), DMOE_S8(8), DMOE_S8(16), DMOE_S8(24)
+      : "r"(ta), "r"(tb)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle layout written by
+// TMA (rows of 128 bytes, 8-row groups 1024 bytes apart): LBO = 16 B (unused), SBO = 1024 B,
+// descriptor version 1 (sm_100), layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D fp32, A/B f16 or bf16, both K-major, M=128, N=256.
+template <int DT>
+__host__ __device__ constexpr uint32_t make_idesc() {
+  return (1u << 4) | ((DT == DMOE_BF16 ? 1u : 0u) << 7) | ((DT == DMOE_BF16 ? 1u : 0u) << 10) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ float act_fn(float g, int act) {
+  return act == DMOE_ACT_SILU ? g / (1.f + __expf(-g)) : fmaxf(g, 0.f);
+}
+
+struct TileInfo {
+  int row0, row_end, expert, nt;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(int tile, int total_m, int n_tiles_n, int raster_n_fast, int n_seg,
+                                                const int32_t* s_start, const int32_t* s_end,
+                                                const int32_t* s_expert, const int32_t* s_tile) {
+  int mt, nt;
+  if (raster_n_fast) {
+    mt = tile / n_tiles_n;
+    nt = tile - mt * n_tiles_n;
+  } else {
+    nt = tile / total_m;
+    mt = tile - nt * total_m;
+  }
+  int lo = 0, hi = n_seg - 1;  // last segment whose first tile is <= mt (skips empty segments)
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_tile[mid] <= mt) lo = mid; else hi = mid - 1;
+  }
+  TileInfo ti;
+  ti.row0 = s_start[lo] + (mt - s_tile[lo]) * BM;
+  ti.row_end = s_end[lo];
+  ti.expert = s_expert[lo];
+  ti.nt = nt;
+  return ti;
+}
+
+template <bool GATED, int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
+                        const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ GemmSegs segs,
+                        const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* fin = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_start = reinterpret_cast<int32_t*>(smem + STAGES * STAGE_BYTES + kBarBytes);
+  int32_t* s_end = s_start + (kMaxSegDev + 1);
+  int32_t* s_expert = s_end + (kMaxSegDev + 1);
+  int32_t* s_tile = s_expert + (kMaxSegDev + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_seg = segs.n_seg;
+
+  for (int i = threadIdx.x; i < n_seg; i += blockDim.x) {
+    s_expert[i] = segs.dev_expert ? segs.dev_expert[i] : segs.expert[i];
+    s_end[i] = segs.dev_end ? segs.dev_end[i] : segs.end[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev = 0, tiles = 0, bad = 0;
+    for (int i = 0; i < n_seg; ++i) {
+      int en = s_end[i];
+      if (en < prev || en > segs.m_rows) {
+        bad = 1;
+        en = en < prev ? prev : segs.m_rows;
+      }
+      int e = s_expert[i];
+      int len = en - prev;
+      if (e < 0 || e >= segs.e_stack) {
+        bad = 1;
+        len = 0;
+        s_expert[i] = 0;
+      }
+      s_start[i] = prev;
+      s_end[i] = prev + len;
+      s_tile[i] = tiles;
+      tiles += (len + BM - 1) / BM;
+      prev = en;
+    }
+    s_tile[n_seg] = tiles;
+    if (bad && blockIdx.x == 0) atomicOr(args.status, DMOE_DEVERR_BAD_SEGMENT);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 4);
+    }
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_m = s_tile[n_seg];
+  const int total = total_m * args.n_tiles_n;
+  const int nk = (args.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t armed = 0, armed_ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TileInfo ti = decode_tile(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+                                        s_expert, s_tile);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sa, &tm_a, &full[stage], kb * BK, ti.row0);
+          if constexpr (GATED) {
+            tma_load_3d(sb, &tm_b0, &full[stage], kb * BK, ti.nt * (BN / 2), ti.expert);
+            tma_load_3d(sb + B_BYTES / 2, &tm_b1, &full[stage], kb * BK, ti.nt * (BN / 2), ti.expert);
+          } else {
+            tma_load_3d(sb, &tm_b0, &full[stage], kb * BK, ti.nt * BN, ti.expert);
+          }
+          armed |= 1u << stage;
+          armed_ph = (armed_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Every copy this thread started must land before the CTA exits.
+      for (int s = 0; s < STAGES; ++s) {
+        if (armed >> s & 1u) {
+          const uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(&full[s], armed_ph >> s & 1u)) {
+            if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+              atomicOr(args.status, DMOE_DEVERR_TIMEOUT_TEARDOWN);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc<DT>();
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        if (!mbar_wait(&acce[acc], acc_ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sdesc_sw128(smem_u32(smem + stage * STAGE_BYTES));
+          const uint64_t bd = sdesc_sw128(smem_u32(smem + stage * STAGE_BYTES + A_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // K=16 per MMA: +32 bytes = +2 in the address field
+            umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&accf[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1u;
+      }
+      // All MMAs issued by this thread complete before TMEM is released.
+      umma_commit(fin);
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(fin, 0)) {
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(args.status, DMOE_DEVERR_TIMEOUT_TEARDOWN);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const TileInfo ti = decode_tile(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+                                      s_expert, s_tile);
+      const bool got = mbar_wait(&accf[acc], acc_ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int row = ti.row0 + q * 32 + lane;
+      const bool valid = row < ti.row_end;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (GATED) {
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          uint32_t g[32], u[32];
+          __syncwarp();
+          tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
+          const int col0 = ti.nt * (BN / 2) + j * 32;
+          if (valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
+              const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
+              pk[i] = pack2<DT>(h0, h1);
+            }
+            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col0 + v * 8 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t y[32];
+          __syncwarp();
+          tmem_ld32(tbase + j * 32, y);
+          const int col0 = ti.nt * BN + j * 32;
+          if (valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
+            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col0 + v * 8 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------- host side
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+// rank-2 or rank-3 row-major tensor; dims innermost first; box innermost first.
+int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_t* dims, const uint32_t* box) {
+  PFN_encodeTiled enc = get_encode_fn();
+  DMOE_REQUIRE(enc != nullptr, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t gdim[3], gstride[2];
+  cuuint32_t bdim[3], estr[3] = {1, 1, 1};
+  uint64_t stride = 2;
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    if (i > 0) gstride[i - 1] = stride;
+    stride *= dims[i];
+  }
+  CUresult r = enc(map, dt == DMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return DMOE_ERR_CUDA;
+  }
+  return DMOE_OK;
+}
+
+template <bool GATED, int DT>
+int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
+                const GemmArgs& args, int grid, cudaStream_t stream) {
+  static int configured_device = -1;
+  int dev = 0;
+  DMOE_CUDA(cudaGetDevice(&dev));
+  if (configured_device != dev) {
+    DMOE_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GATED, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSmemBytes));
+    configured_device = dev;
+  }
+  grouped_gemm_kernel<GATED, DT><<<grid, kThreads, kSmemBytes, stream>>>(a, b0, b1, segs, args);
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <int DT>
+int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack, int d, int I,
+            const GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
+            cudaStream_t stream) {
+  CUtensorMap ta, tg, tu, th, td;
+  {
+    const uint64_t dims[2] = {(uint64_t)d, (uint64_t)m_rows};
+    const uint32_t box[2] = {BK, BM};
+    int r = make_map(&ta, DT, X, 2, dims, box);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)d, (uint64_t)I, (uint64_t)E_stack};
+    const uint32_t box[3] = {BK, BN / 2, 1};
+    int r = make_map(&tg, DT, w_gate, 3, dims, box);
+    if (r) return r;
+    r = make_map(&tu, DT, w_up, 3, dims, box);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)I, (uint64_t)m_rows};
+    const uint32_t box[2] = {BK, BM};
+    int r = make_map(&th, DT, H, 2, dims, box);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
+    const uint32_t box[3] = {BK, BN, 1};
+    int r = make_map(&td, DT, w_down, 3, dims, box);
+    if (r) return r;
+  }
+  const int sms = sm_count();
+  const int nt1 = (I + BN / 2 - 1) / (BN / 2);
+  const int nt2 = (d + BN - 1) / BN;
+  int g1 = sms, g2 = sms;
+  if (total_m_host >= 0) {
+    const int64_t t1 = (int64_t)total_m_host * nt1, t2 = (int64_t)total_m_host * nt2;
+    if (t1 == 0) return DMOE_OK;
+    g1 = (int)(t1 < sms ? t1 : sms);
+    g2 = (int)(t2 < sms ? t2 : sms);
+  }
+  GemmArgs a1{H, I, I, d, nt1, 0, act, status};
+  int r = launch_gemm<true, DT>(ta, tg, tu, segs, a1, g1, stream);
+  if (r) return r;
+  GemmArgs a2{Y, d, d, I, nt2, 1, act, status};
+  return launch_gemm<false, DT>(th, td, td, segs, a2, g2, stream);
+}
+
+}  // namespace
+}  // namespace dmoe
+
+using namespace dmoe;
+
+extern "C" size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype) {
+  (void)dtype;
+  return (size_t)m_rows * (size_t)I * 2 + 256;
+}
+
+extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down,
+                                      int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
+                                      const int32_t* seg_end, int n_seg, int seg_on_device, int m_rows, int act,
+                                      void* Y, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                      void* stream) {
+  clear_error();
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_grouped_gated_mlp: dtype must be f16 or bf16");
+  DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "dmoe_grouped_gated_mlp: bad activation %d", act);
+  DMOE_REQUIRE(d > 0 && I > 0 && d % 8 == 0 && I % 8 == 0, "dmoe_grouped_gated_mlp: d=%d, I=%d must be multiples of 8",
+               d, I);
+  DMOE_REQUIRE(E_stack >= 1 && m_rows >= 0, "dmoe_grouped_gated_mlp: bad E_stack/m_rows");
+  DMOE_REQUIRE(n_seg >= 0, "dmoe_grouped_gated_mlp: bad n_seg");
+  if (n_seg == 0 || m_rows == 0) return DMOE_OK;
+  DMOE_REQUIRE(X && w_gate && w_up && w_down && Y && workspace && dev_status && seg_expert && seg_end,
+               "dmoe_grouped_gated_mlp: null pointer");
+  DMOE_REQUIRE(aligned16(X) && aligned16(w_gate) && aligned16(w_up) && aligned16(w_down) && aligned16(Y) &&
+                   aligned16(workspace),
+               "dmoe_grouped_gated_mlp: tensors must be 16-byte aligned");
+  DMOE_REQUIRE(workspace_bytes >= dmoe_grouped_mlp_workspace_size(m_rows, I, dtype),
+               "dmoe_grouped_gated_mlp: workspace %zu < %zu bytes", workspace_bytes,
+               dmoe_grouped_mlp_workspace_size(m_rows, I, dtype));
+  static thread_local GemmSegs segs;
+  segs.n_seg = n_seg;
+  segs.m_rows = m_rows;
+  segs.e_stack = E_stack;
+  int total_m = -1;
+  if (seg_on_device) {
+    DMOE_REQUIRE(n_seg <= kMaxSegDev, "dmoe_grouped_gated_mlp: n_seg=%d > %d", n_seg, kMaxSegDev);
+    segs.dev_expert = seg_expert;
+    segs.dev_end = seg_end;
+  } else {
+    DMOE_REQUIRE(n_seg <= kMaxSegParam, "dmoe_grouped_gated_mlp: n_seg=%d > %d for host segment tables", n_seg,
+                 kMaxSegParam);
+    segs.dev_expert = nullptr;
+    segs.dev_end = nullptr;
+    int prev = 0;
+    total_m = 0;
+    for (int i = 0; i < n_seg; ++i) {
+      DMOE_REQUIRE(seg_end[i] >= prev && seg_end[i] <= m_rows, "dmoe_grouped_gated_mlp: segment %d end %d invalid", i,
+                   seg_end[i]);
+      DMOE_REQUIRE(seg_expert[i] >= 0 && seg_expert[i] < E_stack, "dmoe_grouped_gated_mlp: segment %d expert %d", i,
+                   seg_expert[i]);
+      segs.expert[i] = seg_expert[i];
+      segs.end[i] = seg_end[i];
+      total_m += (seg_end[i] - prev + BM - 1) / BM;
+      prev = seg_end[i];
+    }
+  }
+  void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DMOE_BF16)
+    return run_mlp<DMOE_BF16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s);
+  return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s);
+}

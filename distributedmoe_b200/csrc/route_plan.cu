@@ -1,0 +1,176 @@
+// Routing plan: stable counting sort of the T*k activations by expert.
+//
+// Replaces the one-hot mask and the per-expert torch.where loop of
+// MoE/DistMoEBlock.py:568-605.  torch.where(expert_mask[e]) on the [k, T] slice lists an
+// expert's activations slot-major, then by ascending token.  Walking the activations in
+// that flattened order f = s*T + t and sorting stably by expert reproduces it exactly, for
+// all experts at once, without a host synchronisation per expert.
+//
+// Three launches:
+//   1. plan_hist    : chunk c of the flattened order -> hist[c][e]        (smem atomics)
+//   2. plan_scan    : counts, offsets, and base[c][e] = offsets[e] + sum_{c'<c} hist[c'][e]
+//   3. plan_scatter : each chunk ranks its activations stably (warp match + per-warp
+//                     prefix) and writes perm_token / perm_slot / inverse / perm_weight.
+#include "dmoe_common.cuh"
+
+namespace dmoe {
+namespace {
+
+constexpr int kChunk = 2048;       // activations per CTA
+constexpr int kPlanThreads = 256;  // 8 warps
+constexpr int kMaxPlanExperts = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_hist(const int64_t* idx, int T, int k, int E, int32_t* hist) {
+  extern __shared__ int32_t s_hist[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
+  __syncthreads();
+  const int64_t n = (int64_t)T * k;
+  const int64_t f0 = (int64_t)blockIdx.x * kChunk;
+  for (int64_t f = f0 + threadIdx.x; f < f0 + kChunk && f < n; f += blockDim.x) {
+    const int s = (int)(f / T), t = (int)(f % T);
+    const int e = (int)idx[(int64_t)t * k + s];
+    if (e >= 0 && e < E) atomicAdd(&s_hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(int64_t)blockIdx.x * E + e] = s_hist[e];
+}
+
+// One CTA of up to 1024 threads; thread e owns expert e (loops if E > blockDim).
+__global__ void plan_scan(int32_t* hist, int n_chunks, int E, int32_t* counts, int32_t* offsets) {
+  __shared__ int32_t s_cnt[kMaxPlanExperts];
+  __shared__ int32_t s_warp[32];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int32_t c = 0;
+    for (int j = 0; j < n_chunks; ++j) c += hist[(int64_t)j * E + e];
+    s_cnt[e] = c;
+    counts[e] = c;
+  }
+  __syncthreads();
+  // exclusive scan of s_cnt over E (E <= 1024 = blockDim): one value per thread
+  const int e = threadIdx.x;
+  int32_t v = e < E ? s_cnt[e] : 0;
+  const int lane = e & 31, warp = e >> 5;
+  int32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) / 32;
+    int32_t w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += u;
+    }
+    if (lane < nw) s_warp[lane] = w;
+  }
+  __syncthreads();
+  const int32_t excl = incl - v + (warp > 0 ? s_warp[warp - 1] : 0);
+  if (e < E) offsets[e] = excl;
+  if (e == E - 1) offsets[E] = excl + v;
+  __syncthreads();
+  // base[c][e] = offsets[e] + sum_{c' < c} hist[c'][e]  (in place)
+  for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+    int32_t run = offsets[ee];
+    for (int j = 0; j < n_chunks; ++j) {
+      const int32_t h = hist[(int64_t)j * E + ee];
+      hist[(int64_t)j * E + ee] = run;
+      run += h;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_scatter(const int64_t* idx, const void* w, int w_dtype, int T,
+                                                             int k, int E, const int32_t* base, int32_t* perm_token,
+                                                             int32_t* perm_slot, int32_t* inverse, void* perm_weight) {
+  extern __shared__ int32_t smem[];
+  int32_t* s_run = smem;                 // [E] running position of each expert in this chunk
+  int32_t* s_wcnt = smem + E;            // [8][E] per-warp counts of the current round
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = kPlanThreads / 32;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_run[e] = base[(int64_t)blockIdx.x * E + e];
+  const int64_t n = (int64_t)T * k;
+  const int64_t f0 = (int64_t)blockIdx.x * kChunk;
+  for (int64_t r0 = f0; r0 < f0 + kChunk && r0 < n; r0 += kPlanThreads) {
+    for (int i = threadIdx.x; i < nwarps * E; i += blockDim.x) s_wcnt[i] = 0;
+    __syncthreads();
+    const int64_t f = r0 + threadIdx.x;
+    const bool valid = f < f0 + kChunk && f < n;
+    int s = 0, t = 0, e = -1;
+    if (valid) {
+      s = (int)(f / T);
+      t = (int)(f % T);
+      e = (int)idx[(int64_t)t * k + s];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+    const int leader = __ffs(peers) - 1;
+    if (e >= 0 && lane == leader) s_wcnt[warp * E + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int pos = s_run[e] + rank_in_warp;
+      for (int w2 = 0; w2 < warp; ++w2) pos += s_wcnt[w2 * E + e];
+      perm_token[pos] = t;
+      if (perm_slot) perm_slot[pos] = s;
+      if (inverse) inverse[(int64_t)t * k + s] = pos;
+      if (perm_weight) {
+        const float wv = load_as_float(w, (int64_t)t * k + s, w_dtype);
+        store_from_float(perm_weight, pos, wv, w_dtype);
+      }
+    }
+    __syncthreads();
+    for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+      int32_t add = 0;
+      for (int w2 = 0; w2 < nwarps; ++w2) add += s_wcnt[w2 * E + ee];
+      s_run[ee] += add;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+}  // namespace dmoe
+
+using namespace dmoe;
+
+extern "C" size_t dmoe_route_plan_workspace_size(int T, int k, int E) {
+  const int64_t n = (int64_t)T * k;
+  const int64_t chunks = n > 0 ? (n + kChunk - 1) / kChunk : 1;
+  return (size_t)(chunks * (int64_t)E * sizeof(int32_t));
+}
+
+extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E, int32_t* counts,
+                               int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse,
+                               void* perm_weight, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(E >= 1 && E <= kMaxPlanExperts, "dmoe_route_plan: need 1 <= E <= %d (E=%d)", kMaxPlanExperts, E);
+  DMOE_REQUIRE(T >= 0 && k >= 1 && (int64_t)T * k < (1ll << 31), "dmoe_route_plan: bad T=%d k=%d", T, k);
+  DMOE_REQUIRE(counts && offsets && perm_token && workspace, "dmoe_route_plan: null pointer");
+  DMOE_REQUIRE(perm_weight == nullptr || (w != nullptr && dtype_ok(w_dtype)), "dmoe_route_plan: perm_weight needs w");
+  DMOE_REQUIRE(workspace_bytes >= dmoe_route_plan_workspace_size(T, k, E), "dmoe_route_plan: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  const int64_t n = (int64_t)T * k;
+  const int chunks = n > 0 ? (int)((n + kChunk - 1) / kChunk) : 0;
+  int32_t* hist = reinterpret_cast<int32_t*>(workspace);
+  if (chunks > 0) {
+    plan_hist<<<chunks, kPlanThreads, E * sizeof(int32_t), s>>>(idx, T, k, E, hist);
+    DMOE_LAUNCH_CHECK();
+  }
+  const int scan_threads = E <= 32 ? 32 : ((E + 31) / 32) * 32;
+  plan_scan<<<1, scan_threads, 0, s>>>(hist, chunks, E, counts, offsets);
+  DMOE_LAUNCH_CHECK();
+  if (chunks > 0) {
+    const size_t smem = (size_t)E * sizeof(int32_t) * (1 + kPlanThreads / 32);
+    if (smem > 48 * 1024)
+      DMOE_CUDA(cudaFuncSetAttribute(plan_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    plan_scatter<<<chunks, kPlanThreads, smem, s>>>(idx, w, w_dtype, T, k, E, hist, perm_token, perm_slot, inverse,
+                                                    perm_weight);
+    DMOE_LAUNCH_CHECK();
+  }
+  return DMOE_OK;
+}

@@ -1,0 +1,283 @@
+// Router: fp32 logits, softmax (or sigmoid + group-limited) top-k, routing weights.
+//
+// Replaces MoE/DistMoEBlock.py:556-562 of the reference:
+//   router_logits = self.gate(x); routing_weights = softmax(logits, dim=1, dtype=float)
+//   routing_weights, selected = torch.topk(routing_weights, top_k); .to(dtype)
+// One warp owns one token: the dot products with the E router rows are split over the
+// lanes in 16-byte chunks of the token's row and reduced with shuffles; selection is k
+// rounds of a warp arg-max (ties resolve to the lower expert index).
+#include "dmoe_common.cuh"
+
+namespace dmoe {
+namespace {
+
+constexpr int kRouterWarps = 8;
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 16;
+constexpr int kExpertGroup = 8;  // experts whose dot products one pass over the row computes
+
+template <int DT>
+struct VecTraits {
+  static constexpr int kElems = 8;
+};
+template <>
+struct VecTraits<DMOE_F32> {
+  static constexpr int kElems = 4;
+};
+
+template <int DT>
+__device__ __forceinline__ void load_vec(const void* base, int64_t elem_off, float* f) {
+  const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(base) + elem_off * (DT == DMOE_F32 ? 4 : 2));
+  if constexpr (DT == DMOE_F32) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  } else {
+    unpack8<DT>(v, f);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Arg-max over the warp of (value, index): larger value wins, equal values -> lower index.
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+struct RouterArgs {
+  const void* x;
+  const void* w_r;
+  const float* logit_bias;
+  const float* score_bias;
+  const float* logits_in;
+  float* logits_out;
+  int64_t* idx_out;
+  void* w_out;
+  int T, d, E, k, mode, renormalize, n_group, topk_group, w_dtype;
+  float scale;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a) {
+  __shared__ float s_logit[kRouterWarps][kMaxExperts];
+  __shared__ float s_gscore[kRouterWarps][32];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = a.E;
+  constexpr int VE = VecTraits<DT>::kElems;
+  const int nvec = a.d / VE;
+
+  for (int t = blockIdx.x * kRouterWarps + warp; t < a.T; t += gridDim.x * kRouterWarps) {
+    // ---------------------------------------------------------------- logits
+    if (a.logits_in != nullptr) {
+      for (int e = lane; e < E; e += 32) s_logit[warp][e] = a.logits_in[(int64_t)t * E + e];
+    } else {
+      for (int e0 = 0; e0 < E; e0 += kExpertGroup) {
+        float acc[kExpertGroup];
+#pragma unroll
+        for (int i = 0; i < kExpertGroup; ++i) acc[i] = 0.f;
+        for (int c = lane; c < nvec; c += 32) {
+          float xv[VE];
+          load_vec<DT>(a.x, (int64_t)t * a.d + (int64_t)c * VE, xv);
+#pragma unroll
+          for (int i = 0; i < kExpertGroup; ++i) {
+            if (e0 + i < E) {
+              float wv[VE];
+              load_vec<DT>(a.w_r, (int64_t)(e0 + i) * a.d + (int64_t)c * VE, wv);
+#pragma unroll
+              for (int j = 0; j < VE; ++j) acc[i] = fmaf(xv[j], wv[j], acc[i]);
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kExpertGroup; ++i) acc[i] = warp_sum(acc[i]);
+        if (lane < kExpertGroup && e0 + lane < E) {
+          float v = acc[0];
+#pragma unroll
+          for (int i = 1; i < kExpertGroup; ++i)
+            if (lane == i) v = acc[i];
+          if (a.logit_bias) v += a.logit_bias[e0 + lane];
+          s_logit[warp][e0 + lane] = v;
+        }
+      }
+      __syncwarp();
+      if (a.logits_out)
+        for (int e = lane; e < E; e += 32) a.logits_out[(int64_t)t * E + e] = s_logit[warp][e];
+    }
+    __syncwarp();
+
+    // ---------------------------------------------------------------- selection
+    constexpr int NJ = kMaxExperts / 32;
+    float sel_val[NJ];   // value used for ranking
+    float wgt[NJ];       // value reported as the routing weight
+    uint32_t avail = 0;  // bit j: expert lane + 32 j is selectable
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int e = lane + 32 * j;
+      sel_val[j] = -INFINITY;
+      wgt[j] = 0.f;
+      if (e < E) {
+        sel_val[j] = s_logit[warp][e];
+        avail |= 1u << j;
+      }
+    }
+    if (a.mode == DMOE_ROUTER_SOFTMAX) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) m = fmaxf(m, sel_val[j]);
+      m = warp_max(m);
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        wgt[j] = (avail >> j & 1u) ? expf(sel_val[j] - m) : 0.f;
+        s += wgt[j];
+      }
+      s = warp_sum(s);
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) wgt[j] = wgt[j] / s;
+      // softmax is monotone in the logits: rank by the logits themselves
+    } else {
+      // sigmoid scores; ranking uses score + selection bias; weights use the score
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int e = lane + 32 * j;
+        if (avail >> j & 1u) {
+          const float sc = 1.f / (1.f + expf(-sel_val[j]));
+          wgt[j] = sc;
+          sel_val[j] = sc + (a.score_bias ? a.score_bias[e] : 0.f);
+          s_logit[warp][e] = sel_val[j];
+        }
+      }
+      __syncwarp();
+      const int per_group = E / a.n_group;
+      if (lane < a.n_group) {
+        float b1 = -INFINITY, b2 = -INFINITY;
+        for (int e = lane * per_group; e < (lane + 1) * per_group; ++e) {
+          const float v = s_logit[warp][e];
+          if (v > b1) {
+            b2 = b1;
+            b1 = v;
+          } else if (v > b2) {
+            b2 = v;
+          }
+        }
+        s_gscore[warp][lane] = (per_group >= 2) ? b1 + b2 : b1;
+      }
+      __syncwarp();
+      float gv = lane < a.n_group ? s_gscore[warp][lane] : -INFINITY;
+      uint32_t kept = 0;
+      for (int r = 0; r < a.topk_group; ++r) {
+        float v = gv;
+        int i = lane < a.n_group ? lane : 0x7fffffff;
+        warp_argmax(v, i);
+        kept |= 1u << i;
+        if (lane == i) gv = -INFINITY;
+      }
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int e = lane + 32 * j;
+        if ((avail >> j & 1u) && !(kept >> (e / per_group) & 1u)) avail &= ~(1u << j);
+      }
+      __syncwarp();
+    }
+
+    float picked_w = 0.f;  // lane r keeps the weight of the r-th pick
+    int picked_e = 0;
+    float wsum = 0.f;
+    for (int r = 0; r < a.k; ++r) {
+      float v = -INFINITY;
+      int idx = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int e = lane + 32 * j;
+        if ((avail >> j & 1u) && (sel_val[j] > v || (sel_val[j] == v && e < idx))) {
+          v = sel_val[j];
+          idx = e;
+        }
+      }
+      warp_argmax(v, idx);
+      float w = 0.f;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+        if (lane + 32 * j == idx) {
+          w = wgt[j];
+          avail &= ~(1u << j);
+        }
+      w = warp_sum(w);  // exactly one lane contributed
+      wsum += w;
+      if (lane == r) {
+        picked_w = w;
+        picked_e = idx;
+      }
+    }
+    if (lane < a.k) {
+      float w = picked_w;
+      if (a.renormalize) w = w / wsum;
+      w *= a.scale;
+      a.idx_out[(int64_t)t * a.k + lane] = picked_e;
+      store_from_float(a.w_out, (int64_t)t * a.k + lane, w, a.w_dtype);
+    }
+    __syncwarp();
+  }
+}
+
+}  // namespace
+}  // namespace dmoe
+
+using namespace dmoe;
+
+extern "C" int dmoe_router(const void* x, const void* w_r, int x_dtype, const float* logit_bias,
+                           const float* score_bias, const float* logits_in, int T, int d, int E, int k, int mode,
+                           int renormalize, float scale, int n_group, int topk_group, float* logits_out,
+                           int64_t* idx_out, void* w_out, int w_dtype, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(T >= 0 && E >= 1 && E <= kMaxExperts, "dmoe_router: need 1 <= E <= %d (E=%d)", kMaxExperts, E);
+  DMOE_REQUIRE(k >= 1 && k <= E && k <= kMaxTopK && k <= 32, "dmoe_router: bad top_k %d", k);
+  DMOE_REQUIRE(dtype_ok(x_dtype) && dtype_ok(w_dtype), "dmoe_router: bad dtype");
+  DMOE_REQUIRE(idx_out && w_out, "dmoe_router: null output");
+  DMOE_REQUIRE(mode == DMOE_ROUTER_SOFTMAX || mode == DMOE_ROUTER_SIGMOID_GROUP, "dmoe_router: bad mode %d", mode);
+  if (mode == DMOE_ROUTER_SIGMOID_GROUP) {
+    DMOE_REQUIRE(n_group >= 1 && n_group <= 32 && E % n_group == 0, "dmoe_router: bad n_group %d", n_group);
+    DMOE_REQUIRE(topk_group >= 1 && topk_group <= n_group, "dmoe_router: bad topk_group %d", topk_group);
+    DMOE_REQUIRE((E / n_group) * topk_group >= k, "dmoe_router: kept groups hold fewer than k experts");
+  }
+  if (logits_in == nullptr) {
+    DMOE_REQUIRE(x && w_r, "dmoe_router: null input");
+    DMOE_REQUIRE(d > 0 && d % 8 == 0, "dmoe_router: d=%d must be a multiple of 8", d);
+    DMOE_REQUIRE(aligned16(x) && aligned16(w_r), "dmoe_router: x and w_r must be 16-byte aligned");
+  }
+  if (T == 0) return DMOE_OK;
+  RouterArgs a{x, w_r, logit_bias, score_bias, logits_in, logits_out, idx_out, w_out, T, d, E, k, mode,
+               renormalize, mode == DMOE_ROUTER_SIGMOID_GROUP ? n_group : 1, topk_group, w_dtype, scale};
+  int blocks = (T + kRouterWarps - 1) / kRouterWarps;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  const dim3 grid(blocks), block(kRouterWarps * 32);
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == DMOE_BF16)
+    router_kernel<DMOE_BF16><<<grid, block, 0, s>>>(a);
+  else if (x_dtype == DMOE_F16)
+    router_kernel<DMOE_F16><<<grid, block, 0, s>>>(a);
+  else
+    router_kernel<DMOE_F32><<<grid, block, 0, s>>>(a);
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}

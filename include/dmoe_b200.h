@@ -1,0 +1,183 @@
+/*
+ * dmoe_b200.h -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * The library (libdmoe_b200.so) replaces the torch-op sequences of the reference
+ * (slivanovich/DistributedMoE, paths relative to src/python/) on the path
+ *   DistMoEBlock routing -> dispatch into BuffersPool input buffers -> grouped expert
+ *   gated MLP -> weighted combine.
+ *
+ * Conventions
+ *  - Plain pointers and sizes; device pointers unless a parameter says "host".
+ *  - Every call is stream-ordered on `stream` (a cudaStream_t passed as void*; NULL is the
+ *    legacy default stream) and returns 0 on success or a DMOE_ERR_* code.  The message of
+ *    the last failure on the calling thread is returned by dmoe_last_error().
+ *  - The library never allocates or frees caller memory.  Scratch is passed in as
+ *    `workspace` with a size query function.
+ *  - Kernels that wait (mbarriers inside the grouped GEMM, dmoe_flag_wait) bound every
+ *    wait by time; on expiry they OR a DMOE_DEVERR_* bit into the caller's device word
+ *    `dev_status` (int32) and return, never trap.
+ *  - dtype codes: DMOE_F32, DMOE_F16, DMOE_BF16.
+ */
+#ifndef DMOE_B200_H
+#define DMOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DMOE_OK 0
+#define DMOE_ERR_INVALID 1     /* bad argument, shape or alignment */
+#define DMOE_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define DMOE_ERR_UNSUPPORTED 3 /* valid request this build does not implement */
+
+#define DMOE_F32 0
+#define DMOE_F16 1
+#define DMOE_BF16 2
+
+#define DMOE_ACT_RELU 0 /* reference: relu(gate) * up  (MoE/PipelineTask.py:518, MoE/MoE.py:25) */
+#define DMOE_ACT_SILU 1 /* SwiGLU: silu(gate) * up */
+
+#define DMOE_ROUTER_SOFTMAX 0       /* softmax(fp32) -> top-k (MoE/DistMoEBlock.py:557-562) */
+#define DMOE_ROUTER_SIGMOID_GROUP 1 /* sigmoid + selection bias + group-limited top-k */
+
+/* device status bits (OR-ed into *dev_status) */
+#define DMOE_DEVERR_TIMEOUT_PRODUCER 0x1
+#define DMOE_DEVERR_TIMEOUT_MMA 0x2
+#define DMOE_DEVERR_TIMEOUT_EPILOGUE 0x4
+#define DMOE_DEVERR_TIMEOUT_TEARDOWN 0x8
+#define DMOE_DEVERR_FLAG_TIMEOUT 0x10
+#define DMOE_DEVERR_BAD_SEGMENT 0x20
+
+/* Library identity: returns a static version string. */
+const char* dmoe_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* dmoe_last_error(void);
+
+/*
+ * Router: logits, top-k selection and routing weights, one warp per token.
+ * Replaces DistMoEBlock._setup_forward_pass routing, MoE/DistMoEBlock.py:556-562
+ * (gate = nn.Linear(d, E, bias=False), :134; softmax in fp32, torch.topk, cast to dtype).
+ *
+ *  x            [T, d] activations (x_dtype); ignored when logits_in != NULL
+ *  w_r          [E, d] router weight (same dtype as x)
+ *  logit_bias   [E] fp32 added to the logits, or NULL (the bias=True gate replacement, :133)
+ *  score_bias   [E] fp32 selection bias for DMOE_ROUTER_SIGMOID_GROUP, or NULL
+ *  logits_in    [T, E] fp32 logits to route from instead of computing them, or NULL
+ *  logits_out   [T, E] fp32 logits written when not NULL (and logits_in == NULL)
+ *  idx_out      [T, k] int64 selected experts, best first (torch.topk order)
+ *  w_out        [T, k] routing weights in w_dtype
+ *  renormalize  divide the k weights by their sum (extension; the reference does not)
+ *  scale        multiply the weights (1.0 in the reference)
+ *  n_group/topk_group  group-limited selection (DMOE_ROUTER_SIGMOID_GROUP)
+ *  Limits: E <= 256, k <= min(E, 16), d % 8 == 0.
+ */
+int dmoe_router(const void* x, const void* w_r, int x_dtype, const float* logit_bias, const float* score_bias,
+                const float* logits_in, int T, int d, int E, int k, int mode, int renormalize, float scale,
+                int n_group, int topk_group, float* logits_out, int64_t* idx_out, void* w_out, int w_dtype,
+                void* stream);
+
+/*
+ * Routing plan: per-expert counts, offsets and the permutation of the T*k activations.
+ * Replaces the one-hot mask + per-expert torch.where loop of MoE/DistMoEBlock.py:568-605:
+ * within an expert, activations are ordered slot-major then by ascending token, exactly as
+ * torch.where(expert_mask[e]) orders them.  Experts are concatenated in index order.
+ *
+ *  idx          [T, k] int64 expert of each (token, slot)
+ *  w            [T, k] routing weights (w_dtype) or NULL
+ *  counts       [E] int32, offsets [E+1] int32 (exclusive prefix of counts)
+ *  perm_token   [T*k] int32 token of each permuted activation
+ *  perm_slot    [T*k] int32 slot of each permuted activation (may be NULL)
+ *  inverse      [T*k] int32 permuted position of (token t, slot s) at t*k+s (may be NULL)
+ *  perm_weight  [T*k] weight of each permuted activation in w_dtype (NULL if w is NULL)
+ *  workspace    dmoe_route_plan_workspace_size(T, k, E) bytes of device scratch
+ *  Limits: 1 <= E <= 1024, T*k < 2^31.
+ */
+size_t dmoe_route_plan_workspace_size(int T, int k, int E);
+int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E, int32_t* counts,
+                    int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse,
+                    void* perm_weight, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Segmented row gather/copy: for segment i and r < seg_len[i]
+ *     dst[seg_dst[i] + r] = src[ row_map ? row_map[seg_src[i] + r] : seg_src[i] + r ]
+ * with rows of row_bytes bytes (multiple of 16, 16-byte aligned bases).
+ * With row_map = perm_token this is the gather of HostPipelineTask.dispatch
+ * (MoE/PipelineTask.py:231-249) into an input buffer; dst may be a peer GPU's buffer
+ * (CUDA IPC / peer pointer).  Without row_map it moves contiguous runs (buffer staging).
+ *  seg_src, seg_dst, seg_len: host arrays of n_seg int32 (n_seg <= 1024).
+ */
+int dmoe_permute_rows(const void* src, void* dst, int64_t row_bytes, const int32_t* row_map,
+                      const int32_t* seg_src, const int32_t* seg_dst, const int32_t* seg_len, int n_seg,
+                      void* stream);
+
+/*
+ * Grouped expert gated MLP over per-expert row segments of one buffer.
+ * Replaces the grouped path of ExpertsBlockPipelineTask.run, MoE/PipelineTask.py:478-520:
+ *   offs = cumulative (padded) segment ends; gate_out = grouped_mm(X, Wg^T); up_out = ...;
+ *   h = act(gate_out) * up_out; Y = grouped_mm(h, Wd^T); copy into the output buffer.
+ * Weights are the stacks of DistExpertsBlock.initialize_expert_layers
+ * (MoE/DistExpertsBlock.py:163-177) in nn.Linear layout:
+ *   w_gate, w_up [E_stack, I, d]; w_down [E_stack, d, I]   (dtype DMOE_F16 or DMOE_BF16)
+ * Segment i covers rows [seg_end[i-1], seg_end[i]) (seg_end[-1] = 0) and uses stack entry
+ * seg_expert[i]; rows outside every segment are not written.  seg_* are host arrays when
+ * seg_on_device == 0 (n_seg <= 256), device arrays otherwise (n_seg <= 1024).
+ *  X [m_rows, d], Y [m_rows, d]; workspace >= dmoe_grouped_mlp_workspace_size(m_rows, I, dtype)
+ *  Computes on tcgen05 tensor cores (fp32 accumulate in TMEM); h is rounded to dtype.
+ *  Limits: d % 64 == 0, I % 64 == 0.
+ */
+size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype);
+int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack,
+                           int d, int I, int dtype, const int32_t* seg_expert, const int32_t* seg_end, int n_seg,
+                           int seg_on_device, int m_rows, int act, void* Y, void* workspace, size_t workspace_bytes,
+                           int32_t* dev_status, void* stream);
+
+/*
+ * Weighted combine (gather form): for each token t
+ *     out[t] = sum_s w[t, s] * rows[inverse[t*k + s]]       (fp32 accumulation, one store)
+ * `rows` [T*k, d] holds the expert outputs in permuted order.  Replaces the per-expert
+ * weighted scatter_add_ of HostPipelineTask.combine (MoE/PipelineTask.py:326-346), which
+ * accumulates in the model dtype; results agree up to summation order and rounding.
+ *  If accumulate != 0, out[t] (dtype) is added to the sum (shared-expert / residual input).
+ */
+int dmoe_combine(const void* rows, const int32_t* inverse, const void* w, int w_dtype, int T, int k, int d,
+                 int dtype, int accumulate, void* out, void* stream);
+
+/*
+ * CUDA IPC for the NVLink TensorTransferEngine backend (replaces NIXL/MoonCake memory
+ * registration: TensorTransferEngine.register_batch / deserialize_descs / deregister_batch,
+ * TensorTransferEngine/TensorTransferEngine.py:146-192).
+ *  handle: 64 opaque bytes (cudaIpcMemHandle_t).
+ */
+int dmoe_ipc_export(const void* dev_ptr, uint8_t* handle_out64);
+int dmoe_ipc_open(const uint8_t* handle64, int device, void** dev_ptr_out);
+int dmoe_ipc_close(void* dev_ptr);
+int dmoe_enable_peer_access(int device, int peer_device);
+
+/*
+ * Byte copy between any two device (or peer-mapped) buffers, stream-ordered.  Replaces the
+ * NIXL READ/WRITE of Buffer.read_from / write_to (MoE/pools/BuffersPool.py:55-90).
+ */
+int dmoe_copy(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
+ * Completion flags (replace the transfer-monitor poll, TensorTransferEngine.py:305-344).
+ * dmoe_flag_signal stores `value` to *flag with release semantics (system scope) after the
+ * preceding work of `stream`.  dmoe_flag_wait makes `stream` wait until *flag >= value, at
+ * most timeout_ns; on expiry it ORs DMOE_DEVERR_FLAG_TIMEOUT into *dev_status and lets the
+ * stream continue.  A waiter and its signaller must run on different GPUs: two kernels on
+ * one GPU are not guaranteed to run concurrently.
+ */
+int dmoe_flag_signal(uint64_t* flag, uint64_t value, void* stream);
+int dmoe_flag_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, int32_t* dev_status, void* stream);
+
+/* Number of kernels this library launched in this process (for launch accounting). */
+uint64_t dmoe_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DMOE_B200_H */

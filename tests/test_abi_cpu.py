@@ -1,0 +1,63 @@
+"""The C-ABI library loads on a machine without a GPU and exports every symbol that
+include/dmoe_b200.h declares (no compute calls)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dmoe_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(dmoe_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_boundary():
+    names = _declared()
+    for required in ["dmoe_router", "dmoe_route_plan", "dmoe_permute_rows", "dmoe_grouped_gated_mlp",
+                     "dmoe_combine", "dmoe_ipc_export", "dmoe_ipc_open", "dmoe_ipc_close", "dmoe_flag_signal",
+                     "dmoe_flag_wait", "dmoe_last_error"]:
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from distributedmoe_b200 import _native as N
+    lib = N.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    # the Python binding covers the whole header
+    assert set(_declared()) <= set(N.SIGNATURES)
+
+
+def test_pure_host_entry_points():
+    from distributedmoe_b200 import _native as N
+    lib = N.lib()
+    assert b"sm_100a" in lib.dmoe_version()
+    assert lib.dmoe_route_plan_workspace_size(4096, 2, 8) == 4 * 8 * 4
+    assert lib.dmoe_grouped_mlp_workspace_size(8192, 14336, 2) >= 8192 * 14336 * 2
+
+
+def test_argument_validation_without_gpu():
+    """Validation runs before any CUDA call, so it works here."""
+    from distributedmoe_b200 import _native as N
+    lib = N.lib()
+    rc = lib.dmoe_router(None, None, 2, None, None, None, 16, 64, 300, 2, 0, 0, 1.0, 1, 1, None, None, None, 2, None)
+    assert rc == 1 and b"E <=" in lib.dmoe_last_error()
+    rc = lib.dmoe_grouped_gated_mlp(None, None, None, None, 8, 100, 64, 2, None, None, 1, 0, 10, 0, None, None, 0,
+                                    None, None)
+    assert rc == 1
+
+
+def test_no_cpu_fallback_in_product():
+    """The product never imports the oracle."""
+    pkg = os.path.join(ROOT, "distributedmoe_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith(".py"):
+                src = open(os.path.join(dirpath, f)).read()
+                assert "oracle" not in re.findall(r"^\s*(?:from|import)\s+(\w+)", src, flags=re.M), f
