@@ -1,0 +1,505 @@
+"""Host side of the distributed MoE layer (reference ``MoE/DistMoEBlock.py``).
+
+Public API as in the reference: ``DistMoEBlockConfig``, ``DistMoEBlock(config, tte_config,
+metrics_collector=None)``, ``forward(x, using_grouped_gemm=True, using_alignment=False)``,
+``disable_experts_block``, ``enable_experts_block``, ``close``; the same control flow for
+dispatch waves, the ``forward_timeout`` SLA (partial result on expiry), the ZeroMQ health
+checker, the P2P handler, and abort + re-dispatch of a dead block's tasks.
+
+Routing differs in where it runs: one router kernel (fp32 logits, softmax or the
+sigmoid/group-limited router, top-k, optional renormalisation) and the routing-plan
+kernels replace the gate GEMM, softmax, top-k, one-hot mask and the per-expert
+``torch.where`` loop with its per-expert host synchronisations (``:553-605``).  The host
+reads back only the E per-expert counts, once per forward.  The output is the gather-form
+weighted combine of the permuted expert outputs, issued on the caller's stream.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import math
+import struct
+import threading
+import timeit
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import zmq
+import zmq.asyncio
+
+from distributedmoe_b200 import _native as N
+from distributedmoe_b200.MoE.DistMoE import ExpertMetaData, P2PHeaders, SegmentQueue
+from distributedmoe_b200.MoE.PipelineTask import ForwardState, HostPipelineTask
+from distributedmoe_b200.MoE.pools.BuffersPool import BuffersPool
+from distributedmoe_b200.MoE.pools.ExpertBlocksPool import ExpertBlocksPool
+from distributedmoe_b200.TensorTransferEngine import create_transfer_engine
+from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import (
+    TensorTransferEngine,
+    TensorTransferEngineBackend,
+    TensorTransferEngineConfig,
+)
+from distributedmoe_b200.TensorTransferEngine.utils import P2PPair, join_host_port
+from distributedmoe_b200.utils.logging_config import get_logger
+
+ACTIVATIONS = {"relu": N.ACT_RELU, "silu": N.ACT_SILU}
+
+
+@dataclass
+class DistMoEBlockConfig:
+    backend: TensorTransferEngineBackend
+    number_of_experts: int
+    expert_blocks: List[List[int]]
+    number_of_io_buffers: int
+    io_buffer_size: int
+    top_k: int
+    hidden_features: int
+    dtype: torch.dtype
+    moe_device: torch.device
+    eb_devices: List[torch.device]
+    forward_timeout: int
+    host_health_check_ports: List[int]
+    remote_health_check_ports: List[int]
+    # ---- options this build adds (defaults reproduce the reference) ----
+    # expert activation: "relu" (reference, MoE/MoE.py:25) or "silu" (SwiGLU)
+    activation: str = "relu"
+    # divide the top-k routing weights by their sum (the reference does not)
+    renormalize: bool = False
+    # router logits in fp32 (False: in the model dtype, as the reference's gate computes them)
+    router_fp32_logits: bool = True
+    # "softmax" (reference) or "sigmoid_group" (DeepSeek-V3 style)
+    router_mode: str = "softmax"
+    routed_scaling_factor: float = 1.0
+    n_group: int = 1
+    topk_group: int = 1
+    # expert block choice: "fifo" (reference round robin) or "least_loaded"
+    expert_block_policy: str = "fifo"
+
+
+class DistMoEBlock(nn.Module):
+    def __init__(self, config: DistMoEBlockConfig, tte_config: TensorTransferEngineConfig, metrics_collector=None):
+        super().__init__()
+        self.logger = get_logger("dist_moe.moe.block")
+        self._is_closed = False
+        self.metrics_collector = metrics_collector
+        self.config = config
+        self.device: torch.device = torch.device(config.moe_device)
+        self.number_of_expert_blocks = len(config.expert_blocks)
+        self.number_of_experts = config.number_of_experts
+        self.top_k = config.top_k
+        self.experts_hit: List[int] = []
+        self.hidden_features = config.hidden_features
+        self.dtype = config.dtype
+        self.forward_timeout = config.forward_timeout
+        self.host_health_check_ports = config.host_health_check_ports
+        self.remote_health_check_ports = config.remote_health_check_ports
+        self.health_check_timeout = tte_config.p2p_timeout_duration
+        if config.activation not in ACTIVATIONS:
+            raise ValueError(f"unknown activation {config.activation!r}")
+        if config.router_mode not in ("softmax", "sigmoid_group"):
+            raise ValueError(f"unknown router mode {config.router_mode!r}")
+
+        self.event_loop = asyncio.new_event_loop()
+        asyncio.set_event_loop(self.event_loop)
+        self._loop_stopped = threading.Event()
+
+        with torch.cuda.device(self.device):
+            self.tensor_transfer_engine: TensorTransferEngine = create_transfer_engine(config.backend, tte_config)
+
+        self.health_check_context = zmq.asyncio.Context()
+        self.health_check_p2p_pairs: Dict[str, P2PPair] = {}
+        self.setup_health_check(tte_config)
+
+        # Router (replaceable like the reference's, :133-134); score_bias feeds the
+        # selection of the sigmoid router only.
+        self.gate: nn.Module = nn.Linear(self.hidden_features, self.number_of_experts, bias=False, dtype=self.dtype,
+                                         device=self.device)
+        self.score_bias: Optional[torch.Tensor] = None
+        self.output_batch: torch.Tensor = torch.zeros(1, dtype=self.dtype, device=self.device)
+
+        self.expert_blocks: List[List[int]] = config.expert_blocks
+        self.expert_blocks_pool = ExpertBlocksPool(self.expert_blocks, policy=config.expert_block_policy)
+        self.initialize_metadata()
+
+        self.number_of_io_buffers = config.number_of_io_buffers
+        self.io_buffer_size = config.io_buffer_size
+        if not (1 <= self.io_buffer_size <= 65535):
+            raise ValueError("io_buffer_size must fit the 16-bit packet fields (1..65535)")
+        self.activations_batch_size_candidates: List[int] = []
+        self.initialize_io_buffers()
+
+        self.async_lock = asyncio.Lock()
+        self.combining = asyncio.Event()
+        self.pipeline_tasks: Dict[bytes, HostPipelineTask] = {}
+        self.dispatch_tasks: Dict[bytes, asyncio.Task] = {}
+        self.combine_tasks: Dict[bytes, asyncio.Task] = {}
+        self.expert_block_tasks: Dict[int, List[bytes]] = {}
+        self.active_pipeline_tasks: List[int] = [0]
+        self.transferred_activations: List[int] = [0]
+        self.total_activations = 0
+        self.forward_state: Optional[ForwardState] = None
+        self._counts_host = torch.empty(self.number_of_experts, dtype=torch.int32, pin_memory=True)
+
+        self.monitoring_flag = True
+        self.monitoring_tasks: List[asyncio.Task] = []
+        self.disabled_expert_blocks: set = set()
+        self.setup_monitoring()
+        self.logger.info(f"DistMoEBlock initialized - Experts: {self.number_of_experts}, "
+                         f"Blocks: {self.number_of_expert_blocks}, Device: {self.device}")
+
+    # ------------------------------------------------------------------ setup
+    def disable_experts_block(self, experts_block_index: int) -> None:
+        self.disabled_expert_blocks.add(experts_block_index)
+        self.expert_blocks_pool.mark_dead(experts_block_index)
+
+    def enable_experts_block(self, experts_block_index: int) -> None:
+        self.disabled_expert_blocks.discard(experts_block_index)
+        self.expert_blocks_pool.mark_alive(experts_block_index)
+
+    def setup_health_check(self, tte_config: TensorTransferEngineConfig) -> None:
+        assert len(self.host_health_check_ports) == len(tte_config.remote_addresses)
+        assert len(self.remote_health_check_ports) == len(tte_config.remote_addresses)
+        for i in range(len(tte_config.remote_addresses)):
+            remote_name = join_host_port(tte_config.remote_addresses[i], tte_config.remote_ports[i])
+            pair = P2PPair(self.health_check_context.socket(zmq.PUSH), self.health_check_context.socket(zmq.PULL))
+            pair.pusher.bind(join_host_port(tte_config.host_address, self.host_health_check_ports[i], "tcp"))
+            pair.pusher.setsockopt(zmq.RCVTIMEO, self.health_check_timeout)
+            pair.puller.connect(join_host_port(tte_config.remote_addresses[i], self.remote_health_check_ports[i], "tcp"))
+            pair.puller.setsockopt(zmq.RCVTIMEO, self.health_check_timeout)
+            self.health_check_p2p_pairs[remote_name] = pair
+
+    def initialize_io_buffers(self) -> None:
+        args = (self.tensor_transfer_engine, self.io_buffer_size, self.hidden_features, self.dtype, self.device)
+        self.input_buffers_pool = BuffersPool(self.number_of_io_buffers, *args)
+        self.output_buffers_pool = BuffersPool(self.number_of_io_buffers, *args)
+        self.tensor_transfer_engine.handshake()  # synchronisation point, as in the reference (:246-247)
+        packet = self._build_io_descriptors_packet()
+
+        async def send_io_descriptors():
+            for remote_name in self.tensor_transfer_engine.remote_names:
+                await self.tensor_transfer_engine.async_send_metadata_to(
+                    remote_name, P2PHeaders.IOTransferDescriptorsSubmit.value, packet)
+
+        self.event_loop.run_until_complete(send_io_descriptors())
+        step = max(self.io_buffer_size // 1024, 1)
+        self.activations_batch_size_candidates = list(range(step, self.io_buffer_size, step)) + [self.io_buffer_size]
+
+    def _build_io_descriptors_packet(self) -> List[Tuple[int, bytes]]:
+        """``!H n`` then (2-byte id, serialized descriptors) per input then output buffer (``:269-289``)."""
+        packet: List[Tuple[int, bytes]] = [(2, struct.pack("!H", self.number_of_io_buffers))]
+        for i, b in enumerate(self.input_buffers_pool.buffers):
+            b.id = i.to_bytes(length=2, byteorder="big")
+            packet += [(2, b.id), b.serialized_transfer_descs]
+        for i, b in enumerate(self.output_buffers_pool.buffers):
+            b.id = (self.number_of_io_buffers + i).to_bytes(length=2, byteorder="big")
+            packet += [(2, b.id), b.serialized_transfer_descs]
+        return packet
+
+    def initialize_metadata(self) -> None:
+        self.experts_metadata: Dict[int, ExpertMetaData] = {}
+        for e in range(self.number_of_experts):
+            self.experts_metadata[e] = ExpertMetaData([], 0, None, None, 0, SegmentQueue())
+        for b in range(self.number_of_expert_blocks):
+            for e in self.expert_blocks[b]:
+                self.experts_metadata[e].block_indexes.append(b)
+                self.experts_metadata[e].expert_shared_rate += 1
+
+    # ------------------------------------------------------------------ fault tolerance
+    async def _abort_all_dispatched_to(self, experts_block_index: int) -> None:
+        async with self.async_lock:
+            names = self.expert_block_tasks.get(experts_block_index, [])
+            self.expert_block_tasks[experts_block_index] = []
+            for name in names:
+                task = self.pipeline_tasks.get(name)
+                if task is not None:
+                    task.abort()
+                    if task.dispatch_done:
+                        self.transferred_activations[0] -= task.used_activations
+                        if not task.combine_done:
+                            self.active_pipeline_tasks[0] -= 1
+                for tasks in (self.dispatch_tasks, self.combine_tasks):
+                    t = tasks.pop(name, None)
+                    if t is not None:
+                        t.cancel()
+                self.pipeline_tasks.pop(name, None)
+            if names:
+                self.combining.set()
+
+    async def _expert_block_health_checker(self, experts_block_index: int, remote_name: str) -> None:
+        try:
+            while self.monitoring_flag:
+                try:
+                    await asyncio.sleep(0.02)
+                    if experts_block_index in self.disabled_expert_blocks:
+                        continue
+                    pair = self.health_check_p2p_pairs.get(remote_name)
+                    if not pair:
+                        continue
+                    try:
+                        await pair.pusher.send(self.tensor_transfer_engine.serialize_p2p_packet(P2PHeaders.Ping.value, []))
+                    except Exception as e:
+                        self.logger.error(f"health check: ping to EB #{experts_block_index} failed: {e}")
+                        continue
+                    try:
+                        packet = await asyncio.wait_for(pair.puller.recv(), timeout=1.0)
+                        header, _ = self.tensor_transfer_engine.deserialize_p2p_packet(packet)
+                        if header != P2PHeaders.Pong.value:
+                            raise RuntimeError(f"unexpected health check header {header}")
+                        md = self.expert_blocks_pool.expert_blocks_metadata[experts_block_index]
+                        if experts_block_index not in self.disabled_expert_blocks and not md.is_alive:
+                            self.expert_blocks_pool.mark_alive(experts_block_index)
+                    except Exception:
+                        if self.expert_blocks_pool.expert_blocks_metadata[experts_block_index].is_alive:
+                            self.expert_blocks_pool.mark_dead(experts_block_index)
+                            self.logger.warning(f"EB #{experts_block_index} marked as dead (no pong)")
+                            await self._abort_all_dispatched_to(experts_block_index)
+                    if self.active_pipeline_tasks[0] == 0:
+                        self.combining.set()
+                except asyncio.CancelledError:
+                    break
+                except Exception as e:
+                    self.expert_blocks_pool.mark_dead(experts_block_index)
+                    await self._abort_all_dispatched_to(experts_block_index)
+                    self.logger.error(f"health check failure for block {experts_block_index}: {e}")
+        except asyncio.CancelledError:
+            pass
+
+    async def _expert_block_p2p_handler(self, experts_block_index: int, remote_name: str) -> None:
+        try:
+            while self.monitoring_flag:
+                try:
+                    header, metadata = await self.tensor_transfer_engine.async_get_metadata_from(remote_name)
+                except asyncio.CancelledError:
+                    break
+                except Exception:
+                    continue
+                md = self.expert_blocks_pool.expert_blocks_metadata[experts_block_index]
+                if experts_block_index not in self.disabled_expert_blocks and not md.is_alive:
+                    self.expert_blocks_pool.mark_alive(experts_block_index)
+                if header == P2PHeaders.HostOutputBufferUnlocked.value:
+                    name: bytes = metadata[-1][1]
+                    task = self.pipeline_tasks.get(name)
+                    if task is not None:
+                        async def combine(task=task, name=name):
+                            try:
+                                await task.combine(self.active_pipeline_tasks, self.output_batch, self.combining)
+                            finally:
+                                self.combine_tasks.pop(name, None)
+                                self.dispatch_tasks.pop(name, None)
+                                self.pipeline_tasks.pop(name, None)
+
+                        self.combine_tasks[name] = asyncio.create_task(combine())
+                    else:
+                        self.logger.debug(f"stale combine ack for task {name.hex()[:8]}")
+                elif header == P2PHeaders.HostInputBufferUnlocked.value:
+                    task = self.pipeline_tasks.get(metadata[-1][1])
+                    if task is not None:
+                        task.release_input_buffer()
+                elif header == P2PHeaders.IOTransferDescriptorsRequest.value:
+                    await self.tensor_transfer_engine.async_send_metadata_to(
+                        remote_name, P2PHeaders.IOTransferDescriptorsSubmit.value, self._build_io_descriptors_packet())
+                elif header == P2PHeaders.Pong.value:
+                    self.expert_blocks_pool.mark_alive(experts_block_index)
+                else:
+                    self.logger.warning(f"P2P handler: unknown header {header}")
+        except asyncio.CancelledError:
+            pass
+
+    def setup_monitoring(self) -> None:
+        for b, remote_name in enumerate(self.tensor_transfer_engine.remote_names):
+            self.monitoring_tasks.append(self.event_loop.create_task(self._expert_block_health_checker(b, remote_name)))
+            self.monitoring_tasks.append(self.event_loop.create_task(self._expert_block_p2p_handler(b, remote_name)))
+
+    # ------------------------------------------------------------------ forward
+    def _route(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        cfg = self.config
+        mode = N.ROUTER_SOFTMAX if cfg.router_mode == "softmax" else N.ROUTER_SIGMOID_GROUP
+        kw = dict(mode=mode, renormalize=cfg.renormalize, scale=cfg.routed_scaling_factor, n_group=cfg.n_group,
+                  topk_group=cfg.topk_group, w_dtype=self.dtype,
+                  score_bias=None if self.score_bias is None else self.score_bias.float().contiguous())
+        g = self.gate
+        plain_linear = isinstance(g, nn.Linear) and g.weight.dtype == x.dtype and g.weight.is_contiguous()
+        if plain_linear and cfg.router_fp32_logits:
+            bias = None if g.bias is None else g.bias.detach().float().contiguous()
+            idx, w, _ = N.router(x, g.weight.detach(), self.top_k, logit_bias=bias, **kw)
+        else:
+            # A replaced gate module, or logits in the model dtype as the reference computes them.
+            with torch.no_grad():
+                logits = g(x).float().contiguous()
+            idx, w, _ = N.router(None, None, self.top_k, logits_in=logits, **kw)
+        return idx, w
+
+    def _setup_forward_pass(self, input_batch: torch.Tensor) -> Tuple[List[int], torch.Tensor]:
+        assert input_batch.dtype == self.dtype
+        assert input_batch.device == self.device
+        if input_batch.dim() == 3:
+            assert input_batch.shape[2] == self.hidden_features
+            input_batch = input_batch.reshape(-1, self.hidden_features)
+        elif input_batch.dim() == 2:
+            assert input_batch.shape[1] == self.hidden_features
+        else:
+            raise RuntimeError(f"Wrong input batch shape: {input_batch.shape} with hidden size: {self.hidden_features}")
+        x = input_batch.contiguous()
+        T, E, k = x.shape[0], self.number_of_experts, self.top_k
+        stream = torch.cuda.current_stream(self.device)
+        self.output_batch = torch.empty(x.shape, dtype=self.dtype, device=self.device)
+        if T == 0:
+            self.forward_state = None
+            return [], x
+        idx, w = self._route(x)
+        plan = N.route_plan(idx, w, E)
+        self._counts_host.copy_(plan["counts"], non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        ready.synchronize()  # the only host synchronisation of the forward: E counts
+        counts = self._counts_host.tolist()
+        experts_hit, offsets, base = [], [0] * (E + 1), 0
+        for e in range(E):
+            offsets[e] = base
+            n = counts[e]
+            if n:
+                experts_hit.append(e)
+                self.experts_metadata[e].bind(plan, base, n)
+            base += n
+        offsets[E] = base
+        arena = torch.empty(T * k, self.hidden_features, dtype=self.dtype, device=self.device)
+        self.forward_state = ForwardState(x, plan, offsets, w, ready, arena)
+        return experts_hit, x
+
+    def _finalize(self) -> None:
+        """Weighted combine of the permuted rows on the caller's stream.  After a timeout,
+        rows that never came back are zeroed first, so their tokens get a partial sum, as
+        the reference's partial output does (``:716-718``)."""
+        fs = self.forward_state
+        stream = torch.cuda.current_stream(self.device)
+        for ev in fs.events:
+            stream.wait_event(ev)
+        T = fs.x.shape[0]
+        if sum(n for _e, _l, n in fs.covered) < T * self.top_k:
+            import numpy as np
+
+            covered = np.zeros(T * self.top_k, dtype=bool)
+            for e, l, n in fs.covered:
+                covered[fs.offsets[e] + l: fs.offsets[e] + l + n] = True
+            missing = np.flatnonzero(~covered)
+            if missing.size:
+                fs.arena[torch.from_numpy(missing).to(self.device)] = 0
+        N.combine(fs.arena, fs.plan["inverse"], fs.routing_weights, self.output_batch)
+
+    def dispatch(self, input_batch: torch.Tensor, number_of_dispatches: int, using_grouped_gemm: bool = True,
+                 using_alignment: bool = False) -> None:
+        submits = 0
+        while self.transferred_activations[0] < self.total_activations and submits < number_of_dispatches:
+            task = HostPipelineTask(self.tensor_transfer_engine, self.input_buffers_pool, self.output_buffers_pool,
+                                    self.experts_hit, self.expert_blocks_pool, self.experts_metadata, self.async_lock,
+                                    self.metrics_collector, forward_state=self.forward_state)
+            self.pipeline_tasks[task.name] = task
+            self.dispatch_tasks[task.name] = asyncio.create_task(task.dispatch(
+                input_batch, self.active_pipeline_tasks, self.transferred_activations, self.expert_block_tasks,
+                self.activations_batch_size_candidates if using_alignment else None, using_grouped_gemm))
+            submits += 1
+
+    async def async_forward(self, input_batch: torch.Tensor, using_grouped_gemm: bool = True,
+                            using_alignment: bool = False) -> torch.Tensor:
+        if self.metrics_collector is not None:
+            self.metrics_collector.start_forward_pass()
+        if self.combine_tasks:
+            await asyncio.gather(*list(self.combine_tasks.values()), return_exceptions=True)
+        self.dispatch_tasks.clear()
+        self.combine_tasks.clear()
+        self.pipeline_tasks.clear()
+        self.expert_block_tasks.clear()
+
+        shape = input_batch.shape
+        self.experts_hit, x = self._setup_forward_pass(input_batch)
+        if not self.experts_hit:
+            self.output_batch.zero_()
+            if self.metrics_collector is not None:
+                self.metrics_collector.end_setup_phase()
+                self.metrics_collector.end_forward_pass()
+            return self.output_batch.reshape(shape)
+
+        self.total_activations = self.top_k * x.shape[0]
+        self.active_pipeline_tasks[0] = 0
+        self.transferred_activations[0] = 0
+        if self.metrics_collector is not None:
+            self.metrics_collector.end_setup_phase()
+
+        start = timeit.default_timer()
+        while self.transferred_activations[0] < self.total_activations:
+            self.combining.clear()
+            n = max(math.ceil((self.total_activations - self.transferred_activations[0]) / self.io_buffer_size), 1)
+            self.dispatch(x, n, using_grouped_gemm, using_alignment)
+            try:
+                elapsed = timeit.default_timer() - start
+                await asyncio.wait_for(self.combining.wait(), timeout=(self.forward_timeout / 1000 - elapsed))
+            except asyncio.TimeoutError:
+                break
+        # Every dispatched task has been combined unless the SLA expired.
+        if self.active_pipeline_tasks[0] > 0:
+            try:
+                elapsed = timeit.default_timer() - start
+                while self.active_pipeline_tasks[0] > 0:
+                    self.combining.clear()
+                    await asyncio.wait_for(self.combining.wait(), timeout=max(self.forward_timeout / 1000 - elapsed, 0))
+            except asyncio.TimeoutError:
+                pass
+        for name, t in list(self.dispatch_tasks.items()):
+            t.cancel()
+            task = self.pipeline_tasks.get(name)
+            if task is not None and not task.combine_done:
+                task.close()
+        for name, t in list(self.combine_tasks.items()):
+            t.cancel()
+        self._finalize()
+        if self.metrics_collector is not None:
+            self.metrics_collector.end_forward_pass()
+        return self.output_batch.reshape(shape)
+
+    def forward(self, input_batch: torch.Tensor, using_grouped_gemm: bool = True, using_alignment: bool = False) -> torch.Tensor:
+        return self.event_loop.run_until_complete(self.async_forward(input_batch, using_grouped_gemm, using_alignment))
+
+    # ------------------------------------------------------------------ shutdown
+    def close(self) -> None:
+        if self._is_closed:
+            return
+
+        async def send_stop_signals():
+            for remote_name in self.tensor_transfer_engine.remote_names:
+                try:
+                    await asyncio.wait_for(self.tensor_transfer_engine.async_send_metadata_to(
+                        remote_name, P2PHeaders.ExpertsBlockStop.value, []), timeout=5.0)
+                except Exception as e:
+                    self.logger.warning(f"stop signal to {remote_name} failed: {e}")
+
+        if not self.event_loop.is_closed():
+            try:
+                self.event_loop.run_until_complete(send_stop_signals())
+            except Exception as e:
+                self.logger.error(f"Error sending stop signals: {e}")
+            self.monitoring_flag = False
+            for t in self.monitoring_tasks:
+                if not t.done():
+                    t.cancel()
+            try:
+                self.event_loop.run_until_complete(
+                    asyncio.wait_for(asyncio.gather(*self.monitoring_tasks, return_exceptions=True), timeout=2.0))
+            except Exception:
+                pass
+            self.event_loop.close()
+        self._loop_stopped.set()
+        self.input_buffers_pool.close()
+        self.output_buffers_pool.close()
+        for pair in self.health_check_p2p_pairs.values():
+            try:
+                pair.pusher.close(linger=0)
+                pair.puller.close(linger=0)
+            except Exception:
+                pass
+        try:
+            self.health_check_context.term()
+        except Exception:
+            pass
+        self.tensor_transfer_engine.close()
+        self._is_closed = True

@@ -1,0 +1,259 @@
+"""NVLink / CUDA-IPC transfer engine: the B200 data plane replacing NIXL/UCX and MoonCake
+(``TensorTransferEngine/NIXLTensorTransferEngine.py``, ``MCTETensorTransferEngine.py``).
+
+A registered region is described by (pid, device, pointer, size, CUDA-IPC memory handle +
+offset, completion-event token).  A peer in the same process uses the pointer directly
+(UVA + peer access over NVLink); a peer in another process maps the IPC handle once and
+caches the mapping.  READ and WRITE are stream-ordered copies issued on the caller's current
+CUDA stream: they wait for the last-access events of both regions, copy over NVLink /
+NVSwitch (or within HBM when both regions are on one GPU), and record both events again.
+Consumers order themselves after a region with :meth:`wait_region` instead of a host round
+trip; :meth:`wait_for_transfer_efficient` still works for callers that want a host wait.
+
+Completion events are CUDA events, shared through a process-local registry or as CUDA IPC
+event handles across processes.  No kernel spins on a flag here, so host and expert block
+may share one GPU.
+"""
+
+from __future__ import annotations
+
+import itertools
+import os
+import socket
+import struct
+import threading
+import timeit
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple
+
+import torch
+
+from distributedmoe_b200 import _native as N
+from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import (
+    TensorTransferEngine,
+    TensorTransferEngineConfig,
+)
+from distributedmoe_b200.TensorTransferEngine.utils import HandshakeType, Transfer, TransferStatus
+from distributedmoe_b200.utils.logging_config import get_logger
+
+# Process-local registry of completion events, addressed by 8-byte tokens in descriptors.
+_EVENTS: Dict[int, torch.cuda.Event] = {}
+_EVENTS_LOCK = threading.Lock()
+_TOKENS = itertools.count(1)
+
+_DESC = struct.Struct("!IhQQ64sQQ64s")  # pid, device, ptr, size, mem handle, offset, event token, event handle
+
+
+@dataclass
+class NVLinkRegion:
+    pid: int
+    device: int
+    ptr: int
+    size: int
+    mem_handle: bytes
+    mem_offset: int
+    event_token: int
+    event_handle: bytes
+
+
+class NVLinkTensorTransferEngine(TensorTransferEngine):
+    """``TensorTransferEngine`` over CUDA IPC + NVLink (backend ``NVLinkIPC``)."""
+
+    stream_ordered = True
+
+    def __init__(self, config: TensorTransferEngineConfig) -> None:
+        super().__init__(config)
+        self.nv_logger = get_logger("dist_moe.tte.nvlink")
+        self.pid = os.getpid()
+        self.remote_info: Dict[str, Tuple[int, int, str]] = {}
+        self._opened_mem: Dict[bytes, int] = {}       # mem handle -> mapped base (other processes)
+        self._opened_events: Dict[bytes, torch.cuda.Event] = {}
+        self._local_regions: Dict[int, NVLinkRegion] = {}
+        self._helpers: Dict[int, torch.cuda.Stream] = {}
+        self._lock = threading.Lock()
+        self._init_transfer_engine()
+        assert self.handshake()
+
+    def _init_transfer_engine(self) -> None:
+        self.transfer_engine = "cuda-ipc"
+
+    # ------------------------------------------------------------------ handshake
+    def _identity(self) -> bytes:
+        dev = torch.cuda.current_device() if torch.cuda.is_available() else -1
+        return struct.pack("!Ih", self.pid, dev) + socket.gethostname().encode()[:200]
+
+    def handshake_with_remote(self, remote_name: str) -> bool:
+        """Exchange (pid, device, hostname); CLIENT speaks first, as the NIXL agents do
+        (``NIXLTensorTransferEngine.py:87-108``)."""
+        try:
+            if self.handshake_type == HandshakeType.CLIENT:
+                ident = self._identity()
+                self.send_metadata_to(remote_name, 0, (len(ident), ident))
+                header, body = self.get_metadata_from(remote_name)
+            elif self.handshake_type == HandshakeType.SERVER:
+                header, body = self.get_metadata_from(remote_name)
+                ident = self._identity()
+                self.send_metadata_to(remote_name, 0, (len(ident), ident))
+            else:
+                return True
+            assert header == 0
+            raw = body[-1][1]
+            pid, dev = struct.unpack("!Ih", raw[:6])
+            self.remote_info[remote_name] = (pid, dev, raw[6:].decode(errors="replace"))
+            if pid == self.pid and dev >= 0 and torch.cuda.is_available():
+                here = torch.cuda.current_device()
+                if dev != here:
+                    N.enable_peer_access(here, dev)
+                    N.enable_peer_access(dev, here)
+            return True
+        except Exception as e:
+            self.nv_logger.error(f"handshake with {remote_name} failed: {e}")
+            return False
+
+    # ------------------------------------------------------------------ registration
+    def register_batch(self, data_ptrs: List[Any], data_location: Optional[str], device_id: int,
+                       data_sizes: Optional[List[int]] = None) -> Tuple[List[NVLinkRegion], List[NVLinkRegion]]:
+        regions = []
+        for i, item in enumerate(data_ptrs):
+            if isinstance(item, torch.Tensor):
+                if not item.is_cuda:
+                    raise ValueError("the NVLink transfer engine registers GPU memory only")
+                ptr, size, dev = item.data_ptr(), item.numel() * item.element_size(), item.device.index
+            else:
+                ptr, size, dev = int(item), int(data_sizes[i]), int(device_id)
+            if data_sizes is not None:
+                size = int(data_sizes[i])
+            with torch.cuda.device(dev):
+                mem_handle, mem_offset = N.ipc_export(ptr)
+                ev = torch.cuda.Event(interprocess=True)
+                ev.record(torch.cuda.current_stream(dev))  # a recorded event: waits on it return at once
+                ev_handle = ev.ipc_handle()
+            token = next(_TOKENS)
+            with _EVENTS_LOCK:
+                _EVENTS[token] = ev
+            r = NVLinkRegion(self.pid, dev, ptr, size, mem_handle, mem_offset, token, bytes(ev_handle))
+            self._local_regions[token] = r
+            regions.append(r)
+        return regions, regions
+
+    def deregister_batch(self, data_registration_descs: List[NVLinkRegion], data_sizes: Optional[List[int]] = None) -> None:
+        for r in data_registration_descs:
+            self._local_regions.pop(r.event_token, None)
+            with _EVENTS_LOCK:
+                _EVENTS.pop(r.event_token, None)
+
+    def serialize_descs(self, data_descs: List[NVLinkRegion]) -> Tuple[int, bytes]:
+        blob = struct.pack("!H", len(data_descs)) + b"".join(
+            _DESC.pack(r.pid, r.device, r.ptr, r.size, r.mem_handle, r.mem_offset, r.event_token, r.event_handle)
+            for r in data_descs)
+        return len(blob), blob
+
+    def deserialize_descs(self, data_serialized_descs: Tuple[int, bytes]) -> List[NVLinkRegion]:
+        _, blob = data_serialized_descs
+        (n,) = struct.unpack("!H", blob[:2])
+        out = []
+        for i in range(n):
+            f = _DESC.unpack_from(blob, 2 + i * _DESC.size)
+            out.append(NVLinkRegion(f[0], f[1], f[2], f[3], f[4], f[5], f[6], f[7]))
+        return out
+
+    # ------------------------------------------------------------------ addressing
+    def region_ptr(self, r: NVLinkRegion) -> int:
+        """A pointer to the region usable from this process (peer pointer or IPC mapping)."""
+        if r.pid == self.pid:
+            return r.ptr
+        with self._lock:
+            base = self._opened_mem.get(r.mem_handle)
+            if base is None:
+                base = N.ipc_open(r.mem_handle, torch.cuda.current_device())
+                self._opened_mem[r.mem_handle] = base
+        return base + r.mem_offset
+
+    def region_event(self, r: NVLinkRegion) -> torch.cuda.Event:
+        if r.pid == self.pid:
+            with _EVENTS_LOCK:
+                return _EVENTS[r.event_token]
+        with self._lock:
+            ev = self._opened_events.get(r.event_handle)
+            if ev is None:
+                ev = torch.cuda.Event.from_ipc_handle(r.device, r.event_handle)
+                self._opened_events[r.event_handle] = ev
+        return ev
+
+    def wait_region(self, regions: List[NVLinkRegion], stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Order `stream` after the last completion recorded for each region."""
+        stream = stream or torch.cuda.current_stream()
+        for r in regions:
+            stream.wait_event(self.region_event(r))
+
+    def _helper_stream(self, device: int) -> torch.cuda.Stream:
+        with self._lock:
+            h = self._helpers.get(device)
+            if h is None:
+                h = torch.cuda.Stream(device=device)
+                self._helpers[device] = h
+        return h
+
+    def signal_region(self, regions: List[NVLinkRegion], stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Record the work issued so far on `stream` as the regions' last access.  A CUDA
+        event can only be recorded on its own device, so a region of another GPU is
+        signalled through a helper stream on that GPU that waits for `stream`."""
+        stream = stream or torch.cuda.current_stream()
+        here = stream.device.index
+        tmp = None
+        for r in regions:
+            ev = self.region_event(r)
+            if r.device == here:
+                ev.record(stream)
+                continue
+            if tmp is None:
+                tmp = torch.cuda.Event()
+                tmp.record(stream)
+            h = self._helper_stream(r.device)
+            h.wait_event(tmp)
+            ev.record(h)
+
+    # ------------------------------------------------------------------ transfers
+    def _transfer(self, remote_name: str, transfer_name: bytes, src: List[NVLinkRegion], dst: List[NVLinkRegion],
+                  sizes: Optional[List[int]]) -> None:
+        stream = torch.cuda.current_stream()
+        total = 0
+        # A region's event marks its last access: wait for both ends, then record both.
+        self.wait_region(list(src) + list(dst), stream)
+        for i, (s, d) in enumerate(zip(src, dst)):
+            n = min(s.size, d.size) if sizes is None else int(sizes[i])
+            if n > min(s.size, d.size):
+                raise ValueError(f"transfer of {n} bytes exceeds the registered regions")
+            N.copy_bytes(self.region_ptr(d), self.region_ptr(s), n, stream.cuda_stream)
+            total += n
+        self.signal_region(list(src) + list(dst), stream)
+        done = torch.cuda.Event()
+        done.record(stream)
+        self._track_transfer(Transfer(transfer_name, TransferStatus.CREATED, remote_name, done, total,
+                                      timeit.default_timer()))
+
+    def read_batch_transfer(self, remote_name: str, transfer_name: bytes, src_data_transfer_descs: List[NVLinkRegion],
+                            dst_data_transfer_descs: List[NVLinkRegion], src_data_sizes: Optional[List[int]] = None) -> None:
+        """Remote -> local, on the current stream (``NIXLTensorTransferEngine.py:205-249``)."""
+        self._transfer(remote_name, transfer_name, src_data_transfer_descs, dst_data_transfer_descs, src_data_sizes)
+
+    def write_batch_transfer(self, remote_name: str, transfer_name: bytes, src_data_transfer_descs: List[NVLinkRegion],
+                             dst_data_transfer_descs: List[NVLinkRegion], src_data_sizes: Optional[List[int]] = None) -> None:
+        """Local -> remote, on the current stream (``NIXLTensorTransferEngine.py:159-203``)."""
+        self._transfer(remote_name, transfer_name, src_data_transfer_descs, dst_data_transfer_descs, src_data_sizes)
+
+    def _check_handler_status(self, transfer: Transfer) -> bool:
+        return bool(transfer.handler.query())
+
+    def close(self) -> None:
+        if self.is_closed:
+            return
+        for base in self._opened_mem.values():
+            try:
+                N.ipc_close(base)
+            except Exception as e:  # pragma: no cover - best effort at shutdown
+                self.nv_logger.warning(f"closing an IPC mapping failed: {e}")
+        self._opened_mem.clear()
+        self._opened_events.clear()
+        self.deregister_batch(list(self._local_regions.values()))
+        super().close()

@@ -58,7 +58,7 @@ SIGNATURES = {
                                               ctypes.c_int, _vp, _vp, _sz, _vp, _vp]),
     "dmoe_combine": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int, _vp, _vp]),
-    "dmoe_ipc_export": (ctypes.c_int, [_vp, _vp]),
+    "dmoe_ipc_export": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_u64)]),
     "dmoe_ipc_open": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp)]),
     "dmoe_ipc_close": (ctypes.c_int, [_vp]),
     "dmoe_enable_peer_access": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
@@ -303,10 +303,12 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, w: torch.Tensor, out: tor
 
 
 # ----------------------------------------------------------------------------- transfer
-def ipc_export(t: torch.Tensor) -> bytes:
+def ipc_export(ptr: int) -> Tuple[bytes, int]:
+    """(64-byte handle of the allocation holding ptr, byte offset of ptr inside it)."""
     buf = (ctypes.c_uint8 * 64)()
-    _check(lib().dmoe_ipc_export(t.data_ptr(), buf), "dmoe_ipc_export")
-    return bytes(buf)
+    off = _u64()
+    _check(lib().dmoe_ipc_export(ptr, buf, ctypes.byref(off)), "dmoe_ipc_export")
+    return bytes(buf), int(off.value)
 
 
 def ipc_open(handle: bytes, device: int) -> int:

@@ -5,6 +5,8 @@
 // as a cudaIpcMemHandle, the peer maps it once, and READ/WRITE become stream-ordered copies
 // over NVLink.  Flags replace the 1 ms transfer-monitor poll
 // (TensorTransferEngine/TensorTransferEngine.py:320-344).
+#include <cuda.h>
+
 #include "dmoe_common.cuh"
 
 namespace dmoe {
@@ -58,12 +60,29 @@ const char* dmoe_last_error(void) { return t_last_error.c_str(); }
 
 uint64_t dmoe_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-int dmoe_ipc_export(const void* dev_ptr, uint8_t* handle_out64) {
-  DMOE_REQUIRE(dev_ptr != nullptr && handle_out64 != nullptr, "dmoe_ipc_export: null pointer");
+int dmoe_ipc_export(const void* dev_ptr, uint8_t* handle_out64, uint64_t* offset_out) {
+  DMOE_REQUIRE(dev_ptr != nullptr && handle_out64 != nullptr && offset_out != nullptr, "dmoe_ipc_export: null pointer");
+  typedef CUresult (*PFN_range)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static PFN_range get_range = nullptr;
+  if (get_range == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    DMOE_CUDA(cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q));
+    DMOE_REQUIRE(q == cudaDriverEntryPointSuccess && p != nullptr, "cuMemGetAddressRange is unavailable");
+    get_range = reinterpret_cast<PFN_range>(p);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = get_range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr));
+  if (r != CUDA_SUCCESS) {
+    set_error("cuMemGetAddressRange failed (%d)", (int)r);
+    return DMOE_ERR_CUDA;
+  }
   cudaIpcMemHandle_t h;
-  DMOE_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+  DMOE_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
   static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
   memcpy(handle_out64, &h, 64);
+  *offset_out = (uint64_t)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
   return DMOE_OK;
 }
 

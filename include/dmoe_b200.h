@@ -127,7 +127,7 @@ int dmoe_permute_rows(const void* src, void* dst, int64_t row_bytes, const int32
  * seg_on_device == 0 (n_seg <= 256), device arrays otherwise (n_seg <= 1024).
  *  X [m_rows, d], Y [m_rows, d]; workspace >= dmoe_grouped_mlp_workspace_size(m_rows, I, dtype)
  *  Computes on tcgen05 tensor cores (fp32 accumulate in TMEM); h is rounded to dtype.
- *  Limits: d % 64 == 0, I % 64 == 0.
+ *  Limits: d % 8 == 0, I % 8 == 0 (K and N tails are zero-filled by TMA and masked).
  */
 size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype);
 int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack,
@@ -150,9 +150,11 @@ int dmoe_combine(const void* rows, const int32_t* inverse, const void* w, int w_
  * CUDA IPC for the NVLink TensorTransferEngine backend (replaces NIXL/MoonCake memory
  * registration: TensorTransferEngine.register_batch / deserialize_descs / deregister_batch,
  * TensorTransferEngine/TensorTransferEngine.py:146-192).
- *  handle: 64 opaque bytes (cudaIpcMemHandle_t).
+ *  handle: 64 opaque bytes (cudaIpcMemHandle_t) of the allocation that contains dev_ptr;
+ *  *offset_out: byte offset of dev_ptr inside that allocation (caching allocators
+ *  sub-allocate).  The importer adds the offset to the pointer dmoe_ipc_open returns.
  */
-int dmoe_ipc_export(const void* dev_ptr, uint8_t* handle_out64);
+int dmoe_ipc_export(const void* dev_ptr, uint8_t* handle_out64, uint64_t* offset_out);
 int dmoe_ipc_open(const uint8_t* handle64, int device, void** dev_ptr_out);
 int dmoe_ipc_close(void* dev_ptr);
 int dmoe_enable_peer_access(int device, int peer_device);
