@@ -1,0 +1,334 @@
+"""MoE-layer throughput benchmark (tokens/s) of the B200 framework, or of the reference's
+CPU path with ``--impl reference``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
+
+Workload (one step): one forward of a Mixtral-8x7B-shape MoE layer, T=4096 tokens, d=4096,
+E=8 experts, top-2 softmax routing renormalised over fp32 router logits, SwiGLU experts with
+inner dim 14336, bf16, seeded synthetic N(0,1) activations and N(0,0.02) weights.  The
+layer runs through the drop-in API: ``DistMoEBlock.forward`` with one ``DistExpertsBlock``
+holding the 8 experts on the same GPU, connected through the NVLink/CUDA-IPC transfer engine.
+
+* ``value``: tokens/s of forwards whose input is already in HBM (device-timed with CUDA
+  events, barrier + synchronize on both sides; max over ranks).
+* ``e2e``: the same API with the input in pinned host memory: the H2D copy of the tokens and
+  the D2H read of the layer output are inside the timed region.
+* ``roofline``: the grouped expert MLP (the tcgen05 GEMM pair) timed with CUDA events on its
+  own stream during the timed steps, against the measured bf16 peak.
+* ``cpu_baseline``: the oracle port of the reference's torch path (routing +
+  ``local_experts``), timed on this host's cores on a bounded token sample.
+
+With N GPUs each rank runs its own layer replica (weak scaling; the layer does not
+exchange data between ranks in this workload).  The expert weights (2.8 GB) exceed L2, so
+every step streams them from HBM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+T_TOK, D, E, K, I = 4096, 4096, 8, 2, 14336
+SEED = 1
+WORKLOAD = "mixtral-8x7b-moe-layer"
+METRIC = "moe_layer_tokens_per_s"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def _config(n_gpus):
+    return {"workload": WORKLOAD, "tokens": T_TOK, "hidden": D, "experts": E, "top_k": K, "inner": I,
+            "router": "softmax top-2 renormalised, fp32 logits", "activation": "silu (SwiGLU)",
+            "expert_blocks": 1, "io_buffer_size": 8192, "transfer_engine": "NVLinkIPC",
+            "l2": "no flush: the 2.8 GB of expert weights exceed the 126 MB L2 every step",
+            "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single gpu", "seed": SEED}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"dmoe_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        mx = max(int(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        loaded = [s for s, r in zip(sm, rows) if float(r[3] or 0) > 300] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3] or 0) for r in rows)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        return dist, dist.get_rank(), ws, int(os.environ.get("LOCAL_RANK", "0"))
+    return None, 0, 1, 0
+
+
+def _barrier(dist, dev):
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+
+
+def _max_over_ranks(dist, v: float, dev) -> float:
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU (oracle port)
+class CpuReference:
+    """The oracle port of the reference's torch path on this host's cores: fp32-logit routing,
+    top-2 renormalised, then ``local_experts`` (per hit expert: gather, gate/up/down in bf16,
+    weighted index_add) on a token sample of the Mixtral-shape layer with full-size weights."""
+
+    def __init__(self, step_budget_s: float = 1.5, max_tokens: int = 1024):
+        from oracle import moe_oracle as O
+
+        self.O = O
+        self.threads = torch.get_num_threads()
+        g = torch.Generator().manual_seed(SEED)
+        # One random matrix per projection, copied per expert: the timing depends on the
+        # shapes, not on the values.
+        base_gu = (torch.randn(I, D, generator=g) * 0.02).to(torch.bfloat16)
+        base_d = (torch.randn(D, I, generator=g) * 0.02).to(torch.bfloat16)
+        self.wg = torch.stack([base_gu] * E)
+        self.wu = torch.stack([base_gu.roll(1, 0)] * E)
+        self.wd = torch.stack([base_d] * E)
+        self.wr = (torch.randn(E, D, generator=g) * 0.02).to(torch.bfloat16)
+        self.g = g
+        n = 64
+        dt = self.step(n)
+        while dt < step_budget_s / 2 and n < max_tokens:
+            n *= 2
+            dt = self.step(n)
+        self.n = n
+
+    def step(self, n: int = 0) -> float:
+        n = n or self.n
+        x = torch.randn(n, D, generator=self.g).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        logits = self.O.router_logits(x, self.wr, fp32_logits=True)
+        self.O.local_experts(x, logits, self.wg, self.wu, self.wd, K, act=self.O.ACT_SILU, renormalize=True)
+        return time.perf_counter() - t0
+
+    def sample(self, reps: int) -> str:
+        return f"{self.n} tokens of the {WORKLOAD} shape per step (full-size bf16 weights, torch CPU), {reps} steps"
+
+    def tokens_per_s(self, reps: int = 3) -> float:
+        return self.n / statistics.median(self.step() for _ in range(reps))
+
+
+def run_reference(args, dist, rank):
+    if rank != 0:
+        return
+    ref = CpuReference()
+    for _ in range(args.warmup):
+        ref.step()
+    times = [ref.step() for _ in range(args.steps)]
+    tok_s = ref.n * len(times) / sum(times)
+    line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": T_TOK / tok_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _config(args.gpus),
+            "impl": "reference",
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+                             "sample": ref.sample(args.steps)},
+            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU (ours)
+def run_ours(args, dist, rank, world, local_rank):
+    from distributedmoe_b200 import _native as N
+    from distributedmoe_b200.MoE.local_cluster import LocalCluster
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(SEED + rank)
+    dt = torch.bfloat16
+    gate = (torch.randn(E, I, D, generator=gen, device=dev) * 0.02).to(dt)
+    up = (torch.randn(E, I, D, generator=gen, device=dev) * 0.02).to(dt)
+    down = (torch.randn(E, D, I, generator=gen, device=dev) * 0.02).to(dt)
+    w_r = (torch.randn(E, D, generator=gen, device=dev) * 0.02).to(dt)
+    x = torch.randn(T_TOK, D, generator=gen, device=dev).to(dt)
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(T_TOK, D, dtype=dt).pin_memory()
+
+    cluster = LocalCluster(E, [list(range(E))], K, D, dt, dev, [dev], stacked=[(gate, up, down)],
+                           io_buffer_size=8192, number_of_io_buffers=2, activation="silu", renormalize=True,
+                           router_fp32_logits=True)
+    moe = cluster.moe
+    with torch.no_grad():
+        moe.gate.weight.copy_(w_r)
+    stream = torch.cuda.current_stream(dev)
+    try:
+        for _ in range(args.warmup):
+            moe(x)
+        _barrier(dist, dev)
+        N.check_device_status(dev)
+
+        # ---------------------------------------------------------- value: device-resident input
+        launches0 = N.launch_count()
+        N.enable_kernel_timing(True)
+        with ClockSampler(dev.index) as clk:
+            _barrier(dist, dev)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                moe(x)
+            t1.record(stream)
+            _barrier(dist, dev)
+        ktimes = N.kernel_times_ms()
+        N.enable_kernel_timing(False)
+        launches = N.launch_count() - launches0
+        ms = _max_over_ranks(dist, t0.elapsed_time(t1) / args.steps, dev)
+        N.check_device_status(dev)
+
+        # ---------------------------------------------------------- e2e: pinned host in/out
+        for _ in range(2):
+            y = moe(x_host.to(dev, non_blocking=True))
+            y_host.copy_(y, non_blocking=True)
+        _barrier(dist, dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            xd = x_host.to(dev, non_blocking=True)
+            y = moe(xd)
+            y_host.copy_(y, non_blocking=True)
+        e1.record(stream)
+        _barrier(dist, dev)
+        e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / args.steps, dev)
+    finally:
+        cluster.close()
+
+    if rank != 0:
+        return
+    burst, sustained, hbm, src = _peaks()
+    flops = 6.0 * T_TOK * K * D * I
+    mlp = ktimes.get("grouped_gated_mlp", [])
+    mlp_ms = statistics.median(mlp) if mlp else None
+    achieved = flops / (mlp_ms * 1e-3) / 1e12 if mlp_ms else None
+    comb = ktimes.get("combine", [])
+    comb_ms = statistics.median(comb) if comb else None
+    comb_bytes = T_TOK * K * D * 2 + T_TOK * D * 2 + T_TOK * K * 4
+    cpu_tok_s, cores, sample = None, None, None
+    if not args.no_cpu:
+        ref = CpuReference()
+        cpu_tok_s, cores, sample = ref.tokens_per_s(3), ref.threads, ref.sample(3)
+    total_tokens = T_TOK * world
+    line = {
+        "metric": METRIC, "value": total_tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _config(world),
+        "impl": "ours",
+        "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": T_TOK * D * 2, "d2h_bytes_per_step": T_TOK * D * 2},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "grouped_gated_mlp (tcgen05 gate/up+SwiGLU, down)",
+                     "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": (achieved / sustained) if achieved else None, "peak_kind": f"{src} sustained bf16",
+                     "frac_of_burst_peak": (achieved / burst) if achieved else None,
+                     "flops_per_launch": flops, "ms_per_launch": mlp_ms, "traffic": None},
+        "hbm_ops": {"combine_ms": comb_ms, "combine_gbs": comb_bytes / (comb_ms * 1e-3) / 1e9 if comb_ms else None,
+                    "hbm_peak_gbs": hbm,
+                    "op_ms": {k: statistics.median(v) for k, v in ktimes.items() if v}},
+        "cpu_baseline": {"value": cpu_tok_s, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if ws > 1 and rank != 0:
+            return
+        run_reference(args, None, rank)
+        return
+    dist, rank, world, local_rank = _dist()
+    try:
+        run_ours(args, dist, rank, world, local_rank)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -156,6 +156,51 @@ class _Scratch:
 scratch = _Scratch()
 
 
+# ----------------------------------------------------------------------------- timing
+_timing: Optional[Dict[str, list]] = None
+_timing_lock = threading.Lock()
+
+
+def enable_kernel_timing(on: bool = True) -> None:
+    """Record CUDA events around every library op (per op name) until disabled."""
+    global _timing
+    with _timing_lock:
+        _timing = {} if on else None
+
+
+def kernel_times_ms() -> Dict[str, list]:
+    """Durations (ms) of the ops recorded since timing was enabled; synchronises."""
+    with _timing_lock:
+        snap = dict(_timing or {})
+    out = {}
+    for name, pairs in snap.items():
+        out[name] = []
+        for a, b in pairs:
+            b.synchronize()
+            out[name].append(a.elapsed_time(b))
+    return out
+
+
+class _Timed:
+    __slots__ = ("name", "stream", "ev")
+
+    def __init__(self, name: str, stream: int, device: torch.device):
+        self.name = name
+        self.ev = None
+        if _timing is not None:
+            self.stream = torch.cuda.ExternalStream(stream, device=device)
+            self.ev = torch.cuda.Event(enable_timing=True)
+            self.ev.record(self.stream)
+
+    def done(self) -> None:
+        if self.ev is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record(self.stream)
+            with _timing_lock:
+                if _timing is not None:
+                    _timing.setdefault(self.name, []).append((self.ev, end))
+
+
 def check_device_status(device: torch.device, reset: bool = True) -> None:
     """Raise if a kernel on `device` reported a timed-out wait or a bad segment table.
     Synchronises with the device status word (a 4-byte read)."""
@@ -199,11 +244,13 @@ def router(x: Optional[torch.Tensor], w_r: Optional[torch.Tensor], top_k: int, *
     for b in (logit_bias, score_bias):
         if b is not None and (b.dtype != torch.float32 or b.numel() != E):
             raise DMoEError("router biases must be fp32 [E]")
+    tm = _Timed("router", _stream(dev), dev)
     rc = lib().dmoe_router(_ptr(x) if logits_in is None else None, _ptr(w_r) if logits_in is None else None,
                            dtype_code(x_dtype), _ptr(logit_bias), _ptr(score_bias), _ptr(logits_in), T, d, E, top_k,
                            mode, int(renormalize), float(scale), n_group, topk_group, _ptr(logits), idx.data_ptr(),
                            w.data_ptr(), dtype_code(w.dtype), _stream(dev))
     _check(rc, "dmoe_router")
+    tm.done()
     return idx, w, logits
 
 
@@ -229,11 +276,13 @@ def route_plan(idx: torch.Tensor, w: Optional[torch.Tensor], num_experts: int, *
         res["perm_weight"] = torch.empty(n, dtype=w.dtype, device=dev)
     ws_bytes = lib().dmoe_route_plan_workspace_size(T, k, E)
     ws = scratch.get(dev, "plan", ws_bytes)
+    tm = _Timed("route_plan", _stream(dev), dev)
     rc = lib().dmoe_route_plan(idx.data_ptr(), _ptr(w), dtype_code(w.dtype) if w is not None else BF16, T, k, E,
                                res["counts"].data_ptr(), res["offsets"].data_ptr(), res["perm_token"].data_ptr(),
                                _ptr(res.get("perm_slot")), _ptr(res.get("inverse")), _ptr(res.get("perm_weight")),
                                ws.data_ptr(), ws.numel(), _stream(dev))
     _check(rc, "dmoe_route_plan")
+    tm.done()
     return res
 
 
@@ -252,10 +301,13 @@ def permute_rows(src: torch.Tensor, dst: torch.Tensor, seg_src: Sequence[int], s
     if dst.shape[-1] * dst.element_size() != row_bytes:
         raise DMoEError("src and dst rows differ in size")
     n = len(seg_len)
+    st = stream if stream is not None else _stream(dev)
+    tm = _Timed("permute_rows", st, dev)
     rc = lib().dmoe_permute_rows(src.data_ptr(), dst_ptr if dst_ptr is not None else dst.data_ptr(), row_bytes,
                                  _ptr(row_map), _i32_array(seg_src), _i32_array(seg_dst), _i32_array(seg_len), n,
-                                 stream if stream is not None else _stream(dev))
+                                 st)
     _check(rc, "dmoe_permute_rows")
+    tm.done()
 
 
 def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
@@ -282,11 +334,13 @@ def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
         a1, a2 = _i32_array(seg_expert), _i32_array(seg_end)
         se, sn, on_dev = ctypes.addressof(a1), ctypes.addressof(a2), 0
         keep = (a1, a2)
+    tm = _Timed("grouped_gated_mlp", _stream(dev), dev)
     rc = lib().dmoe_grouped_gated_mlp(X.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
                                       se, sn, n_seg, on_dev, m_rows, act, Y.data_ptr(), ws.data_ptr(), ws.numel(),
                                       scratch.status(dev).data_ptr(), _stream(dev))
     del keep
     _check(rc, "dmoe_grouped_gated_mlp")
+    tm.done()
 
 
 def combine(rows: torch.Tensor, inverse: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
@@ -297,9 +351,11 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, w: torch.Tensor, out: tor
     d = out.shape[-1]
     if rows.dtype != out.dtype:
         raise DMoEError("rows and out must share a dtype")
+    tm = _Timed("combine", _stream(dev), dev)
     rc = lib().dmoe_combine(rows.data_ptr(), inverse.data_ptr(), w.data_ptr(), dtype_code(w.dtype), T, k, d,
                             dtype_code(out.dtype), int(accumulate), out.data_ptr(), _stream(dev))
     _check(rc, "dmoe_combine")
+    tm.done()
 
 
 # ----------------------------------------------------------------------------- transfer
