@@ -51,6 +51,8 @@ SIGNATURES = {
     "dmoe_route_plan_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "dmoe_route_plan": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
                                        _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "dmoe_route_plan_noalloc": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                               _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dmoe_permute_rows": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, ctypes.c_int, _vp]),
     "dmoe_grouped_mlp_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "dmoe_grouped_gated_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,

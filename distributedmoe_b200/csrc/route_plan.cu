@@ -11,6 +11,8 @@
 //   2. plan_scan    : counts, offsets, and base[c][e] = offsets[e] + sum_{c'<c} hist[c'][e]
 //   3. plan_scatter : each chunk ranks its activations stably (warp match + per-warp
 //                     prefix) and writes perm_token / perm_slot / inverse / perm_weight.
+#include <mutex>
+
 #include "dmoe_common.cuh"
 
 namespace dmoe {
@@ -133,6 +135,39 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter(const int64_t* idx,
   }
 }
 
+// Scratch of dmoe_route_plan_noalloc: the per-chunk histogram matrix lives in this
+// library-owned device array instead of caller memory.  Every GPU that loads the library
+// holds it until the process exits.
+constexpr size_t kNoAllocScratchBytes = 512 * 1024;
+static __device__ __align__(256) int32_t g_plan_scratch[kNoAllocScratchBytes / sizeof(int32_t)];
+
+// The array's name in host code is a host-side stand-in, not a device address; the device
+// address comes from cudaGetSymbolAddress, once per device, with that device current.
+int32_t* plan_scratch_address(int* rc) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static int32_t* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("dmoe_route_plan_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
+    *rc = DMOE_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_plan_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("dmoe_route_plan_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+      *rc = DMOE_ERR_CUDA;
+      return nullptr;
+    }
+    addr[dev] = reinterpret_cast<int32_t*>(p);
+  }
+  return addr[dev];
+}
+
 }  // namespace
 }  // namespace dmoe
 
@@ -173,4 +208,23 @@ extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, i
     DMOE_LAUNCH_CHECK();
   }
   return DMOE_OK;
+}
+
+extern "C" int dmoe_route_plan_noalloc(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E,
+                                       int32_t* counts, int32_t* offsets, int32_t* perm_token, int32_t* perm_slot,
+                                       int32_t* inverse, void* perm_weight, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(E >= 1 && E <= kMaxPlanExperts, "dmoe_route_plan_noalloc: need 1 <= E <= %d (E=%d)", kMaxPlanExperts, E);
+  DMOE_REQUIRE(T >= 0 && k >= 1 && (int64_t)T * k < (1ll << 31), "dmoe_route_plan_noalloc: bad T=%d k=%d", T, k);
+  const size_t need = dmoe_route_plan_workspace_size(T, k, E);
+  DMOE_REQUIRE(need <= kNoAllocScratchBytes,
+               "dmoe_route_plan_noalloc: T*k=%lld with E=%d needs %zu bytes of scratch, more than the library's "
+               "static %zu bytes; use dmoe_route_plan with a caller workspace",
+               (long long)T * k, E, need, kNoAllocScratchBytes);
+  int rc = DMOE_OK;
+  int32_t* scratch = plan_scratch_address(&rc);
+  if (scratch == nullptr) return rc;
+  // plan_hist writes every histogram entry it later reads, so the shared scratch needs no clearing.
+  return dmoe_route_plan(idx, w, w_dtype, T, k, E, counts, offsets, perm_token, perm_slot, inverse, perm_weight,
+                         scratch, kNoAllocScratchBytes, stream);
 }

@@ -102,6 +102,27 @@ int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, int T, int k
                     void* perm_weight, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Routing plan without caller scratch.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory around a call -- an FFI host that is handed
+ * only its input and output buffers, or a serving loop whose device memory is owned by
+ * another allocator and where cudaMalloc/cudaFree (which can synchronise the device) are
+ * not allowed.  Same arguments and results as dmoe_route_plan, minus the workspace; it
+ * calls no allocator.
+ *  Scratch: a 512 KiB library-owned static device array, held by every GPU that loads the
+ *  library until the process exits.  Limit: dmoe_route_plan_workspace_size(T, k, E) must be
+ *  <= 512 KiB, i.e. ceil(T*k / 2048) * E <= 131072 (T*k <= 1048576 with E <= 256,
+ *  T*k <= 262144 with E <= 1024); larger requests fail with DMOE_ERR_INVALID and a message.
+ *  The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *  with that device current; make that first call before any stream capture.
+ *  All calls share the one array: calls whose executions overlap on the GPU (different
+ *  streams, or different host threads) race and corrupt each other's plans.  Serialise
+ *  them on one stream.
+ */
+int dmoe_route_plan_noalloc(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E, int32_t* counts,
+                            int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse,
+                            void* perm_weight, void* stream);
+
+/*
  * Segmented row gather/copy: for segment i and r < seg_len[i]
  *     dst[seg_dst[i] + r] = src[ row_map ? row_map[seg_src[i] + r] : seg_src[i] + r ]
  * with rows of row_bytes bytes (multiple of 16, 16-byte aligned bases).
