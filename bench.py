@@ -306,6 +306,36 @@ def run_ours(args, dist, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_gemm_only(args):
+    """Kernel-only mode for profiling the grouped expert MLP: X [rows, 4096] split evenly over
+    `gemm_experts` experts of the Mixtral expert shape, SwiGLU, bf16.  Prints one JSON line
+    with the CUDA-event time per launch pair (not a bench line)."""
+    from distributedmoe_b200 import _native as N
+
+    dev = torch.device("cuda", 0)
+    Eg, rows = args.gemm_experts, args.gemm_rows
+    gen = torch.Generator(device=dev).manual_seed(SEED)
+    X = torch.randn(rows, D, generator=gen, device=dev).to(torch.bfloat16)
+    wg = (torch.randn(Eg, I, D, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    wu = (torch.randn(Eg, I, D, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(Eg, D, I, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    Y = torch.empty(rows, D, dtype=torch.bfloat16, device=dev)
+    ends = [rows * (e + 1) // Eg for e in range(Eg)]
+    for _ in range(args.warmup):
+        N.grouped_gated_mlp(X, wg, wu, wd, list(range(Eg)), ends, N.ACT_SILU, Y)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        N.grouped_gated_mlp(X, wg, wu, wd, list(range(Eg)), ends, N.ACT_SILU, Y)
+    b.record()
+    torch.cuda.synchronize()
+    N.check_device_status(dev)
+    ms = a.elapsed_time(b) / args.steps
+    print(json.dumps({"mode": "gemm", "rows": rows, "experts": Eg, "ms_per_launch_pair": ms,
+                      "tflops": 6.0 * rows * D * I / (ms * 1e-3) / 1e12}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -313,7 +343,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--mode", default="layer", choices=["layer", "gemm"],
+                    help="gemm: time only the grouped expert MLP (for kernel profiling)")
+    ap.add_argument("--gemm-rows", type=int, default=4096)
+    ap.add_argument("--gemm-experts", type=int, default=2)
     args = ap.parse_args()
+    if args.mode == "gemm":
+        run_gemm_only(args)
+        return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))

@@ -22,6 +22,9 @@
 // and reports through the caller's device status word instead of hanging.
 #include <cuda.h>
 
+#include <cstdlib>
+#include <cstring>
+
 #include "dmoe_common.cuh"
 
 namespace dmoe {
@@ -62,6 +65,7 @@ struct GemmArgs {
   int n_tiles_n;    // output column tiles
   int raster_n_fast;
   int act;
+  int prefetch;     // k-blocks of L2 prefetch ahead of the TMA loads (0: off)
   int32_t* status;
 };
 
@@ -100,9 +104,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: true once the phase of `parity` completed; false on timeout or when another
 // role of this CTA already gave up (abort flag).
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
-                                       int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
+                                            int code) {
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -113,6 +116,11 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile 
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
+                                          int code) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, status, code);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -129,6 +137,21 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+// L2 prefetch of a tile (no shared memory, no barrier): hides the DRAM latency of the
+// weight tiles that several CTAs request at the same time.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
@@ -214,6 +237,7 @@ struct TileInfo {
   int row0, row_end, expert, nt;
 };
 
+template <int TILE_M>
 __device__ __forceinline__ TileInfo decode_tile(int tile, int total_m, int n_tiles_n, int raster_n_fast, int n_seg,
                                                 const int32_t* s_start, const int32_t* s_end,
                                                 const int32_t* s_expert, const int32_t* s_tile) {
@@ -231,7 +255,7 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, int total_m, int n_til
     if (s_tile[mid] <= mt) lo = mid; else hi = mid - 1;
   }
   TileInfo ti;
-  ti.row0 = s_start[lo] + (mt - s_tile[lo]) * BM;
+  ti.row0 = s_start[lo] + (mt - s_tile[lo]) * TILE_M;
   ti.row_end = s_end[lo];
   ti.expert = s_expert[lo];
   ti.nt = nt;
@@ -322,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t armed = 0, armed_ph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const TileInfo ti = decode_tile(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+        const TileInfo ti = decode_tile<BM>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
                                         s_expert, s_tile);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_PRODUCER)) {
@@ -338,6 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(sb + B_BYTES / 2, &tm_b1, &full[stage], kb * BK, ti.nt * (BN / 2), ti.expert);
           } else {
             tma_load_3d(sb, &tm_b0, &full[stage], kb * BK, ti.nt * BN, ti.expert);
+          }
+          const int kp = kb + args.prefetch;
+          if (args.prefetch > 0 && kp < nk) {
+            tma_prefetch_2d(&tm_a, kp * BK, ti.row0);
+            if constexpr (GATED) {
+              tma_prefetch_3d(&tm_b0, kp * BK, ti.nt * (BN / 2), ti.expert);
+              tma_prefetch_3d(&tm_b1, kp * BK, ti.nt * (BN / 2), ti.expert);
+            } else {
+              tma_prefetch_3d(&tm_b0, kp * BK, ti.nt * BN, ti.expert);
+            }
           }
           armed |= 1u << stage;
           armed_ph = (armed_ph & ~(1u << stage)) | (ph << stage);
@@ -411,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-      const TileInfo ti = decode_tile(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+      const TileInfo ti = decode_tile<BM>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
                                       s_expert, s_tile);
       const bool got = mbar_wait(&accf[acc], acc_ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, got)) break;
@@ -477,6 +511,382 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------- 2-SM variant
+// A CTA pair (cluster of 2) computes a 256-row x 256-column tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  Each CTA loads its own 128 rows of A and
+// its own half of B (128 of the 256 B rows), which
+// halves the B traffic per SM.  A stage spans K=128 (two 64-wide TMA boxes per operand,
+// 8 MMAs per barrier round): 3 stages of 64 KB.  Each CTA's TMEM holds its 128 rows x 256
+// fp32 columns; each CTA's epilogue drains its own TMEM.  For the gated GEMM, CTA 0's B
+// half is the gate tile and CTA 1's the up tile, so each accumulator again holds gate in
+// columns 0..127 and up in 128..255.
+// Synchronisation (all waits bounded):
+//   full[s]   (leader only) count 1: the leader's producer arms expect_tx with both CTAs'
+//             bytes; both CTAs' TMA loads (.cta_group::2) complete on the leader's barrier.
+//   empty[s]  (both) count 1: the leader's MMA commit arrives on both CTAs.
+//   accf[a]   (both) count 1: the leader's commit after a tile arrives on both CTAs.
+//   acce[a]   (leader) count 8: 4 epilogue warps of each CTA (the peer's remotely).
+//   bye       (both) count 1: exit handshake, so no CTA leaves while the peer may still
+//             touch its shared memory.
+constexpr int BM2 = 256;
+constexpr int BK2 = 128;                      // two 64-wide swizzle atoms per stage: 8 MMAs per barrier round
+constexpr int STAGES2 = 3;
+constexpr int SUB2_BYTES = 128 * BK * 2;      // one [128 x 64] box
+constexpr int A2_BYTES = 2 * SUB2_BYTES;
+constexpr int B2_BYTES = 2 * SUB2_BYTES;
+constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int kSmemBytes2 = 1024 + STAGES2 * STAGE2_BYTES + kBarBytes + kSegBytes;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                                 int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair once the MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
+  const uint16_t both = 0x3;
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                   "r"(smem_u32(bar)),
+               "h"(both)
+               : "memory");
+}
+
+template <int DT>
+__host__ __device__ constexpr uint32_t make_idesc_pair() {
+  return (1u << 4) | ((DT == DMOE_BF16 ? 1u : 0u) << 7) | ((DT == DMOE_BF16 ? 1u : 0u) << 10) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+}
+
+template <bool GATED, int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
+                            const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ GemmSegs segs,
+                            const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint64_t* empty = full + STAGES2;
+  uint64_t* accf = empty + STAGES2;
+  uint64_t* acce = accf + 2;
+  uint64_t* fin = acce + 2;
+  uint64_t* bye = fin + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bye + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_start = reinterpret_cast<int32_t*>(smem + STAGES2 * STAGE2_BYTES + kBarBytes);
+  int32_t* s_end = s_start + (kMaxSegDev + 1);
+  int32_t* s_expert = s_end + (kMaxSegDev + 1);
+  int32_t* s_tile = s_expert + (kMaxSegDev + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int n_seg = segs.n_seg;
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+
+  for (int i = threadIdx.x; i < n_seg; i += blockDim.x) {
+    s_expert[i] = segs.dev_expert ? segs.dev_expert[i] : segs.expert[i];
+    s_end[i] = segs.dev_end ? segs.dev_end[i] : segs.end[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev = 0, tiles = 0, bad = 0;
+    for (int i = 0; i < n_seg; ++i) {
+      int en = s_end[i];
+      if (en < prev || en > segs.m_rows) {
+        bad = 1;
+        en = en < prev ? prev : segs.m_rows;
+      }
+      int len = en - prev;
+      if (s_expert[i] < 0 || s_expert[i] >= segs.e_stack) {
+        bad = 1;
+        len = 0;
+        s_expert[i] = 0;
+      }
+      s_start[i] = prev;
+      s_end[i] = prev + len;
+      s_tile[i] = tiles;
+      tiles += (len + BM2 - 1) / BM2;
+      prev = en;
+    }
+    s_tile[n_seg] = tiles;
+    if (bad && blockIdx.x == 0) atomicOr(args.status, DMOE_DEVERR_BAD_SEGMENT);
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 8);
+    }
+    mbar_init(fin, 1);
+    mbar_init(bye, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or TMA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_m = s_tile[n_seg];
+  const int total = total_m * args.n_tiles_n;
+  const int nk = (args.K + BK2 - 1) / BK2;
+  const uint32_t full_leader0 = map_to_cta(smem_u32(&full[0]), 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t armed = 0, armed_ph = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total && ok; tile += n_pairs) {
+        const TileInfo ti = decode_tile<BM2>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+                                        s_expert, s_tile);
+        const int arow = ti.row0 + (int)rank * 128;
+        const int brow = GATED ? ti.nt * 128 : ti.nt * BN + (int)rank * 128;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE2_BYTES;
+          uint8_t* sb = sa + A2_BYTES;
+          const uint32_t fbar = full_leader0 + (uint32_t)(stage * sizeof(uint64_t));
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE2_BYTES);
+          const CUtensorMap* tb = (GATED && rank == 1) ? &tm_b1 : &tm_b0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int k0 = kb * BK2 + h * BK;  // a box past K reads zeros and still counts its bytes
+            tma_load_2d_pair(sa + h * SUB2_BYTES, &tm_a, fbar, k0, arow);
+            tma_load_3d_pair(sb + h * SUB2_BYTES, tb, fbar, k0, brow, ti.expert);
+          }
+          const int kp = kb + args.prefetch;
+          if (args.prefetch > 0 && kp < nk) {
+            tma_prefetch_2d(&tm_a, kp * BK2, arow);
+            tma_prefetch_3d(tb, kp * BK2, brow, ti.expert);
+          }
+          armed |= 1u << stage;
+          armed_ph = (armed_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == STAGES2) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // The leader's full barriers count both CTAs' bytes: wait for every phase it armed.
+      if (leader) {
+        for (int s = 0; s < STAGES2; ++s) {
+          if (armed >> s & 1u) {
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait(&full[s], armed_ph >> s & 1u)) {
+              if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+                atomicOr(args.status, DMOE_DEVERR_TIMEOUT_TEARDOWN);
+                break;
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc_pair<DT>();
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total && ok; tile += n_pairs) {
+        if (!mbar_wait(&acce[acc], acc_ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sdesc_sw128(smem_u32(smem + stage * STAGE2_BYTES));
+          const uint64_t bd = sdesc_sw128(smem_u32(smem + stage * STAGE2_BYTES + A2_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK2 / 16; ++k) {
+            // sub-box k/4 (16 KB = 1024 in the descriptor's 16-byte units), then +32 bytes per K=16
+            const uint64_t off = (uint64_t)((k >> 2) * (SUB2_BYTES >> 4) + 2 * (k & 3));
+            umma_f16_pair(d_tmem, ad + off, bd + off, idesc, (kb | k) != 0);
+          }
+          umma_commit_both(&empty[stage]);
+          if (++stage == STAGES2) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_both(&accf[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1u;
+      }
+      umma_commit_both(fin);
+    }
+    if (lane == 0) {
+      // Every MMA of the pair (issued by the leader) has completed once `fin` fires in this CTA.
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(fin, 0)) {
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(args.status, DMOE_DEVERR_TIMEOUT_TEARDOWN);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const uint32_t acce_leader0 = map_to_cta(smem_u32(&acce[0]), 0);
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = pair; tile < total; tile += n_pairs) {
+      const TileInfo ti = decode_tile<BM2>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+                                      s_expert, s_tile);
+      const bool got = mbar_wait(&accf[acc], acc_ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int row = ti.row0 + (int)rank * 128 + q * 32 + lane;
+      const bool valid = row < ti.row_end;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (GATED) {
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          uint32_t g[32], u[32];
+          __syncwarp();
+          tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
+          const int col0 = ti.nt * (BN / 2) + j * 32;
+          if (valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
+              const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
+              pk[i] = pack2<DT>(h0, h1);
+            }
+            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col0 + v * 8 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t y[32];
+          __syncwarp();
+          tmem_ld32(tbase + j * 32, y);
+          const int col0 = ti.nt * BN + j * 32;
+          if (valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
+            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col0 + v * 8 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // Exit handshake: tell the peer this CTA is done with the pair's shared state, then wait
+  // (bounded) until the peer says the same.
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(map_to_cta(smem_u32(bye), rank ^ 1u));
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bye, 0)) {
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(args.status, DMOE_DEVERR_TIMEOUT_TEARDOWN);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------------- host side
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -535,6 +945,62 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
   return DMOE_OK;
 }
 
+template <bool GATED, int DT>
+int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
+                    const GemmArgs& args, int max_pairs, cudaStream_t stream) {
+  static int configured_device = -1;
+  static int max_clusters = 0;
+  int dev = 0;
+  DMOE_CUDA(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes2;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (configured_device != dev) {
+    DMOE_CUDA(cudaFuncSetAttribute(grouped_gemm_2sm_kernel<GATED, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSmemBytes2));
+    cfg.gridDim = dim3(2 * 74);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_2sm_kernel<GATED, DT>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 64;
+    }
+    max_clusters = n;
+    configured_device = dev;
+  }
+  int pairs = max_clusters;
+  if (max_pairs >= 0 && max_pairs < pairs) pairs = max_pairs;
+  if (pairs < 1) pairs = 1;
+  cfg.gridDim = dim3(2 * pairs);
+  DMOE_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_2sm_kernel<GATED, DT>, a, b0, b1, segs, args));
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}
+
+// Kernel variant: DMOE_GEMM_VARIANT=1sm|2sm forces one; otherwise 2-SM tiles are used when the
+// segments average at least 128 rows (a 256-row pair tile would otherwise be mostly padding).
+// L2 prefetch distance in k-blocks (DMOE_GEMM_PREFETCH; default 0 = off: on B200 the extra TMA
+// prefetch requests cost more throughput than the latency they hide for these shapes).
+int prefetch_distance() {
+  const char* v = getenv("DMOE_GEMM_PREFETCH");
+  if (v && *v) return atoi(v);
+  return 0;
+}
+
+bool use_2sm(int n_seg, int m_rows) {
+  const char* v = getenv("DMOE_GEMM_VARIANT");
+  if (v && strcmp(v, "1sm") == 0) return false;
+  if (v && strcmp(v, "2sm") == 0) return true;
+  return n_seg > 0 && m_rows / n_seg >= 128;
+}
+
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -578,9 +1044,32 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     int r = make_map(&td, DT, w_down, 3, dims, box);
     if (r) return r;
   }
-  const int sms = sm_count();
   const int nt1 = (I + BN / 2 - 1) / (BN / 2);
   const int nt2 = (d + BN - 1) / BN;
+  if (use_2sm(segs.n_seg, m_rows)) {
+    CUtensorMap td2;
+    const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
+    const uint32_t box[3] = {BK, 128, 1};
+    int r = make_map(&td2, DT, w_down, 3, dims, box);
+    if (r) return r;
+    int p1 = -1, p2 = -1;
+    if (total_m_host >= 0) {  // total_m_host counts 128-row tiles; pair tiles are 256 rows
+      if (total_m_host == 0) return DMOE_OK;
+      int pair_m = 0, prev = 0;
+      for (int i = 0; i < segs.n_seg; ++i) {
+        pair_m += (segs.end[i] - prev + BM2 - 1) / BM2;
+        prev = segs.end[i];
+      }
+      p1 = pair_m * nt1;
+      p2 = pair_m * nt2;
+    }
+    GemmArgs a1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
+    r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, p1, stream);
+    if (r) return r;
+    GemmArgs a2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
+    return launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, p2, stream);
+  }
+  const int sms = sm_count();
   int g1 = sms, g2 = sms;
   if (total_m_host >= 0) {
     const int64_t t1 = (int64_t)total_m_host * nt1, t2 = (int64_t)total_m_host * nt2;
@@ -588,10 +1077,10 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     g1 = (int)(t1 < sms ? t1 : sms);
     g2 = (int)(t2 < sms ? t2 : sms);
   }
-  GemmArgs a1{H, I, I, d, nt1, 0, act, status};
+  GemmArgs a1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
   int r = launch_gemm<true, DT>(ta, tg, tu, segs, a1, g1, stream);
   if (r) return r;
-  GemmArgs a2{Y, d, d, I, nt2, 1, act, status};
+  GemmArgs a2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
   return launch_gemm<false, DT>(th, td, td, segs, a2, g2, stream);
 }
 
