@@ -325,10 +325,31 @@ class ExpertsBlockPipelineTask(PipelineTask):
                 seg_end.append(off + size)
             rows = seg_end[-1] if seg_end else 0
 
-            # READ: only the rows this task packed.
             if self.input_buffer_index == -1:
                 self.input_buffer_index, self.input_buffer = await self.input_buffers_pool.acquire()
             in_buf = self.input_buffer
+            tte = self.tensor_transfer_engine
+            host_in = host_input_buffers_transfer_descs[host_in_id]
+            host_out = host_output_buffers_transfer_descs[host_out_id]
+            dev = in_buf.device.index
+            if hasattr(tte, "region_is_local") and tte.region_is_local(host_in[0], dev) \
+                    and tte.region_is_local(host_out[0], dev):
+                # The host's buffers live on this GPU: compute straight from its input buffer
+                # into its output buffer (no READ/WRITE copies), ordered by their region events.
+                s = in_buf.cuda_stream
+                with torch.cuda.stream(s):
+                    tte.wait_region(host_in + host_out, s)
+                    N.grouped_gated_mlp_ptrs(tte.region_ptr(host_in[0]), tte.region_ptr(host_out[0]), max(rows, 1),
+                                             gate_w, up_w, down_w, seg_pos, seg_end, self.activation)
+                    tte.signal_region(host_in + host_out, s)
+                self.input_buffers_pool.release(self.input_buffer_index)
+                self.input_buffer = None
+                self.input_buffer_index = -1
+                await tte.async_send_metadata_to(
+                    self.host_address, P2PHeaders.HostOutputBufferUnlocked.value, [(len(host_task_name), host_task_name)])
+                return
+
+            # READ: only the rows this task packed.
             if self.metrics_collector is not None:
                 self.metrics_collector.record_transfer_start(task_id, "read", rows * in_buf.row_bytes)
             await in_buf.read_from(self.host_address, host_input_buffers_transfer_descs[host_in_id],

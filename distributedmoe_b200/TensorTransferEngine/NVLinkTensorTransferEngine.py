@@ -17,12 +17,14 @@ may share one GPU.
 
 from __future__ import annotations
 
+import asyncio
 import itertools
 import os
 import socket
 import struct
 import threading
 import timeit
+from collections import deque
 from dataclasses import dataclass
 from typing import Any, Dict, List, Optional, Tuple
 
@@ -35,6 +37,48 @@ from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import (
 )
 from distributedmoe_b200.TensorTransferEngine.utils import HandshakeType, Transfer, TransferStatus
 from distributedmoe_b200.utils.logging_config import get_logger
+
+# Engines of this process by their own name ("address:port"), for the in-process metadata channel.
+_ENGINES: Dict[str, "NVLinkTensorTransferEngine"] = {}
+_ENGINES_LOCK = threading.Lock()
+
+
+class _Inbox:
+    """Thread-safe FIFO of metadata packets from one in-process peer; the receiving coroutine
+    sleeps on a future of its own event loop and is woken with call_soon_threadsafe."""
+
+    def __init__(self) -> None:
+        self.lock = threading.Lock()
+        self.items: deque = deque()
+        self.waiter: Optional[asyncio.Future] = None
+
+    def put(self, packet: bytes) -> None:
+        with self.lock:
+            self.items.append(packet)
+            w, self.waiter = self.waiter, None
+        if w is not None:
+            w.get_loop().call_soon_threadsafe(_wake, w)
+
+    async def get(self, timeout_s: float) -> bytes:
+        while True:
+            with self.lock:
+                if self.items:
+                    return self.items.popleft()
+                fut = asyncio.get_running_loop().create_future()
+                self.waiter = fut
+            try:
+                await asyncio.wait_for(fut, timeout_s)
+            except asyncio.TimeoutError:
+                with self.lock:
+                    if self.waiter is fut:
+                        self.waiter = None
+                raise
+
+
+def _wake(fut: asyncio.Future) -> None:
+    if not fut.done():
+        fut.set_result(None)
+
 
 # Process-local registry of completion events, addressed by 8-byte tokens in descriptors.
 _EVENTS: Dict[int, torch.cuda.Event] = {}
@@ -71,6 +115,12 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self._local_regions: Dict[int, NVLinkRegion] = {}
         self._helpers: Dict[int, torch.cuda.Stream] = {}
         self._lock = threading.Lock()
+        # Peers in this process exchange metadata through in-memory inboxes instead of ZeroMQ
+        # once the handshake has shown that they share the process.
+        self._inproc: Dict[str, bool] = {}
+        self._inboxes: Dict[str, _Inbox] = {name: _Inbox() for name in self.remote_names}
+        with _ENGINES_LOCK:
+            _ENGINES[self.host_name] = self
         self._init_transfer_engine()
         assert self.handshake()
 
@@ -100,6 +150,11 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
             raw = body[-1][1]
             pid, dev = struct.unpack("!Ih", raw[:6])
             self.remote_info[remote_name] = (pid, dev, raw[6:].decode(errors="replace"))
+            if pid == self.pid:
+                with _ENGINES_LOCK:
+                    peer = _ENGINES.get(remote_name)
+                if peer is not None and self.host_name in peer._inboxes:
+                    self._inproc[remote_name] = True
             if pid == self.pid and dev >= 0 and torch.cuda.is_available():
                 here = torch.cuda.current_device()
                 if dev != here:
@@ -109,6 +164,22 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         except Exception as e:
             self.nv_logger.error(f"handshake with {remote_name} failed: {e}")
             return False
+
+    # ------------------------------------------------------------------ metadata channel
+    async def async_send_metadata_to(self, remote_name: str, header: int, body) -> None:
+        if self._inproc.get(remote_name):
+            with _ENGINES_LOCK:
+                peer = _ENGINES.get(remote_name)
+            if peer is not None and not peer.is_closed:
+                peer._inboxes[self.host_name].put(self.serialize_p2p_packet(header, body))
+                return
+        await super().async_send_metadata_to(remote_name, header, body)
+
+    async def async_get_metadata_from(self, remote_name: str):
+        if self._inproc.get(remote_name):
+            packet = await self._inboxes[remote_name].get(self.p2p_timeout_duration / 1000.0)
+            return self.deserialize_p2p_packet(packet)
+        return await super().async_get_metadata_from(remote_name)
 
     # ------------------------------------------------------------------ registration
     def register_batch(self, data_ptrs: List[Any], data_location: Optional[str], device_id: int,
@@ -168,6 +239,11 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
                 base = N.ipc_open(r.mem_handle, torch.cuda.current_device())
                 self._opened_mem[r.mem_handle] = base
         return base + r.mem_offset
+
+    def region_is_local(self, r: NVLinkRegion, device: int) -> bool:
+        """True when the region is memory of `device` mapped in this process (kernels on that
+        GPU can use it directly, with no transfer)."""
+        return r.pid == self.pid and r.device == device
 
     def region_event(self, r: NVLinkRegion) -> torch.cuda.Event:
         if r.pid == self.pid:
@@ -256,4 +332,7 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self._opened_mem.clear()
         self._opened_events.clear()
         self.deregister_batch(list(self._local_regions.values()))
+        with _ENGINES_LOCK:
+            if _ENGINES.get(self.host_name) is self:
+                del _ENGINES[self.host_name]
         super().close()

@@ -316,16 +316,26 @@ def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
                       seg_expert, seg_end, act: int, Y: torch.Tensor, m_rows: Optional[int] = None) -> None:
     """Grouped expert MLP over row segments.  seg_expert/seg_end: Python int sequences (host
     table) or int32 CUDA tensors (device table)."""
-    dev = _require_cuda(X, w_gate, w_up, w_down, Y)
+    _require_cuda(X, Y)
+    if X.shape[1] != w_gate.shape[2] or Y.shape[1] != w_gate.shape[2]:
+        raise DMoEError("X and Y must be [rows, d]")
+    if not (X.dtype == w_gate.dtype == Y.dtype):
+        raise DMoEError("grouped MLP operands must share one dtype")
+    grouped_gated_mlp_ptrs(X.data_ptr(), Y.data_ptr(), X.shape[0] if m_rows is None else m_rows, w_gate, w_up, w_down,
+                           seg_expert, seg_end, act)
+
+
+def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Tensor, w_up: torch.Tensor,
+                           w_down: torch.Tensor, seg_expert, seg_end, act: int) -> None:
+    """Same as :func:`grouped_gated_mlp` on raw device pointers (rows of d elements of the
+    weights' dtype), e.g. a transfer-engine buffer of another block on this GPU."""
+    dev = _require_cuda(w_gate, w_up, w_down)
     E, I, d = w_gate.shape
     if w_up.shape != (E, I, d) or w_down.shape != (E, d, I):
         raise DMoEError("expert stacks must be gate/up [E, I, d] and down [E, d, I]")
-    if X.shape[1] != d or Y.shape[1] != d:
-        raise DMoEError("X and Y must be [rows, d]")
-    if not (X.dtype == w_gate.dtype == w_up.dtype == w_down.dtype == Y.dtype):
+    if not (w_gate.dtype == w_up.dtype == w_down.dtype):
         raise DMoEError("grouped MLP operands must share one dtype")
-    m_rows = X.shape[0] if m_rows is None else m_rows
-    dt = dtype_code(X.dtype)
+    dt = dtype_code(w_gate.dtype)
     ws = scratch.get(dev, "mlp", lib().dmoe_grouped_mlp_workspace_size(m_rows, I, dt))
     if isinstance(seg_expert, torch.Tensor):
         n_seg = seg_expert.numel()
@@ -337,8 +347,8 @@ def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
         se, sn, on_dev = ctypes.addressof(a1), ctypes.addressof(a2), 0
         keep = (a1, a2)
     tm = _Timed("grouped_gated_mlp", _stream(dev), dev)
-    rc = lib().dmoe_grouped_gated_mlp(X.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
-                                      se, sn, n_seg, on_dev, m_rows, act, Y.data_ptr(), ws.data_ptr(), ws.numel(),
+    rc = lib().dmoe_grouped_gated_mlp(x_ptr, w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
+                                      se, sn, n_seg, on_dev, m_rows, act, y_ptr, ws.data_ptr(), ws.numel(),
                                       scratch.status(dev).data_ptr(), _stream(dev))
     del keep
     _check(rc, "dmoe_grouped_gated_mlp")

@@ -40,7 +40,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int kThreads = 192;
 constexpr int kMaxSegDev = 1024;
-constexpr int kMaxSegParam = 256;
+constexpr int kMaxSegParam = 512;  // host tables hold up to 256 segments; the pair/single split doubles that
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
 constexpr int kBarBytes = 256;
@@ -300,7 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int e = s_expert[i];
       int len = en - prev;
-      if (e < 0 || e >= segs.e_stack) {
+      if (e == -1) {  // rows another launch computes
+        len = 0;
+        s_expert[i] = 0;
+      } else if (e < 0 || e >= segs.e_stack) {
         bad = 1;
         len = 0;
         s_expert[i] = 0;
@@ -654,7 +657,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         en = en < prev ? prev : segs.m_rows;
       }
       int len = en - prev;
-      if (s_expert[i] < 0 || s_expert[i] >= segs.e_stack) {
+      if (s_expert[i] == -1) {  // rows another launch computes
+        len = 0;
+        s_expert[i] = 0;
+      } else if (s_expert[i] < 0 || s_expert[i] >= segs.e_stack) {
         bad = 1;
         len = 0;
         s_expert[i] = 0;
@@ -906,8 +912,31 @@ PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
+// Encoded maps are reused: weights and registered buffers keep their addresses across calls.
+struct MapCacheEntry {
+  const void* base;
+  int dt, rank;
+  uint64_t dims[3];
+  uint32_t box[3];
+  int dev;
+  CUtensorMap map;
+};
+constexpr int kMapCache = 64;
+
 // rank-2 or rank-3 row-major tensor; dims innermost first; box innermost first.
 int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_t* dims, const uint32_t* box) {
+  static thread_local MapCacheEntry cache[kMapCache];
+  static thread_local int cache_n = 0, cache_next = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (int i = 0; i < cache_n; ++i) {
+    const MapCacheEntry& c = cache[i];
+    if (c.base == base && c.dt == dt && c.rank == rank && c.dev == dev && c.dims[0] == dims[0] && c.box[0] == box[0] &&
+        c.dims[1] == dims[1] && c.box[1] == box[1] && (rank < 3 || (c.dims[2] == dims[2] && c.box[2] == box[2]))) {
+      *map = c.map;
+      return DMOE_OK;
+    }
+  }
   PFN_encodeTiled enc = get_encode_fn();
   DMOE_REQUIRE(enc != nullptr, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t gdim[3], gstride[2];
@@ -926,6 +955,18 @@ int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_
     set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
     return DMOE_ERR_CUDA;
   }
+  MapCacheEntry& c = cache[cache_next];
+  c.base = base;
+  c.dt = dt;
+  c.rank = rank;
+  c.dev = dev;
+  for (int i = 0; i < 3; ++i) {
+    c.dims[i] = i < rank ? dims[i] : 0;
+    c.box[i] = i < rank ? box[i] : 0;
+  }
+  c.map = *map;
+  cache_next = (cache_next + 1) % kMapCache;
+  if (cache_n < kMapCache) ++cache_n;
   return DMOE_OK;
 }
 
@@ -1052,22 +1093,69 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     const uint32_t box[3] = {BK, 128, 1};
     int r = make_map(&td2, DT, w_down, 3, dims, box);
     if (r) return r;
-    int p1 = -1, p2 = -1;
-    if (total_m_host >= 0) {  // total_m_host counts 128-row tiles; pair tiles are 256 rows
-      if (total_m_host == 0) return DMOE_OK;
-      int pair_m = 0, prev = 0;
-      for (int i = 0; i < segs.n_seg; ++i) {
-        pair_m += (segs.end[i] - prev + BM2 - 1) / BM2;
-        prev = segs.end[i];
-      }
-      p1 = pair_m * nt1;
-      p2 = pair_m * nt2;
-    }
     GemmArgs a1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
-    r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, p1, stream);
-    if (r) return r;
     GemmArgs a2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
-    return launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, p2, stream);
+    const char* hyb = getenv("DMOE_GEMM_HYBRID");
+    if (total_m_host < 0 || (hyb && strcmp(hyb, "0") == 0)) {  // device table (or hybrid off): pair tiles only
+      r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
+      if (r) return r;
+      return launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, -1, stream);
+    }
+    if (total_m_host == 0) return DMOE_OK;
+    // Host table: whole 256-row blocks (and remainders over 128 rows) go to the pair kernel; a
+    // remainder of at most 128 rows is one 128-row tile of the single-SM kernel instead of a
+    // mostly empty pair tile.  Rows a launch skips carry expert -1 in its table.
+    static thread_local GemmSegs pair_segs, rest_segs;
+    pair_segs.n_seg = rest_segs.n_seg = 0;
+    pair_segs.m_rows = rest_segs.m_rows = segs.m_rows;
+    pair_segs.e_stack = rest_segs.e_stack = segs.e_stack;
+    pair_segs.dev_expert = rest_segs.dev_expert = nullptr;
+    pair_segs.dev_end = rest_segs.dev_end = nullptr;
+    int pair_m = 0, rest_m = 0, prev = 0;
+    auto push = [](GemmSegs& g, int e, int end) {
+      g.expert[g.n_seg] = e;
+      g.end[g.n_seg] = end;
+      ++g.n_seg;
+    };
+    for (int i = 0; i < segs.n_seg; ++i) {
+      const int len = segs.end[i] - prev;
+      int full = (len / BM2) * BM2;
+      if (len - full > 128) full = len;
+      const int rem = len - full;
+      if (full > 0) {
+        push(pair_segs, segs.expert[i], prev + full);
+        pair_m += (full + BM2 - 1) / BM2;
+      }
+      if (rem > 0) {
+        push(pair_segs, -1, segs.end[i]);
+        if (full > 0) push(rest_segs, -1, prev + full);
+        push(rest_segs, segs.expert[i], segs.end[i]);
+        rest_m += 1;
+      } else {
+        push(rest_segs, -1, segs.end[i]);
+      }
+      prev = segs.end[i];
+    }
+    if (pair_m > 0) {
+      r = launch_gemm_2sm<true, DT>(ta, tg, tu, pair_segs, a1, pair_m * nt1, stream);
+      if (r) return r;
+    }
+    const int sms1 = sm_count();
+    if (rest_m > 0) {
+      const int64_t t1 = (int64_t)rest_m * nt1;
+      r = launch_gemm<true, DT>(ta, tg, tu, rest_segs, a1, (int)(t1 < sms1 ? t1 : sms1), stream);
+      if (r) return r;
+    }
+    if (pair_m > 0) {
+      r = launch_gemm_2sm<false, DT>(th, td2, td2, pair_segs, a2, pair_m * nt2, stream);
+      if (r) return r;
+    }
+    if (rest_m > 0) {
+      const int64_t t2 = (int64_t)rest_m * nt2;
+      r = launch_gemm<false, DT>(th, td, td, rest_segs, a2, (int)(t2 < sms1 ? t2 : sms1), stream);
+      if (r) return r;
+    }
+    return DMOE_OK;
   }
   const int sms = sm_count();
   int g1 = sms, g2 = sms;
@@ -1125,8 +1213,7 @@ extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const v
     segs.dev_expert = seg_expert;
     segs.dev_end = seg_end;
   } else {
-    DMOE_REQUIRE(n_seg <= kMaxSegParam, "dmoe_grouped_gated_mlp: n_seg=%d > %d for host segment tables", n_seg,
-                 kMaxSegParam);
+    DMOE_REQUIRE(n_seg <= 256, "dmoe_grouped_gated_mlp: n_seg=%d > 256 for host segment tables", n_seg);
     segs.dev_expert = nullptr;
     segs.dev_end = nullptr;
     int prev = 0;

@@ -210,6 +210,9 @@ def _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act):
     (4, 256, 384, [1, 127, 128, 129, 0, 300]),
     (8, 200, 320, [5, 0, 260, 64]),          # K tail (200 % 64), N tails (I=320, d=200)
     (3, 512, 256, [1000]),
+    # segments averaging >= 128 rows take the pair (2-SM) kernel; remainders of <= 128 rows
+    # go to the single-SM kernel
+    (6, 256, 384, [1030, 1000, 300, 129, 0, 256, 511, 385]),
 ])
 def test_grouped_mlp_matches_fp32_reference(dtype, act, E, d, I, sizes):
     N = _nat()
