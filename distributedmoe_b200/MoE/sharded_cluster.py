@@ -1,0 +1,123 @@
+"""Expert-parallel MoE layer over the GPUs of one node, one process per GPU.
+
+Every rank g owns the experts ``[g*E/G, (g+1)*E/G)`` (its stacked weights) and runs:
+
+* one host ``DistMoEBlock`` for its own tokens, whose ``expert_blocks`` list has one block
+  per rank (block b = the experts of rank b), and
+* G ``DistExpertsBlock`` threads, block g of every rank's host, all sharing this rank's
+  weights.
+
+So there are G x G expert-block objects in total, and no single host GPU funnels all
+traffic (a star with one host would be bound by that GPU's NVLink egress).  Hosts
+and blocks talk through the NVLink transfer engine: metadata over ZeroMQ between
+processes, activations over NVLink through CUDA-IPC peer buffers (completion notices
+order the accesses).  ``torch.distributed`` (any backend) is used once, to exchange the
+ports of all engines, plus barriers at set-up and shut-down; the data path has no
+collective.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from distributedmoe_b200.MoE.DistExpertsBlock import DistExpertsBlock
+from distributedmoe_b200.MoE.DistMoEBlock import DistMoEBlock, DistMoEBlockConfig
+from distributedmoe_b200.MoE.local_cluster import free_ports
+from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import (
+    TensorTransferEngineBackend,
+    TensorTransferEngineConfig,
+)
+from distributedmoe_b200.TensorTransferEngine.utils import HandshakeType, TransferProtocol
+
+
+def experts_of_rank(number_of_experts: int, world: int, rank: int) -> List[int]:
+    per = number_of_experts // world
+    return list(range(rank * per, (rank + 1) * per))
+
+
+class ShardedCluster:
+    """``with ShardedCluster(...) as moe: y = moe(x_local)`` on every rank.
+
+    stacked: this rank's (gate [E_g, I, d], up [E_g, I, d], down [E_g, d, I]) on its GPU."""
+
+    def __init__(self, number_of_experts: int, top_k: int, hidden_features: int, dtype: torch.dtype,
+                 device: torch.device, stacked, group: Optional[dist.ProcessGroup] = None,
+                 io_buffer_size: int = 8192, number_of_io_buffers: int = 2, forward_timeout: int = 60000,
+                 p2p_timeout_ms: int = 3000, address: str = "127.0.0.1", **options):
+        G = dist.get_world_size(group)
+        r = dist.get_rank(group)
+        if number_of_experts % G:
+            raise ValueError("number_of_experts must divide evenly over the ranks")
+        self.group = group
+        self.rank, self.world = r, G
+        device = torch.device(device)
+        p = free_ports(1 + 5 * G)
+        mine = {"host_port": p[0], "host_p2p": p[1:1 + G], "host_hc": p[1 + G:1 + 2 * G],
+                "eb_port": p[1 + 2 * G:1 + 3 * G], "eb_p2p": p[1 + 3 * G:1 + 4 * G], "eb_hc": p[1 + 4 * G:1 + 5 * G],
+                "address": address, "device": device.index}
+        table: List[dict] = [None] * G  # type: ignore[list-item]
+        dist.all_gather_object(table, mine, group=group)
+        blocks = [experts_of_rank(number_of_experts, G, g) for g in range(G)]
+        eb_devices = [torch.device("cuda", table[g]["device"]) for g in range(G)]
+
+        def config_of_host(h: int) -> DistMoEBlockConfig:
+            # host h's view: block g lives on rank g and uses the ports rank g opened for host h
+            return DistMoEBlockConfig(
+                backend=TensorTransferEngineBackend.NVLinkIPC, number_of_experts=number_of_experts,
+                expert_blocks=blocks, number_of_io_buffers=number_of_io_buffers, io_buffer_size=io_buffer_size,
+                top_k=top_k, hidden_features=hidden_features, dtype=dtype, moe_device=eb_devices[h],
+                eb_devices=eb_devices, forward_timeout=forward_timeout,
+                host_health_check_ports=list(table[h]["host_hc"]),
+                remote_health_check_ports=[table[g]["eb_hc"][h] for g in range(G)], **options)
+
+        self.errors: List[BaseException] = []
+        self.threads: List[threading.Thread] = []
+        for h in range(G):
+            cfg = config_of_host(h)
+            eb_tte = TensorTransferEngineConfig(
+                host_address=address, host_port=mine["eb_port"][h], host_p2p_ports=[mine["eb_p2p"][h]],
+                remote_addresses=[table[h]["address"]], remote_ports=[table[h]["host_port"]],
+                remote_p2p_ports=[table[h]["host_p2p"][r]], p2p_timeout_duration=p2p_timeout_ms,
+                handshake_type=HandshakeType.CLIENT, transfer_protocol=TransferProtocol.NVLINK, ib_device_names="")
+
+            def job(cfg=cfg, eb_tte=eb_tte):
+                try:
+                    torch.cuda.set_device(device)
+                    blk = DistExpertsBlock(r, cfg, [], eb_tte, None, stacked_weights=stacked)
+                    blk.main_loop()
+                except BaseException as e:  # surfaced by close()
+                    self.errors.append(e)
+
+            t = threading.Thread(target=job, daemon=True, name=f"experts-block-{r}-for-host-{h}")
+            t.start()
+            self.threads.append(t)
+
+        host_tte = TensorTransferEngineConfig(
+            host_address=address, host_port=mine["host_port"], host_p2p_ports=list(mine["host_p2p"]),
+            remote_addresses=[table[g]["address"] for g in range(G)],
+            remote_ports=[table[g]["eb_port"][r] for g in range(G)],
+            remote_p2p_ports=[table[g]["eb_p2p"][r] for g in range(G)], p2p_timeout_duration=p2p_timeout_ms,
+            handshake_type=HandshakeType.SERVER, transfer_protocol=TransferProtocol.NVLINK, ib_device_names="")
+        with torch.cuda.device(device):
+            self.moe = DistMoEBlock(config_of_host(r), host_tte)
+        dist.barrier(group=group)  # every host and block of every rank is up before the first forward
+
+    def __enter__(self) -> DistMoEBlock:
+        return self.moe
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def close(self) -> None:
+        # Stop this rank's host (which stops its G blocks on all ranks), then wait until every
+        # host has done the same before joining this rank's blocks.
+        self.moe.close()
+        dist.barrier(group=self.group)
+        for t in self.threads:
+            t.join(timeout=30.0)
+        if self.errors:
+            raise RuntimeError(f"an expert block failed: {self.errors[0]!r}") from self.errors[0]

@@ -10,9 +10,14 @@ NVSwitch (or within HBM when both regions are on one GPU), and record both event
 Consumers order themselves after a region with :meth:`wait_region` instead of a host round
 trip; :meth:`wait_for_transfer_efficient` still works for callers that want a host wait.
 
-Completion events are CUDA events, shared through a process-local registry or as CUDA IPC
-event handles across processes.  No kernel spins on a flag here, so host and expert block
-may share one GPU.
+Completion events are raw CUDA events of the library (``dmoe_event_*``), shared through a
+process-local registry or as CUDA IPC event handles across processes.  Only the owner of a
+region records its event.  A process that touched another process's region records an
+interprocess event of its own on that stream and sends the owner a completion notice ahead
+of its next message; the owner then orders the region's event after it.  An interprocess
+event is only waited on by streams of the GPU it belongs to: other GPUs go through a helper
+stream on that GPU.  No kernel spins on a flag here, so host and expert block may share one
+GPU.
 """
 
 from __future__ import annotations
@@ -80,12 +85,16 @@ def _wake(fut: asyncio.Future) -> None:
         fut.set_result(None)
 
 
-# Process-local registry of completion events, addressed by 8-byte tokens in descriptors.
-_EVENTS: Dict[int, torch.cuda.Event] = {}
+# Process-local registry of region events (raw interprocess CUDA events), addressed by
+# 8-byte tokens in descriptors.
+_EVENTS: Dict[int, int] = {}
 _EVENTS_LOCK = threading.Lock()
 _TOKENS = itertools.count(1)
 
 _DESC = struct.Struct("!IhQQ64sQQ64s")  # pid, device, ptr, size, mem handle, offset, event token, event handle
+
+# Metadata header of a completion notice (outside the pipeline's 1000-1999 range).
+NOTICE_HEADER = 4738
 
 
 @dataclass
@@ -111,10 +120,21 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self.pid = os.getpid()
         self.remote_info: Dict[str, Tuple[int, int, str]] = {}
         self._opened_mem: Dict[bytes, int] = {}       # mem handle -> mapped base (other processes)
-        self._opened_events: Dict[bytes, torch.cuda.Event] = {}
+        self._opened_events: Dict[Tuple[bytes, int], int] = {}  # (IPC event handle, device) -> event
         self._local_regions: Dict[int, NVLinkRegion] = {}
         self._helpers: Dict[int, torch.cuda.Stream] = {}
         self._lock = threading.Lock()
+        # Local (not interprocess) events of each GPU for hand-offs between streams; one is
+        # recorded and waited on as one step under _tmp_lock.
+        self._tmp_events: Dict[int, int] = {}
+        self._tmp_lock = threading.Lock()
+        # Notice events: one interprocess event per stream that touched another process's
+        # region, with its exported handle.  Re-recording it on the same stream only makes a
+        # late waiter wait longer.
+        self._notice_events: Dict[int, Tuple[int, int, bytes]] = {}  # stream -> (device, event, handle)
+        self._pending_notice: Dict[str, Dict[int, set]] = {}  # owner -> stream -> region tokens
+        self._region_owner: Dict[int, str] = {}
+        self._notice_outbox: Dict[str, deque] = {}
         # Peers in this process exchange metadata through in-memory inboxes instead of ZeroMQ
         # once the handshake has shown that they share the process.
         self._inproc: Dict[str, bool] = {}
@@ -167,19 +187,34 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
 
     # ------------------------------------------------------------------ metadata channel
     async def async_send_metadata_to(self, remote_name: str, header: int, body) -> None:
+        # Notices go first and stay queued until sent, so a send that times out and is
+        # retried still delivers them ahead of the message.
+        outbox = self._notice_outbox.setdefault(remote_name, deque())
+        outbox.extend(self._take_notices(remote_name))
+        while outbox:
+            await self._send_packet(remote_name, outbox[0])
+            outbox.popleft()
+        await self._send_packet(remote_name, self.serialize_p2p_packet(header, body))
+
+    async def _send_packet(self, remote_name: str, packet: bytes) -> None:
         if self._inproc.get(remote_name):
             with _ENGINES_LOCK:
                 peer = _ENGINES.get(remote_name)
             if peer is not None and not peer.is_closed:
-                peer._inboxes[self.host_name].put(self.serialize_p2p_packet(header, body))
+                peer._inboxes[self.host_name].put(packet)
                 return
-        await super().async_send_metadata_to(remote_name, header, body)
+        await self.async_send_packet_to(remote_name, packet)
 
     async def async_get_metadata_from(self, remote_name: str):
-        if self._inproc.get(remote_name):
-            packet = await self._inboxes[remote_name].get(self.p2p_timeout_duration / 1000.0)
-            return self.deserialize_p2p_packet(packet)
-        return await super().async_get_metadata_from(remote_name)
+        while True:
+            if self._inproc.get(remote_name):
+                packet = await self._inboxes[remote_name].get(self.p2p_timeout_duration / 1000.0)
+                header, body = self.deserialize_p2p_packet(packet)
+            else:
+                header, body = await super().async_get_metadata_from(remote_name)
+            if header != NOTICE_HEADER:
+                return header, body
+            self._apply_notice(body)
 
     # ------------------------------------------------------------------ registration
     def register_batch(self, data_ptrs: List[Any], data_location: Optional[str], device_id: int,
@@ -196,13 +231,12 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
                 size = int(data_sizes[i])
             with torch.cuda.device(dev):
                 mem_handle, mem_offset = N.ipc_export(ptr)
-                ev = torch.cuda.Event(interprocess=True)
-                ev.record(torch.cuda.current_stream(dev))  # a recorded event: waits on it return at once
-                ev_handle = ev.ipc_handle()
+            ev = N.event_create(dev, interprocess=True)  # not recorded yet: waits on it return at once
+            ev_handle = N.ipc_event_export(ev)
             token = next(_TOKENS)
             with _EVENTS_LOCK:
                 _EVENTS[token] = ev
-            r = NVLinkRegion(self.pid, dev, ptr, size, mem_handle, mem_offset, token, bytes(ev_handle))
+            r = NVLinkRegion(self.pid, dev, ptr, size, mem_handle, mem_offset, token, ev_handle)
             self._local_regions[token] = r
             regions.append(r)
         return regions, regions
@@ -211,7 +245,12 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         for r in data_registration_descs:
             self._local_regions.pop(r.event_token, None)
             with _EVENTS_LOCK:
-                _EVENTS.pop(r.event_token, None)
+                ev = _EVENTS.pop(r.event_token, None)
+            if ev is not None:
+                try:
+                    N.event_destroy(ev)
+                except Exception as e:  # pragma: no cover - best effort at shutdown
+                    self.nv_logger.warning(f"destroying a region event failed: {e}")
 
     def serialize_descs(self, data_descs: List[NVLinkRegion]) -> Tuple[int, bytes]:
         blob = struct.pack("!H", len(data_descs)) + b"".join(
@@ -245,22 +284,42 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         GPU can use it directly, with no transfer)."""
         return r.pid == self.pid and r.device == device
 
-    def region_event(self, r: NVLinkRegion) -> torch.cuda.Event:
+    def region_event(self, r: NVLinkRegion) -> int:
+        """The region's last-access event: the registry entry for this process's regions, the
+        owner's event opened once (on the owner's GPU) for another process's."""
         if r.pid == self.pid:
             with _EVENTS_LOCK:
                 return _EVENTS[r.event_token]
+        return self._open_event(r.event_handle, r.device)
+
+    def _open_event(self, handle: bytes, device: int) -> int:
+        key = (bytes(handle), device)
         with self._lock:
-            ev = self._opened_events.get(r.event_handle)
+            ev = self._opened_events.get(key)
             if ev is None:
-                ev = torch.cuda.Event.from_ipc_handle(r.device, r.event_handle)
-                self._opened_events[r.event_handle] = ev
+                ev = N.ipc_event_open(handle, device)
+                self._opened_events[key] = ev
         return ev
 
     def wait_region(self, regions: List[NVLinkRegion], stream: Optional[torch.cuda.Stream] = None) -> None:
         """Order `stream` after the last completion recorded for each region."""
         stream = stream or torch.cuda.current_stream()
         for r in regions:
-            stream.wait_event(self.region_event(r))
+            self._wait_event_of(stream, self.region_event(r), r.device)
+
+    def _wait_event_of(self, stream: torch.cuda.Stream, ev: int, ev_device: int) -> None:
+        """Order `stream` after interprocess event `ev` of GPU `ev_device`.  Such an event is
+        waited on only by a stream of its own GPU: for a stream elsewhere a helper stream on
+        that GPU waits for it and hands over through a local event."""
+        if stream.device.index == ev_device:
+            N.stream_wait_event(stream.cuda_stream, ev)
+            return
+        h = self._helper_stream(ev_device)
+        with self._tmp_lock:
+            tmp = self._tmp_event(ev_device)
+            N.stream_wait_event(h.cuda_stream, ev)
+            N.event_record(tmp, h.cuda_stream)
+            N.stream_wait_event(stream.cuda_stream, tmp)
 
     def _helper_stream(self, device: int) -> torch.cuda.Stream:
         with self._lock:
@@ -270,24 +329,94 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
                 self._helpers[device] = h
         return h
 
+    def _tmp_event(self, device: int) -> int:
+        with self._lock:
+            ev = self._tmp_events.get(device)
+            if ev is None:
+                ev = N.event_create(device)
+                self._tmp_events[device] = ev
+        return ev
+
     def signal_region(self, regions: List[NVLinkRegion], stream: Optional[torch.cuda.Stream] = None) -> None:
-        """Record the work issued so far on `stream` as the regions' last access.  A CUDA
-        event can only be recorded on its own device, so a region of another GPU is
-        signalled through a helper stream on that GPU that waits for `stream`."""
+        """Record the work issued so far on `stream` as the regions' last access.  An event is
+        recorded on a stream of its own GPU, so a region of another GPU is signalled through
+        a helper stream there that waits for `stream`.  Regions of other processes get a
+        completion notice instead."""
         stream = stream or torch.cuda.current_stream()
         here = stream.device.index
-        tmp = None
+        foreign = [r for r in regions if r.pid != self.pid]
+        if foreign:
+            self._note_foreign(foreign, stream)
         for r in regions:
+            if r.pid != self.pid:
+                continue
             ev = self.region_event(r)
             if r.device == here:
-                ev.record(stream)
+                N.event_record(ev, stream.cuda_stream)
                 continue
-            if tmp is None:
-                tmp = torch.cuda.Event()
-                tmp.record(stream)
             h = self._helper_stream(r.device)
-            h.wait_event(tmp)
-            ev.record(h)
+            with self._tmp_lock:
+                tmp = self._tmp_event(here)
+                N.event_record(tmp, stream.cuda_stream)
+                N.stream_wait_event(h.cuda_stream, tmp)
+            N.event_record(ev, h.cuda_stream)
+
+    # ------------------------------------------------------------------ cross-process ordering
+    def _note_foreign(self, regions: List[NVLinkRegion], stream: torch.cuda.Stream) -> None:
+        """Record this stream's notice event after its work so far and remember, per owner,
+        which of the owner's regions the work touched; the notice goes out ahead of the next
+        message to that owner."""
+        key = stream.cuda_stream
+        with self._lock:
+            entry = self._notice_events.get(key)
+            if entry is None:
+                dev = stream.device.index
+                ev = N.event_create(dev, interprocess=True)
+                entry = (dev, ev, N.ipc_event_export(ev))
+                self._notice_events[key] = entry
+            N.event_record(entry[1], key)
+            for r in regions:
+                owner = self._owner_name(r)
+                if owner is None:
+                    raise RuntimeError(f"no peer of this engine owns the region of pid {r.pid}")
+                self._pending_notice.setdefault(owner, {}).setdefault(key, set()).add(r.event_token)
+
+    def _owner_name(self, r: NVLinkRegion) -> Optional[str]:
+        name = self._region_owner.get(r.event_token)
+        if name is not None:
+            return name
+        for remote, (pid, _dev, _host) in self.remote_info.items():
+            if pid == r.pid:
+                self._region_owner[r.event_token] = remote
+                return remote
+        return None
+
+    def _take_notices(self, remote_name: str) -> List[bytes]:
+        with self._lock:
+            pending = self._pending_notice.pop(remote_name, None)
+            if not pending:
+                return []
+            out = []
+            for key, tokens in pending.items():
+                dev, _ev, handle = self._notice_events[key]
+                body = [(2, struct.pack("!h", dev)), (len(handle), handle)] + \
+                       [(8, struct.pack("!Q", t)) for t in sorted(tokens)]
+                out.append(self.serialize_p2p_packet(NOTICE_HEADER, body))
+        return out
+
+    def _apply_notice(self, body) -> None:
+        """Order the named regions' next users after the sender's work: a helper stream on
+        each region's GPU waits for the sender's event, then records the region's event."""
+        (dev,) = struct.unpack("!h", body[0][1])
+        ev = self._open_event(body[1][1], dev)
+        for _, raw in body[2:]:
+            (token,) = struct.unpack("!Q", raw)
+            r = self._local_regions.get(token)
+            if r is None:
+                continue
+            h = self._helper_stream(r.device)
+            self._wait_event_of(h, ev, dev)
+            N.event_record(self.region_event(r), h.cuda_stream)
 
     # ------------------------------------------------------------------ transfers
     def _transfer(self, remote_name: str, transfer_name: bytes, src: List[NVLinkRegion], dst: List[NVLinkRegion],
@@ -319,7 +448,7 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self._transfer(remote_name, transfer_name, src_data_transfer_descs, dst_data_transfer_descs, src_data_sizes)
 
     def _check_handler_status(self, transfer: Transfer) -> bool:
-        return bool(transfer.handler.query())
+        return bool(transfer.handler.query())  # a local torch event of the copy stream
 
     def close(self) -> None:
         if self.is_closed:
@@ -330,7 +459,16 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
             except Exception as e:  # pragma: no cover - best effort at shutdown
                 self.nv_logger.warning(f"closing an IPC mapping failed: {e}")
         self._opened_mem.clear()
+        events = list(self._opened_events.values()) + list(self._tmp_events.values()) + \
+            [e[1] for e in self._notice_events.values()]
+        for ev in events:
+            try:
+                N.event_destroy(ev)
+            except Exception:  # pragma: no cover - best effort at shutdown
+                pass
         self._opened_events.clear()
+        self._tmp_events.clear()
+        self._notice_events.clear()
         self.deregister_batch(list(self._local_regions.values()))
         with _ENGINES_LOCK:
             if _ENGINES.get(self.host_name) is self:

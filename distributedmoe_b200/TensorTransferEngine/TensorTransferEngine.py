@@ -198,8 +198,11 @@ class TensorTransferEngine(ABC):
         return header, body
 
     async def async_send_metadata_to(self, remote_name: str, header: int, body) -> None:
+        await self.async_send_packet_to(remote_name, self.serialize_p2p_packet(header, body))
+
+    async def async_send_packet_to(self, remote_name: str, packet: bytes) -> None:
         try:
-            await asyncio.wait_for(self.metadata_p2p_pairs[remote_name].pusher.send(self.serialize_p2p_packet(header, body)),
+            await asyncio.wait_for(self.metadata_p2p_pairs[remote_name].pusher.send(packet),
                                    self.p2p_timeout_duration / 1000.0)
         except zmq.Again:
             raise asyncio.TimeoutError()

@@ -67,6 +67,13 @@ SIGNATURES = {
     "dmoe_copy": (ctypes.c_int, [_vp, _vp, _sz, _vp]),
     "dmoe_flag_signal": (ctypes.c_int, [_vp, _u64, _vp]),
     "dmoe_flag_wait": (ctypes.c_int, [_vp, _u64, _u64, _vp, _vp]),
+    "dmoe_event_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "dmoe_event_destroy": (ctypes.c_int, [_vp]),
+    "dmoe_event_record": (ctypes.c_int, [_vp, _vp]),
+    "dmoe_event_query": (ctypes.c_int, [_vp]),
+    "dmoe_stream_wait_event": (ctypes.c_int, [_vp, _vp]),
+    "dmoe_ipc_event_export": (ctypes.c_int, [_vp, _vp]),
+    "dmoe_ipc_event_open": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp)]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -394,6 +401,53 @@ def ipc_close(ptr: int) -> None:
 
 def enable_peer_access(device: int, peer: int) -> None:
     _check(lib().dmoe_enable_peer_access(device, peer), "dmoe_enable_peer_access")
+
+
+DMOE_NOT_READY = 4
+
+
+def event_create(device: int, interprocess: bool = False) -> int:
+    """A raw CUDA event (timing disabled) of `device`; returns its handle as an int."""
+    out = _vp()
+    _check(lib().dmoe_event_create(device, int(interprocess), ctypes.byref(out)), "dmoe_event_create")
+    return int(out.value)
+
+
+def event_destroy(event: int) -> None:
+    _check(lib().dmoe_event_destroy(event), "dmoe_event_destroy")
+
+
+def event_record(event: int, stream: int) -> None:
+    _check(lib().dmoe_event_record(event, stream), "dmoe_event_record")
+
+
+def event_query(event: int) -> bool:
+    """True when the work before the event's last record has finished."""
+    rc = lib().dmoe_event_query(event)
+    if rc == DMOE_NOT_READY:
+        return False
+    _check(rc, "dmoe_event_query")
+    return True
+
+
+def stream_wait_event(stream: int, event: int) -> None:
+    _check(lib().dmoe_stream_wait_event(stream, event), "dmoe_stream_wait_event")
+
+
+def ipc_event_export(event: int) -> bytes:
+    buf = (ctypes.c_uint8 * 64)()
+    _check(lib().dmoe_ipc_event_export(event, buf), "dmoe_ipc_event_export")
+    return bytes(buf)
+
+
+def ipc_event_open(handle: bytes, device: int) -> int:
+    """Open another process's event in the context of `device` (the GPU it is recorded on)."""
+    if len(handle) != 64:
+        raise DMoEError("an IPC event handle is 64 bytes")
+    buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+    out = _vp()
+    _check(lib().dmoe_ipc_event_open(buf, device, ctypes.byref(out)), "dmoe_ipc_event_open")
+    return int(out.value)
 
 
 def copy_bytes(dst_ptr: int, src_ptr: int, nbytes: int, stream: int) -> None:

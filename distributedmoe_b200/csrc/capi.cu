@@ -136,6 +136,82 @@ int dmoe_copy(void* dst, const void* src, size_t bytes, void* stream) {
   return DMOE_OK;
 }
 
+// Raw CUDA events for the transfer engine's cross-process ordering.  An event created with
+// interprocess != 0 can be exported; an imported event is opened in the context of the GPU
+// that recorded it, and is only waited on by streams of that GPU.
+int dmoe_event_create(int device, int interprocess, void** event_out) {
+  DMOE_REQUIRE(event_out != nullptr, "dmoe_event_create: null pointer");
+  int prev = 0;
+  DMOE_CUDA(cudaGetDevice(&prev));
+  DMOE_CUDA(cudaSetDevice(device));
+  cudaEvent_t ev = nullptr;
+  cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming | (interprocess ? cudaEventInterprocess : 0));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    set_error("cudaEventCreateWithFlags failed: %s", cudaGetErrorString(e));
+    return DMOE_ERR_CUDA;
+  }
+  *event_out = ev;
+  return DMOE_OK;
+}
+
+int dmoe_event_destroy(void* event) {
+  if (event == nullptr) return DMOE_OK;
+  DMOE_CUDA(cudaEventDestroy(reinterpret_cast<cudaEvent_t>(event)));
+  return DMOE_OK;
+}
+
+int dmoe_event_record(void* event, void* stream) {
+  DMOE_REQUIRE(event != nullptr, "dmoe_event_record: null event");
+  DMOE_CUDA(cudaEventRecord(reinterpret_cast<cudaEvent_t>(event), as_stream(stream)));
+  return DMOE_OK;
+}
+
+int dmoe_event_query(void* event) {
+  DMOE_REQUIRE(event != nullptr, "dmoe_event_query: null event");
+  cudaError_t e = cudaEventQuery(reinterpret_cast<cudaEvent_t>(event));
+  if (e == cudaSuccess) return DMOE_OK;
+  if (e == cudaErrorNotReady) {
+    cudaGetLastError();
+    return DMOE_NOT_READY;
+  }
+  set_error("cudaEventQuery failed: %s", cudaGetErrorString(e));
+  return DMOE_ERR_CUDA;
+}
+
+int dmoe_stream_wait_event(void* stream, void* event) {
+  DMOE_REQUIRE(event != nullptr, "dmoe_stream_wait_event: null event");
+  DMOE_CUDA(cudaStreamWaitEvent(as_stream(stream), reinterpret_cast<cudaEvent_t>(event), 0));
+  return DMOE_OK;
+}
+
+int dmoe_ipc_event_export(void* event, uint8_t* handle_out64) {
+  DMOE_REQUIRE(event != nullptr && handle_out64 != nullptr, "dmoe_ipc_event_export: null pointer");
+  cudaIpcEventHandle_t h;
+  static_assert(sizeof(h) == 64, "cudaIpcEventHandle_t is 64 bytes");
+  DMOE_CUDA(cudaIpcGetEventHandle(&h, reinterpret_cast<cudaEvent_t>(event)));
+  memcpy(handle_out64, &h, 64);
+  return DMOE_OK;
+}
+
+int dmoe_ipc_event_open(const uint8_t* handle64, int device, void** event_out) {
+  DMOE_REQUIRE(handle64 != nullptr && event_out != nullptr, "dmoe_ipc_event_open: null pointer");
+  int prev = 0;
+  DMOE_CUDA(cudaGetDevice(&prev));
+  DMOE_CUDA(cudaSetDevice(device));
+  cudaIpcEventHandle_t h;
+  memcpy(&h, handle64, 64);
+  cudaEvent_t ev = nullptr;
+  cudaError_t e = cudaIpcOpenEventHandle(&ev, h);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    set_error("cudaIpcOpenEventHandle failed: %s", cudaGetErrorString(e));
+    return DMOE_ERR_CUDA;
+  }
+  *event_out = ev;
+  return DMOE_OK;
+}
+
 int dmoe_flag_signal(uint64_t* flag, uint64_t value, void* stream) {
   DMOE_REQUIRE(flag != nullptr && (reinterpret_cast<uintptr_t>(flag) & 7u) == 0, "dmoe_flag_signal: bad flag");
   flag_signal_kernel<<<1, 1, 0, as_stream(stream)>>>(flag, value);

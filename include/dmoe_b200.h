@@ -32,6 +32,7 @@ extern "C" {
 #define DMOE_ERR_INVALID 1     /* bad argument, shape or alignment */
 #define DMOE_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
 #define DMOE_ERR_UNSUPPORTED 3 /* valid request this build does not implement */
+#define DMOE_NOT_READY 4       /* dmoe_event_query: work before the event is still pending */
 
 #define DMOE_F32 0
 #define DMOE_F16 1
@@ -185,6 +186,23 @@ int dmoe_enable_peer_access(int device, int peer_device);
  * NIXL READ/WRITE of Buffer.read_from / write_to (MoE/pools/BuffersPool.py:55-90).
  */
 int dmoe_copy(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
+ * Raw CUDA events for stream-ordered completion (replace the transfer handles that the
+ * completion monitor polls, TensorTransferEngine/TensorTransferEngine.py:305-344, and the
+ * NIXL/MoonCake transfer-state queries, NIXLTensorTransferEngine.py:251-262).  Events have
+ * timing disabled; interprocess != 0 makes them exportable.  dmoe_event_query returns
+ * DMOE_OK when the work before the last record is done and DMOE_NOT_READY otherwise.
+ * dmoe_ipc_event_open opens another process's event in the context of `device`, which must
+ * be the GPU the exporter records it on; only streams of that GPU wait on the result.
+ */
+int dmoe_event_create(int device, int interprocess, void** event_out);
+int dmoe_event_destroy(void* event);
+int dmoe_event_record(void* event, void* stream);
+int dmoe_event_query(void* event);
+int dmoe_stream_wait_event(void* stream, void* event);
+int dmoe_ipc_event_export(void* event, uint8_t* handle_out64);
+int dmoe_ipc_event_open(const uint8_t* handle64, int device, void** event_out);
 
 /*
  * Completion flags (replace the transfer-monitor poll, TensorTransferEngine.py:305-344).
