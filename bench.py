@@ -19,9 +19,13 @@ holding the 8 experts on the same GPU, connected through the NVLink/CUDA-IPC tra
 * ``cpu_baseline``: the oracle port of the reference's torch path (routing +
   ``local_experts``), timed on this host's cores on a bounded token sample.
 
-With N GPUs each rank runs its own layer replica (weak scaling; the layer does not
-exchange data between ranks in this workload).  The expert weights (2.8 GB) exceed L2, so
-every step streams them from HBM.
+With N GPUs (``--parallel experts``, the default for N > 1) the experts are sharded: GPU g
+holds experts [g*8/N, (g+1)*8/N), every rank hosts its own 4096 tokens, and every host
+sends each token to the GPUs of its two experts and combines the results (one
+``DistMoEBlock`` per rank whose expert blocks span all N GPUs; activations cross NVLink
+through the CUDA-IPC transfer engine).  Per-GPU work stays fixed as N grows (weak scaling).
+``--parallel replicas`` runs an independent single-GPU layer per rank instead.  The expert
+weights (2.8 GB in all) exceed L2, so every step streams them from HBM.
 """
 
 from __future__ import annotations
@@ -55,12 +59,19 @@ def _peaks():
         return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def _config(n_gpus):
-    return {"workload": WORKLOAD, "tokens": T_TOK, "hidden": D, "experts": E, "top_k": K, "inner": I,
+def _config(n_gpus, parallel="single", io_buffers=2):
+    if parallel == "experts":
+        par = f"ep{n_gpus}: {E // n_gpus} experts per GPU, one host per GPU with {T_TOK} tokens"
+    elif parallel == "replicas":
+        par = f"replicas x{n_gpus}"
+    else:
+        par = "single gpu"
+    return {"workload": WORKLOAD, "tokens_per_gpu": T_TOK, "hidden": D, "experts": E, "top_k": K, "inner": I,
             "router": "softmax top-2 renormalised, fp32 logits", "activation": "silu (SwiGLU)",
-            "expert_blocks": 1, "io_buffer_size": 8192, "transfer_engine": "NVLinkIPC",
+            "expert_blocks": n_gpus if parallel == "experts" else 1, "io_buffer_size": 8192,
+            "io_buffers": io_buffers, "transfer_engine": "NVLinkIPC",
             "l2": "no flush: the 2.8 GB of expert weights exceed the 126 MB L2 every step",
-            "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single gpu", "seed": SEED}
+            "parallelism": par, "seed": SEED}
 
 
 class ClockSampler:
@@ -195,7 +206,9 @@ def run_reference(args, dist, rank):
     tok_s = ref.n * len(times) / sum(times)
     line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": T_TOK / tok_s * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _config(args.gpus),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": _config(args.gpus, args.parallel if args.gpus > 1 else "single",
+                              2 * args.gpus if args.gpus > 1 and args.parallel == "experts" else 2),
             "impl": "reference",
             "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
                              "sample": ref.sample(args.steps)},
@@ -207,22 +220,31 @@ def run_reference(args, dist, rank):
 def run_ours(args, dist, rank, world, local_rank):
     from distributedmoe_b200 import _native as N
     from distributedmoe_b200.MoE.local_cluster import LocalCluster
+    from distributedmoe_b200.MoE.sharded_cluster import ShardedCluster
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    parallel = args.parallel if world > 1 else "single"
+    if parallel == "experts" and E % world:
+        raise SystemExit(f"--parallel experts needs a GPU count that divides {E}")
+    E_here = E // world if parallel == "experts" else E
+    io_buffers = 2 * world if parallel == "experts" else 2
     gen = torch.Generator(device=dev).manual_seed(SEED + rank)
     dt = torch.bfloat16
-    gate = (torch.randn(E, I, D, generator=gen, device=dev) * 0.02).to(dt)
-    up = (torch.randn(E, I, D, generator=gen, device=dev) * 0.02).to(dt)
-    down = (torch.randn(E, D, I, generator=gen, device=dev) * 0.02).to(dt)
+    gate = (torch.randn(E_here, I, D, generator=gen, device=dev) * 0.02).to(dt)
+    up = (torch.randn(E_here, I, D, generator=gen, device=dev) * 0.02).to(dt)
+    down = (torch.randn(E_here, D, I, generator=gen, device=dev) * 0.02).to(dt)
     w_r = (torch.randn(E, D, generator=gen, device=dev) * 0.02).to(dt)
     x = torch.randn(T_TOK, D, generator=gen, device=dev).to(dt)
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(T_TOK, D, dtype=dt).pin_memory()
 
-    cluster = LocalCluster(E, [list(range(E))], K, D, dt, dev, [dev], stacked=[(gate, up, down)],
-                           io_buffer_size=8192, number_of_io_buffers=2, activation="silu", renormalize=True,
-                           router_fp32_logits=True)
+    opts = dict(io_buffer_size=8192, number_of_io_buffers=io_buffers, activation="silu", renormalize=True,
+                router_fp32_logits=True)
+    if parallel == "experts":
+        cluster = ShardedCluster(E, K, D, dt, dev, (gate, up, down), **opts)
+    else:
+        cluster = LocalCluster(E, [list(range(E))], K, D, dt, dev, [dev], stacked=[(gate, up, down)], **opts)
     moe = cluster.moe
     with torch.no_grad():
         moe.gate.weight.copy_(w_r)
@@ -245,7 +267,8 @@ def run_ours(args, dist, rank, world, local_rank):
                 moe(x)
             t1.record(stream)
             _barrier(dist, dev)
-        ktimes = N.kernel_times_ms()
+        krecs = N.kernel_records()
+        ktimes = {name: [ms for ms, _ in recs] for name, recs in krecs.items()}
         N.enable_kernel_timing(False)
         launches = N.launch_count() - launches0
         ms = _max_over_ranks(dist, t0.elapsed_time(t1) / args.steps, dev)
@@ -272,10 +295,14 @@ def run_ours(args, dist, rank, world, local_rank):
     if rank != 0:
         return
     burst, sustained, hbm, src = _peaks()
-    flops = 6.0 * T_TOK * K * D * I
-    mlp = ktimes.get("grouped_gated_mlp", [])
-    mlp_ms = statistics.median(mlp) if mlp else None
-    achieved = flops / (mlp_ms * 1e-3) / 1e12 if mlp_ms else None
+    # Grouped MLP launches on this GPU: FLOPs of the rows each launch computed (6 d I per
+    # row) over the summed CUDA-event durations.  With one launch per step that is the
+    # layer's 6 T k d I over the mean launch time.
+    mlp = krecs.get("grouped_gated_mlp", [])
+    flops_each = [w if w is not None else 6.0 * T_TOK * K * D * I for _, w in mlp]
+    mlp_ms = statistics.mean(ms for ms, _ in mlp) if mlp else None
+    flops = statistics.mean(flops_each) if mlp else None
+    achieved = sum(flops_each) / (sum(ms for ms, _ in mlp) * 1e-3) / 1e12 if mlp else None
     comb = ktimes.get("combine", [])
     comb_ms = statistics.median(comb) if comb else None
     comb_bytes = T_TOK * K * D * 2 + T_TOK * D * 2 + T_TOK * K * 4
@@ -287,7 +314,7 @@ def run_ours(args, dist, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": total_tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _config(world),
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _config(world, parallel, io_buffers),
         "impl": "ours",
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": T_TOK * D * 2, "d2h_bytes_per_step": T_TOK * D * 2},
@@ -296,7 +323,8 @@ def run_ours(args, dist, rank, world, local_rank):
                      "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
                      "frac": (achieved / sustained) if achieved else None, "peak_kind": f"{src} sustained bf16",
                      "frac_of_burst_peak": (achieved / burst) if achieved else None,
-                     "flops_per_launch": flops, "ms_per_launch": mlp_ms, "traffic": None},
+                     "flops_per_launch": flops, "ms_per_launch": mlp_ms, "launches_per_step": len(mlp) / args.steps,
+                     "traffic": None},
         "hbm_ops": {"combine_ms": comb_ms, "combine_gbs": comb_bytes / (comb_ms * 1e-3) / 1e9 if comb_ms else None,
                     "hbm_peak_gbs": hbm,
                     "op_ms": {k: statistics.median(v) for k, v in ktimes.items() if v}},
@@ -343,6 +371,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--parallel", default="experts", choices=["experts", "replicas"],
+                    help="with N > 1 GPUs: shard the experts over the GPUs, or run one layer per GPU")
     ap.add_argument("--mode", default="layer", choices=["layer", "gemm"],
                     help="gemm: time only the grouped expert MLP (for kernel profiling)")
     ap.add_argument("--gemm-rows", type=int, default=4096)

@@ -32,6 +32,18 @@ from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import (
     TensorTransferEngineConfig,
 )
 from distributedmoe_b200.TensorTransferEngine.utils import HandshakeType, TransferProtocol
+from distributedmoe_b200.utils.logging_config import get_logger
+
+
+def _ports_collide(table: List[dict]) -> bool:
+    seen = set()
+    for row in table:
+        ports = [row["host_port"], *row["host_p2p"], *row["host_hc"], *row["eb_port"], *row["eb_p2p"], *row["eb_hc"]]
+        for port in ports:
+            if (row["address"], port) in seen:
+                return True
+            seen.add((row["address"], port))
+    return False
 
 
 def experts_of_rank(number_of_experts: int, world: int, rank: int) -> List[int]:
@@ -55,12 +67,20 @@ class ShardedCluster:
         self.group = group
         self.rank, self.world = r, G
         device = torch.device(device)
-        p = free_ports(1 + 5 * G)
-        mine = {"host_port": p[0], "host_p2p": p[1:1 + G], "host_hc": p[1 + G:1 + 2 * G],
-                "eb_port": p[1 + 2 * G:1 + 3 * G], "eb_p2p": p[1 + 3 * G:1 + 4 * G], "eb_hc": p[1 + 4 * G:1 + 5 * G],
-                "address": address, "device": device.index}
-        table: List[dict] = [None] * G  # type: ignore[list-item]
-        dist.all_gather_object(table, mine, group=group)
+        # The first collective sets up the process group's own sockets (NCCL binds its
+        # listeners lazily), so it runs before this rank picks free ports for the engines.
+        dist.barrier(group=group)
+        for _attempt in range(5):
+            p = free_ports(1 + 5 * G)
+            mine = {"host_port": p[0], "host_p2p": p[1:1 + G], "host_hc": p[1 + G:1 + 2 * G],
+                    "eb_port": p[1 + 2 * G:1 + 3 * G], "eb_p2p": p[1 + 3 * G:1 + 4 * G],
+                    "eb_hc": p[1 + 4 * G:1 + 5 * G], "address": address, "device": device.index}
+            table: List[dict] = [None] * G  # type: ignore[list-item]
+            dist.all_gather_object(table, mine, group=group)
+            if not _ports_collide(table):  # every rank sees the same table and decides alike
+                break
+        else:
+            raise RuntimeError("could not pick distinct engine ports on all ranks")
         blocks = [experts_of_rank(number_of_experts, G, g) for g in range(G)]
         eb_devices = [torch.device("cuda", table[g]["device"]) for g in range(G)]
 
@@ -74,6 +94,7 @@ class ShardedCluster:
                 host_health_check_ports=list(table[h]["host_hc"]),
                 remote_health_check_ports=[table[g]["eb_hc"][h] for g in range(G)], **options)
 
+        self.logger = get_logger("dist_moe.sharded_cluster")
         self.errors: List[BaseException] = []
         self.threads: List[threading.Thread] = []
         for h in range(G):
@@ -84,12 +105,13 @@ class ShardedCluster:
                 remote_p2p_ports=[table[h]["host_p2p"][r]], p2p_timeout_duration=p2p_timeout_ms,
                 handshake_type=HandshakeType.CLIENT, transfer_protocol=TransferProtocol.NVLINK, ib_device_names="")
 
-            def job(cfg=cfg, eb_tte=eb_tte):
+            def job(cfg=cfg, eb_tte=eb_tte, h=h):
                 try:
                     torch.cuda.set_device(device)
                     blk = DistExpertsBlock(r, cfg, [], eb_tte, None, stacked_weights=stacked)
                     blk.main_loop()
-                except BaseException as e:  # surfaced by close()
+                except BaseException as e:  # logged now (a host may be waiting for it), raised by close()
+                    self.logger.error(f"expert block {r} for host {h} failed: {e!r}")
                     self.errors.append(e)
 
             t = threading.Thread(target=job, daemon=True, name=f"experts-block-{r}-for-host-{h}")

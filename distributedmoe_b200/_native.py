@@ -179,23 +179,30 @@ def enable_kernel_timing(on: bool = True) -> None:
 
 def kernel_times_ms() -> Dict[str, list]:
     """Durations (ms) of the ops recorded since timing was enabled; synchronises."""
+    return {name: [ms for ms, _ in recs] for name, recs in kernel_records().items()}
+
+
+def kernel_records() -> Dict[str, list]:
+    """(duration ms, work) per recorded op; work is the op's algorithmic FLOPs where the
+    wrapper knows them (the grouped MLP with a host segment table), else None."""
     with _timing_lock:
         snap = dict(_timing or {})
     out = {}
-    for name, pairs in snap.items():
+    for name, recs in snap.items():
         out[name] = []
-        for a, b in pairs:
+        for a, b, work in recs:
             b.synchronize()
-            out[name].append(a.elapsed_time(b))
+            out[name].append((a.elapsed_time(b), work))
     return out
 
 
 class _Timed:
-    __slots__ = ("name", "stream", "ev")
+    __slots__ = ("name", "stream", "ev", "work")
 
-    def __init__(self, name: str, stream: int, device: torch.device):
+    def __init__(self, name: str, stream: int, device: torch.device, work: Optional[float] = None):
         self.name = name
         self.ev = None
+        self.work = work
         if _timing is not None:
             self.stream = torch.cuda.ExternalStream(stream, device=device)
             self.ev = torch.cuda.Event(enable_timing=True)
@@ -207,7 +214,7 @@ class _Timed:
             end.record(self.stream)
             with _timing_lock:
                 if _timing is not None:
-                    _timing.setdefault(self.name, []).append((self.ev, end))
+                    _timing.setdefault(self.name, []).append((self.ev, end, self.work))
 
 
 def check_device_status(device: torch.device, reset: bool = True) -> None:
@@ -344,6 +351,7 @@ def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Te
         raise DMoEError("grouped MLP operands must share one dtype")
     dt = dtype_code(w_gate.dtype)
     ws = scratch.get(dev, "mlp", lib().dmoe_grouped_mlp_workspace_size(m_rows, I, dt))
+    work = None
     if isinstance(seg_expert, torch.Tensor):
         n_seg = seg_expert.numel()
         se, sn, on_dev = seg_expert.data_ptr(), seg_end.data_ptr(), 1
@@ -353,7 +361,14 @@ def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Te
         a1, a2 = _i32_array(seg_expert), _i32_array(seg_end)
         se, sn, on_dev = ctypes.addressof(a1), ctypes.addressof(a2), 0
         keep = (a1, a2)
-    tm = _Timed("grouped_gated_mlp", _stream(dev), dev)
+        if _timing is not None:  # rows of real (expert >= 0) segments x 6 d I
+            rows, start = 0, 0
+            for e, end in zip(seg_expert, seg_end):
+                if e >= 0:
+                    rows += end - start
+                start = end
+            work = 6.0 * rows * d * I
+    tm = _Timed("grouped_gated_mlp", _stream(dev), dev, work)
     rc = lib().dmoe_grouped_gated_mlp(x_ptr, w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
                                       se, sn, n_seg, on_dev, m_rows, act, y_ptr, ws.data_ptr(), ws.numel(),
                                       scratch.status(dev).data_ptr(), _stream(dev))
