@@ -50,6 +50,12 @@ class SegmentQueue:
     def items(self) -> List[Tuple[int, int]]:
         return list(self._q)
 
+    def has_rows(self) -> bool:
+        """True if a queued segment still holds rows.  Dispatch re-queues a segment after
+        taking rows from it even when it is used up (``MoE/PipelineTask.py:218``), so
+        ``empty()`` alone does not mean there is work left."""
+        return any(r > l for l, r in self._q)
+
 
 class ExpertMetaData:
     """Per-expert routing state of one forward pass (reference dataclass, same fields).

@@ -75,6 +75,10 @@ class DistMoEBlockConfig:
     topk_group: int = 1
     # expert block choice: "fifo" (reference round robin) or "least_loaded"
     expert_block_policy: str = "fifo"
+    # every dispatch wave sends at least one task to each alive block that holds pending
+    # activations (False: ceil(remaining / io_buffer_size) tasks per wave, as the reference,
+    # which sends the blocks' work one wave after another when it fits one buffer)
+    dispatch_all_blocks: bool = False
 
 
 class DistMoEBlock(nn.Module):
@@ -117,6 +121,10 @@ class DistMoEBlock(nn.Module):
                                          device=self.device)
         self.score_bias: Optional[torch.Tensor] = None
         self.output_batch: torch.Tensor = torch.zeros(1, dtype=self.dtype, device=self.device)
+        # Optional always-on shared expert (DeepSeek-V3 extension; the reference has none),
+        # computed on this GPU beside the routed experts and added with weight 1.
+        self.shared_expert: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None
+        self._shared_stream: Optional[torch.cuda.Stream] = None
 
         self.expert_blocks: List[List[int]] = config.expert_blocks
         self.expert_blocks_pool = ExpertBlocksPool(self.expert_blocks, policy=config.expert_block_policy)
@@ -352,6 +360,8 @@ class DistMoEBlock(nn.Module):
         self._counts_host.copy_(plan["counts"], non_blocking=True)
         ready = torch.cuda.Event()
         ready.record(stream)
+        # The shared expert (if any) goes to the GPU before the host waits for the counts.
+        shared_done = self._launch_shared_expert(x) if self.shared_expert is not None else None
         ready.synchronize()  # the only host synchronisation of the forward: E counts
         counts = self._counts_host.tolist()
         experts_hit, offsets, base = [], [0] * (E + 1), 0
@@ -365,6 +375,8 @@ class DistMoEBlock(nn.Module):
         offsets[E] = base
         arena = torch.empty(T * k, self.hidden_features, dtype=self.dtype, device=self.device)
         self.forward_state = ForwardState(x, plan, offsets, w, ready, arena)
+        if shared_done is not None:
+            self.forward_state.events.append(shared_done)
         return experts_hit, x
 
     def _finalize(self) -> None:
@@ -385,11 +397,53 @@ class DistMoEBlock(nn.Module):
             missing = np.flatnonzero(~covered)
             if missing.size:
                 fs.arena[torch.from_numpy(missing).to(self.device)] = 0
-        N.combine(fs.arena, fs.plan["inverse"], fs.routing_weights, self.output_batch)
+        N.combine(fs.arena, fs.plan["inverse"], fs.routing_weights, self.output_batch,
+                  accumulate=self.shared_expert is not None)
+
+    def set_shared_expert(self, gate_proj: torch.Tensor, up_proj: torch.Tensor, down_proj: torch.Tensor) -> None:
+        """Add an always-on shared expert: act(x W_g^T) * (x W_u^T) W_d^T with weight 1 for
+        every token (W_g, W_u [I_s, d]; W_d [d, I_s]).  It runs on the host's GPU on a side
+        stream while the routed tokens are dispatched (the shared expert is replicated on
+        every GPU, so it never crosses NVLink)."""
+        d = self.hidden_features
+        if gate_proj.shape != up_proj.shape or gate_proj.dim() != 2 or gate_proj.shape[1] != d \
+                or down_proj.shape != (d, gate_proj.shape[0]):
+            raise ValueError("shared expert weights must be gate/up [I_s, d] and down [d, I_s]")
+        prep = lambda w: w.detach().to(device=self.device, dtype=self.dtype).contiguous().unsqueeze(0)
+        self.shared_expert = (prep(gate_proj), prep(up_proj), prep(down_proj))
+        if self._shared_stream is None:
+            self._shared_stream = torch.cuda.Stream(device=self.device)
+
+    def _launch_shared_expert(self, x: torch.Tensor) -> torch.cuda.Event:
+        """Shared expert over all tokens into output_batch on the side stream; the final
+        combine waits for the returned event and accumulates the routed sum on top."""
+        g, u, dn = self.shared_expert
+        cur = torch.cuda.current_stream(self.device)
+        side = self._shared_stream
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            N.grouped_gated_mlp(x, g, u, dn, [0], [x.shape[0]], ACTIVATIONS[self.config.activation], self.output_batch)
+            done = torch.cuda.Event()
+            done.record(side)
+        x.record_stream(side)
+        self.output_batch.record_stream(side)
+        return done
+
+    def _blocks_with_pending_work(self) -> int:
+        hit = set(self.experts_hit)
+        n = 0
+        for md in self.expert_blocks_pool.expert_blocks_metadata:
+            if md.is_alive and any(e in hit and self.experts_metadata[e].expert_offsets.has_rows()
+                                   for e in md.expert_indexes):
+                n += 1
+        return n
 
     def dispatch(self, input_batch: torch.Tensor, number_of_dispatches: int, using_grouped_gemm: bool = True,
-                 using_alignment: bool = False) -> None:
+                 using_alignment: bool = False) -> List[asyncio.Task]:
+        """Create up to `number_of_dispatches` host tasks (``MoE/DistMoEBlock.py:638-668``);
+        returns their dispatch coroutines' tasks."""
         submits = 0
+        wave: List[asyncio.Task] = []
         while self.transferred_activations[0] < self.total_activations and submits < number_of_dispatches:
             task = HostPipelineTask(self.tensor_transfer_engine, self.input_buffers_pool, self.output_buffers_pool,
                                     self.experts_hit, self.expert_blocks_pool, self.experts_metadata, self.async_lock,
@@ -398,7 +452,9 @@ class DistMoEBlock(nn.Module):
             self.dispatch_tasks[task.name] = asyncio.create_task(task.dispatch(
                 input_batch, self.active_pipeline_tasks, self.transferred_activations, self.expert_block_tasks,
                 self.activations_batch_size_candidates if using_alignment else None, using_grouped_gemm))
+            wave.append(self.dispatch_tasks[task.name])
             submits += 1
+        return wave
 
     async def async_forward(self, input_batch: torch.Tensor, using_grouped_gemm: bool = True,
                             using_alignment: bool = False) -> torch.Tensor:
@@ -427,11 +483,28 @@ class DistMoEBlock(nn.Module):
             self.metrics_collector.end_setup_phase()
 
         start = timeit.default_timer()
+        stalled_waves = 0
         while self.transferred_activations[0] < self.total_activations:
             self.combining.clear()
-            n = max(math.ceil((self.total_activations - self.transferred_activations[0]) / self.io_buffer_size), 1)
-            self.dispatch(x, n, using_grouped_gemm, using_alignment)
+            before = self.transferred_activations[0]
+            n = max(math.ceil((self.total_activations - before) / self.io_buffer_size), 1)
+            if self.config.dispatch_all_blocks:
+                n = max(n, self._blocks_with_pending_work())
+            wave = self.dispatch(x, n, using_grouped_gemm, using_alignment)
             try:
+                if wave:
+                    await asyncio.wait(wave, timeout=max(self.forward_timeout / 1000 - (timeit.default_timer() - start), 0))
+                if self.active_pipeline_tasks[0] == 0 and self.transferred_activations[0] == before:
+                    # Every task of the wave drew a block with nothing left to pack (a FIFO
+                    # turn can land on such a block): take the next turn at once instead of
+                    # waiting for a combine that will not come.
+                    stalled_waves += 1
+                    if stalled_waves > len(self.expert_blocks) + 1 or \
+                            timeit.default_timer() - start > self.forward_timeout / 1000:
+                        self.logger.error("dispatch made no progress; returning a partial result")
+                        break
+                    continue
+                stalled_waves = 0
                 elapsed = timeit.default_timer() - start
                 await asyncio.wait_for(self.combining.wait(), timeout=(self.forward_timeout / 1000 - elapsed))
             except asyncio.TimeoutError:

@@ -105,7 +105,7 @@ class HostPipelineTask(PipelineTask):
         out = []
         for md in self.experts_block_pool.expert_blocks_metadata:
             for e in md.expert_indexes:
-                if e in hit and not self.experts_metadata[e].expert_offsets.empty():
+                if e in hit and self.experts_metadata[e].expert_offsets.has_rows():
                     out.append(md.experts_block_index)
                     break
         return out

@@ -60,6 +60,7 @@ class ShardedCluster:
                  device: torch.device, stacked, group: Optional[dist.ProcessGroup] = None,
                  io_buffer_size: int = 8192, number_of_io_buffers: int = 2, forward_timeout: int = 60000,
                  p2p_timeout_ms: int = 3000, address: str = "127.0.0.1", **options):
+        options.setdefault("dispatch_all_blocks", True)  # one task per GPU's block at once
         G = dist.get_world_size(group)
         r = dist.get_rank(group)
         if number_of_experts % G:

@@ -28,8 +28,9 @@ import os
 import socket
 import struct
 import threading
+import time
 import timeit
-from collections import deque
+from collections import OrderedDict, deque
 from dataclasses import dataclass
 from typing import Any, Dict, List, Optional, Tuple
 
@@ -93,6 +94,9 @@ _TOKENS = itertools.count(1)
 
 _DESC = struct.Struct("!IhQQ64sQQ64s")  # pid, device, ptr, size, mem handle, offset, event token, event handle
 
+# Copy handles kept for wait_for_transfer_efficient.
+_KEPT_TRANSFERS = 4096
+
 # Metadata header of a completion notice (outside the pipeline's 1000-1999 range).
 NOTICE_HEADER = 4738
 
@@ -135,6 +139,8 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self._pending_notice: Dict[str, Dict[int, set]] = {}  # owner -> stream -> region tokens
         self._region_owner: Dict[int, str] = {}
         self._notice_outbox: Dict[str, deque] = {}
+        self._xfers: "OrderedDict[bytes, Transfer]" = OrderedDict()
+        self._xfer_lock = threading.Lock()
         # Peers in this process exchange metadata through in-memory inboxes instead of ZeroMQ
         # once the handshake has shown that they share the process.
         self._inproc: Dict[str, bool] = {}
@@ -449,6 +455,33 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
 
     def _check_handler_status(self, transfer: Transfer) -> bool:
         return bool(transfer.handler.query())  # a local torch event of the copy stream
+
+    # ------------------------------------------------------------------ completion
+    def _track_transfer(self, transfer: Transfer) -> None:
+        """Copies are stream-ordered, so the pipeline never waits for them on the host.  The
+        handle is kept (the most recent _KEPT_TRANSFERS) for callers of
+        wait_for_transfer_efficient, which polls it itself; the monitor thread stays idle."""
+        with self._xfer_lock:
+            self._xfers[transfer.name] = transfer
+            while len(self._xfers) > _KEPT_TRANSFERS:
+                self._xfers.popitem(last=False)
+
+    def wait_for_transfer_efficient(self, transfer_name: bytes, timeout: Optional[int] = None) -> Optional[Transfer]:
+        """Block until the named copy finished; None after ``timeout`` ms or for an unknown
+        name (``TensorTransferEngine.py:305-314``)."""
+        with self._xfer_lock:
+            t = self._xfers.get(transfer_name)
+        if t is None:
+            return None
+        deadline = time.monotonic() + timeout / 1000 if timeout is not None else None
+        while not self._check_handler_status(t):
+            if deadline is not None and time.monotonic() >= deadline:
+                return None
+            time.sleep(20e-6)
+        if t.status != TransferStatus.FINISHED:
+            t.status = TransferStatus.FINISHED
+            t.duration = (timeit.default_timer() - t.duration) * 1000
+        return t
 
     def close(self) -> None:
         if self.is_closed:

@@ -96,7 +96,7 @@ def route(logits: torch.Tensor, top_k: int, out_dtype: torch.dtype, *, mode: int
         grouped = biased.view(T, n_group, per_group)
         group_score = grouped.topk(2, dim=-1).values.sum(dim=-1)             # [T, n_group]
         keep_groups = group_score.topk(topk_group, dim=-1).indices           # [T, topk_group]
-        group_mask = torch.zeros(T, n_group, dtype=torch.bool)
+        group_mask = torch.zeros(T, n_group, dtype=torch.bool, device=logits.device)
         group_mask.scatter_(1, keep_groups, True)
         expert_mask = group_mask.unsqueeze(-1).expand(T, n_group, per_group).reshape(T, E)
         masked = biased.masked_fill(~expert_mask, float("-inf"))
@@ -395,7 +395,7 @@ def local_experts(x: torch.Tensor, logits: torch.Tensor, gate_w: torch.Tensor, u
     E = gate_w.shape[0]
     rw, sel = route(logits, top_k, dtype if compute_dtype is None else torch.float32, mode=mode,
                     renormalize=renormalize, score_bias=score_bias, scale=scale, n_group=n_group, topk_group=topk_group)
-    out = torch.zeros(x.shape, dtype=dtype)
+    out = torch.zeros(x.shape, dtype=dtype, device=x.device)
     xin = x.to(dtype)
     mask = F.one_hot(sel, num_classes=E).permute(2, 1, 0)
     hit = torch.greater(mask.sum(dim=(-1, -2)), 0).nonzero().flatten().tolist()
