@@ -210,8 +210,7 @@ def _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act):
     (4, 256, 384, [1, 127, 128, 129, 0, 300]),
     (8, 200, 320, [5, 0, 260, 64]),          # K tail (200 % 64), N tails (I=320, d=200)
     (3, 512, 256, [1000]),
-    # segments averaging >= 128 rows take the pair (2-SM) kernel; remainders of <= 128 rows
-    # go to the single-SM kernel
+    # segments averaging >= 128 rows take the pair (2-SM) kernel
     (6, 256, 384, [1030, 1000, 300, 129, 0, 256, 511, 385]),
 ])
 def test_grouped_mlp_matches_fp32_reference(dtype, act, E, d, I, sizes):
@@ -225,6 +224,25 @@ def test_grouped_mlp_matches_fp32_reference(dtype, act, E, d, I, sizes):
     n = ends[-1]
     _assert_close_bf16(Y[:n].cpu(), ref[:n])
     assert torch.all(Y[n:].cpu() == 7.0), "rows outside the segments must stay untouched"
+
+
+@gpu
+@pytest.mark.parametrize("env", [{"DMOE_GEMM_HYBRID": "1"}, {"DMOE_GEMM_RASTER": "0"}, {"DMOE_GEMM_RASTER": "1"},
+                                 {"DMOE_GEMM_VARIANT": "1sm"}])
+def test_grouped_mlp_launch_variants(env, monkeypatch):
+    """The non-default launch shapes (pair tiles with single-SM remainders, the other tile
+    orders, single-SM tiles only) give the same results."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    N = _nat()
+    dtype, act = torch.bfloat16, O.ACT_SILU
+    X, wg, wu, wd, experts, ends = _mlp_case(77, 6, 256, 384, [1030, 1000, 300, 129, 0, 256, 511, 385], dtype, act)
+    Y = torch.zeros(X.shape[0], 256, dtype=dtype, device=DEV)
+    N.grouped_gated_mlp(X.to(DEV), wg.to(DEV), wu.to(DEV), wd.to(DEV), experts, ends, act, Y)
+    torch.cuda.synchronize()
+    _status_ok()
+    ref = _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act)
+    _assert_close_bf16(Y[:ends[-1]].cpu(), ref[:ends[-1]])
 
 
 @gpu
