@@ -92,7 +92,11 @@ def lib() -> ctypes.CDLL:
             if _lib is None:
                 if not os.path.exists(LIB_PATH):
                     raise DMoEError(f"{LIB_PATH} is missing: build it with `python -m distributedmoe_b200._build`")
-                handle = ctypes.CDLL(LIB_PATH)
+                # Every entry point only enqueues GPU work or touches host state for
+                # microseconds, so calls keep the GIL (PyDLL): releasing and re-taking it
+                # around each call hands the interpreter to another thread (the host's and
+                # the expert blocks' event loops share a process) at every launch.
+                handle = ctypes.PyDLL(LIB_PATH)
                 for name, (res, args) in SIGNATURES.items():
                     fn = getattr(handle, name)
                     fn.restype = res
