@@ -24,6 +24,7 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
+from distributedmoe_b200 import _native as N
 from distributedmoe_b200.MoE.DistExpertsBlock import DistExpertsBlock
 from distributedmoe_b200.MoE.DistMoEBlock import DistMoEBlock, DistMoEBlockConfig
 from distributedmoe_b200.MoE.local_cluster import free_ports
@@ -127,6 +128,12 @@ class ShardedCluster:
             handshake_type=HandshakeType.SERVER, transfer_protocol=TransferProtocol.NVLINK, ib_device_names="")
         with torch.cuda.device(device):
             self.moe = DistMoEBlock(config_of_host(r), host_tte)
+            # Load the grouped-MLP kernels once here rather than inside a block's first task,
+            # where the first launches would delay its health-check replies.
+            g, u, dn = stacked
+            rows = torch.zeros(256, hidden_features, dtype=dtype, device=device)
+            N.grouped_gated_mlp(rows, g, u, dn, [0], [256], N.ACT_SILU, torch.empty_like(rows))
+            torch.cuda.synchronize(device)
         dist.barrier(group=group)  # every host and block of every rank is up before the first forward
 
     def __enter__(self) -> DistMoEBlock:

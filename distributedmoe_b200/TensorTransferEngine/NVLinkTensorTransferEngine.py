@@ -271,6 +271,15 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         for i in range(n):
             f = _DESC.unpack_from(blob, 2 + i * _DESC.size)
             out.append(NVLinkRegion(f[0], f[1], f[2], f[3], f[4], f[5], f[6], f[7]))
+        # Map another process's buffers, open their events and set up the helper stream on
+        # their GPU now (set-up time), not inside the first transfer.
+        if torch.cuda.is_available():
+            for r in out:
+                if r.pid != self.pid:
+                    self.region_ptr(r)
+                    self.region_event(r)
+                    self._helper_stream(r.device)
+                    self._tmp_event(r.device)
         return out
 
     # ------------------------------------------------------------------ addressing

@@ -77,6 +77,7 @@ SIGNATURES = {
 }
 
 _lib: Optional[ctypes.CDLL] = None
+_lib_setup: Optional[ctypes.CDLL] = None
 _lib_lock = threading.Lock()
 
 
@@ -92,17 +93,33 @@ def lib() -> ctypes.CDLL:
             if _lib is None:
                 if not os.path.exists(LIB_PATH):
                     raise DMoEError(f"{LIB_PATH} is missing: build it with `python -m distributedmoe_b200._build`")
-                # Every entry point only enqueues GPU work or touches host state for
-                # microseconds, so calls keep the GIL (PyDLL): releasing and re-taking it
-                # around each call hands the interpreter to another thread (the host's and
-                # the expert blocks' event loops share a process) at every launch.
-                handle = ctypes.PyDLL(LIB_PATH)
-                for name, (res, args) in SIGNATURES.items():
-                    fn = getattr(handle, name)
-                    fn.restype = res
-                    fn.argtypes = args
-                _lib = handle
+                # Launches, copies and event operations only enqueue work, so these calls
+                # keep the GIL (PyDLL): releasing and re-taking it around each call hands the
+                # interpreter to another thread (the host's and the expert blocks' event loops
+                # share a process) at every launch.
+                _lib = _load(ctypes.PyDLL)
     return _lib
+
+
+def lib_setup() -> ctypes.CDLL:
+    """The same library with the GIL released during calls, for set-up calls that can take
+    milliseconds (IPC mappings, events of another GPU, which may create its context)."""
+    global _lib_setup
+    if _lib_setup is None:
+        lib()
+        with _lib_lock:
+            if _lib_setup is None:
+                _lib_setup = _load(ctypes.CDLL)
+    return _lib_setup
+
+
+def _load(kind) -> ctypes.CDLL:
+    handle = kind(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.restype = res
+        fn.argtypes = args
+    return handle
 
 
 def _check(rc: int, what: str) -> None:
@@ -401,7 +418,7 @@ def ipc_export(ptr: int) -> Tuple[bytes, int]:
     """(64-byte handle of the allocation holding ptr, byte offset of ptr inside it)."""
     buf = (ctypes.c_uint8 * 64)()
     off = _u64()
-    _check(lib().dmoe_ipc_export(ptr, buf, ctypes.byref(off)), "dmoe_ipc_export")
+    _check(lib_setup().dmoe_ipc_export(ptr, buf, ctypes.byref(off)), "dmoe_ipc_export")
     return bytes(buf), int(off.value)
 
 
@@ -410,16 +427,16 @@ def ipc_open(handle: bytes, device: int) -> int:
         raise DMoEError("IPC handle must be 64 bytes")
     buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
     out = _vp()
-    _check(lib().dmoe_ipc_open(buf, device, ctypes.byref(out)), "dmoe_ipc_open")
+    _check(lib_setup().dmoe_ipc_open(buf, device, ctypes.byref(out)), "dmoe_ipc_open")
     return int(out.value)
 
 
 def ipc_close(ptr: int) -> None:
-    _check(lib().dmoe_ipc_close(ptr), "dmoe_ipc_close")
+    _check(lib_setup().dmoe_ipc_close(ptr), "dmoe_ipc_close")
 
 
 def enable_peer_access(device: int, peer: int) -> None:
-    _check(lib().dmoe_enable_peer_access(device, peer), "dmoe_enable_peer_access")
+    _check(lib_setup().dmoe_enable_peer_access(device, peer), "dmoe_enable_peer_access")
 
 
 DMOE_NOT_READY = 4
@@ -428,12 +445,12 @@ DMOE_NOT_READY = 4
 def event_create(device: int, interprocess: bool = False) -> int:
     """A raw CUDA event (timing disabled) of `device`; returns its handle as an int."""
     out = _vp()
-    _check(lib().dmoe_event_create(device, int(interprocess), ctypes.byref(out)), "dmoe_event_create")
+    _check(lib_setup().dmoe_event_create(device, int(interprocess), ctypes.byref(out)), "dmoe_event_create")
     return int(out.value)
 
 
 def event_destroy(event: int) -> None:
-    _check(lib().dmoe_event_destroy(event), "dmoe_event_destroy")
+    _check(lib_setup().dmoe_event_destroy(event), "dmoe_event_destroy")
 
 
 def event_record(event: int, stream: int) -> None:
@@ -455,7 +472,7 @@ def stream_wait_event(stream: int, event: int) -> None:
 
 def ipc_event_export(event: int) -> bytes:
     buf = (ctypes.c_uint8 * 64)()
-    _check(lib().dmoe_ipc_event_export(event, buf), "dmoe_ipc_event_export")
+    _check(lib_setup().dmoe_ipc_event_export(event, buf), "dmoe_ipc_event_export")
     return bytes(buf)
 
 
@@ -465,7 +482,7 @@ def ipc_event_open(handle: bytes, device: int) -> int:
         raise DMoEError("an IPC event handle is 64 bytes")
     buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
     out = _vp()
-    _check(lib().dmoe_ipc_event_open(buf, device, ctypes.byref(out)), "dmoe_ipc_event_open")
+    _check(lib_setup().dmoe_ipc_event_open(buf, device, ctypes.byref(out)), "dmoe_ipc_event_open")
     return int(out.value)
 
 
