@@ -38,6 +38,11 @@ import subprocess
 import sys
 import time
 
+# Up to 32 hardware work queues per GPU (CUDA's default is 8): an expert-parallel process
+# drives a few tens of streams (buffer pools, helper streams), and streams that share a queue
+# serialise.  Must be set before CUDA starts.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)

@@ -1,7 +1,11 @@
 """Registered I/O buffers and their pool (reference ``MoE/pools/BuffersPool.py``).
 
 A ``Buffer`` is a ``[size, hidden]`` tensor registered with the transfer engine plus a
-dedicated CUDA stream.  With a stream-ordered engine (the NVLink backend) ``read_from`` and
+CUDA stream.  The buffers of one pool share one stream (the reference gives each buffer its
+own ``torch.cuda.Stream``, ``BuffersPool.py:45-46``; torch hands out 32 distinct streams
+per device and priority, so with the many buffers of an expert-parallel process unrelated
+buffers ended up sharing streams anyway).  The work on a pool's buffers is sequential:
+one task's gather, copy or expert MLP after another.  With a stream-ordered engine (the NVLink backend) ``read_from`` and
 ``write_to`` enqueue the copy on the buffer's stream and return: work issued later on that
 stream, or ordered after the region's completion event, sees the data.  Other engines are
 waited for on the host with a 1000 ms limit, as the reference does (``BuffersPool.py:55-90``).
@@ -24,7 +28,7 @@ from distributedmoe_b200.utils.logging_config import get_logger
 
 class Buffer:
     def __init__(self, tensor_transfer_engine: TensorTransferEngine, size: int, hidden_features: int,
-                 dtype: torch.dtype, device: torch.device) -> None:
+                 dtype: torch.dtype, device: torch.device, cuda_stream: Optional[torch.cuda.Stream] = None) -> None:
         assert tensor_transfer_engine is not None
         self.id: bytes = b""
         self.logger = get_logger("dist_moe.buffer")
@@ -36,7 +40,7 @@ class Buffer:
         self.size_in_bytes = size * self.row_bytes
         self.device = device
         self.data = torch.empty(size, hidden_features, dtype=dtype, device=device)
-        self.cuda_stream = torch.cuda.Stream(device=device)
+        self.cuda_stream = cuda_stream if cuda_stream is not None else torch.cuda.Stream(device=device)
         self.last_use = torch.cuda.Event()
         self.transfer_descs, self.register_descs = tensor_transfer_engine.register_batch(
             [self.data], "VRAM" if device.type == "cuda" else "DRAM", device.index)
@@ -101,8 +105,10 @@ class BuffersPool:
         self.device = device
         self.buffers: List[Buffer] = []
         self.buffer_index_pool: asyncio.Queue = asyncio.Queue()
+        self.cuda_stream = torch.cuda.Stream(device=device) if device.type == "cuda" else None
         for i in range(pool_size):
-            self.buffers.append(Buffer(tensor_transfer_engine, buffer_size, hidden_features, dtype, device))
+            self.buffers.append(Buffer(tensor_transfer_engine, buffer_size, hidden_features, dtype, device,
+                                       cuda_stream=self.cuda_stream))
             self.buffer_index_pool.put_nowait(i)
 
     async def acquire(self) -> Tuple[int, Buffer]:
@@ -125,3 +131,4 @@ class BuffersPool:
                 self.logger.error(f"Failed to close buffer {i}: {e}")
         if failed:
             self.logger.warning(f"BuffersPool cleanup: {failed} of {len(self.buffers)} buffers failed")
+

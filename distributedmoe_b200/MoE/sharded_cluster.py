@@ -55,13 +55,17 @@ def experts_of_rank(number_of_experts: int, world: int, rank: int) -> List[int]:
 class ShardedCluster:
     """``with ShardedCluster(...) as moe: y = moe(x_local)`` on every rank.
 
-    stacked: this rank's (gate [E_g, I, d], up [E_g, I, d], down [E_g, d, I]) on its GPU."""
+    stacked: this rank's (gate [E_g, I, d], up [E_g, I, d], down [E_g, d, I]) on its GPU.
+    gemm_sm_reserve: SMs the grouped-MLP launches of this process leave free (process-wide)."""
 
     def __init__(self, number_of_experts: int, top_k: int, hidden_features: int, dtype: torch.dtype,
                  device: torch.device, stacked, group: Optional[dist.ProcessGroup] = None,
                  io_buffer_size: int = 8192, number_of_io_buffers: int = 2, forward_timeout: int = 60000,
-                 p2p_timeout_ms: int = 3000, address: str = "127.0.0.1", **options):
+                 p2p_timeout_ms: int = 3000, address: str = "127.0.0.1", gemm_sm_reserve: int = 8, **options):
         options.setdefault("dispatch_all_blocks", True)  # one task per GPU's block at once
+        # Each GPU computes other hosts' experts while its own host gathers and combines: keep
+        # a few SMs out of the persistent grouped-MLP launches for those short kernels.
+        N.set_gemm_sm_reserve(gemm_sm_reserve)
         G = dist.get_world_size(group)
         r = dist.get_rank(group)
         if number_of_experts % G:

@@ -126,7 +126,7 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self._opened_mem: Dict[bytes, int] = {}       # mem handle -> mapped base (other processes)
         self._opened_events: Dict[Tuple[bytes, int], int] = {}  # (IPC event handle, device) -> event
         self._local_regions: Dict[int, NVLinkRegion] = {}
-        self._helpers: Dict[int, torch.cuda.Stream] = {}
+        self._helpers: Dict[Tuple[int, Any], torch.cuda.Stream] = {}
         self._lock = threading.Lock()
         # Local (not interprocess) events of each GPU for hand-offs between streams; one is
         # recorded and waited on as one step under _tmp_lock.
@@ -278,8 +278,7 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
                 if r.pid != self.pid:
                     self.region_ptr(r)
                     self.region_event(r)
-                    self._helper_stream(r.device)
-                    self._tmp_event(r.device)
+                    self._tmp_event(r.device)  # also brings up this process's context on that GPU
         return out
 
     # ------------------------------------------------------------------ addressing
@@ -329,19 +328,25 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         if stream.device.index == ev_device:
             N.stream_wait_event(stream.cuda_stream, ev)
             return
-        h = self._helper_stream(ev_device)
+        h = self._helper_stream(ev_device, stream.cuda_stream)
         with self._tmp_lock:
             tmp = self._tmp_event(ev_device)
             N.stream_wait_event(h.cuda_stream, ev)
             N.event_record(tmp, h.cuda_stream)
             N.stream_wait_event(stream.cuda_stream, tmp)
 
-    def _helper_stream(self, device: int) -> torch.cuda.Stream:
+    def _helper_stream(self, device: int, user: Any) -> torch.cuda.Stream:
+        """A dedicated stream on `device` for one user (a stream, or a notice source).  A
+        helper only waits and records; one per user keeps a late event of one user from
+        holding up the others queued behind it."""
+        key = (device, user)
         with self._lock:
-            h = self._helpers.get(device)
+            h = self._helpers.get(key)
             if h is None:
-                h = torch.cuda.Stream(device=device)
-                self._helpers[device] = h
+                # torch's high-priority pool: apart from the buffer pools' streams, which come
+                # from the default-priority pool.
+                h = torch.cuda.Stream(device=device, priority=-1)
+                self._helpers[key] = h
         return h
 
     def _tmp_event(self, device: int) -> int:
@@ -369,7 +374,7 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
             if r.device == here:
                 N.event_record(ev, stream.cuda_stream)
                 continue
-            h = self._helper_stream(r.device)
+            h = self._helper_stream(r.device, stream.cuda_stream)
             with self._tmp_lock:
                 tmp = self._tmp_event(here)
                 N.event_record(tmp, stream.cuda_stream)
@@ -429,7 +434,9 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
             r = self._local_regions.get(token)
             if r is None:
                 continue
-            h = self._helper_stream(r.device)
+            # One helper per sending GPU: its notices come from the one block there that
+            # serves this host, in that block's order.
+            h = self._helper_stream(r.device, ("notice", dev))
             self._wait_event_of(h, ev, dev)
             N.event_record(self.region_event(r), h.cuda_stream)
 
@@ -511,6 +518,7 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         self._opened_events.clear()
         self._tmp_events.clear()
         self._notice_events.clear()
+        self._helpers.clear()
         self.deregister_batch(list(self._local_regions.values()))
         with _ENGINES_LOCK:
             if _ENGINES.get(self.host_name) is self:

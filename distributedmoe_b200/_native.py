@@ -55,6 +55,7 @@ SIGNATURES = {
                                                _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dmoe_permute_rows": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, ctypes.c_int, _vp]),
     "dmoe_grouped_mlp_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "dmoe_grouped_mlp_set_sm_reserve": (ctypes.c_int, [ctypes.c_int]),
     "dmoe_grouped_gated_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp, _sz, _vp, _vp]),
@@ -396,6 +397,11 @@ def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Te
     del keep
     _check(rc, "dmoe_grouped_gated_mlp")
     tm.done()
+
+
+def set_gemm_sm_reserve(sms: int) -> None:
+    """SMs that later grouped-MLP launches of this process leave free for other streams."""
+    _check(lib().dmoe_grouped_mlp_set_sm_reserve(int(sms)), "dmoe_grouped_mlp_set_sm_reserve")
 
 
 def combine(rows: torch.Tensor, inverse: torch.Tensor, w: torch.Tensor, out: torch.Tensor,

@@ -989,6 +989,11 @@ int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_
   return DMOE_OK;
 }
 
+// SMs the persistent GEMM leaves free (dmoe_grouped_mlp_set_sm_reserve).  A persistent launch
+// holds every SM it gets until its last tile, so without a reserve the small kernels of other
+// streams (gathers, the combine, the router of another host's forward) wait for the whole GEMM.
+std::atomic<int> g_sm_reserve{0};
+
 template <bool GATED, int DT>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
                 const GemmArgs& args, int grid, cudaStream_t stream) {
@@ -1035,7 +1040,7 @@ int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorM
     max_clusters = n;
     configured_device = dev;
   }
-  int pairs = max_clusters;
+  int pairs = max_clusters - (g_sm_reserve.load(std::memory_order_relaxed) + 1) / 2;
   if (max_pairs >= 0 && max_pairs < pairs) pairs = max_pairs;
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs);
@@ -1066,6 +1071,13 @@ bool use_2sm(int n_seg, int m_rows) {
   if (v && strcmp(v, "1sm") == 0) return false;
   if (v && strcmp(v, "2sm") == 0) return true;
   return n_seg > 0 && m_rows / n_seg >= 128;
+}
+
+int sm_count();
+
+int usable_sms() {
+  const int n = sm_count() - g_sm_reserve.load(std::memory_order_relaxed);
+  return n > 1 ? n : 1;
 }
 
 int sm_count() {
@@ -1171,7 +1183,7 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
       r = launch_gemm_2sm<true, DT>(ta, tg, tu, pair_segs, a1, pair_m * nt1, stream);
       if (r) return r;
     }
-    const int sms1 = sm_count();
+    const int sms1 = usable_sms();
     if (rest_m > 0) {
       const int64_t t1 = (int64_t)rest_m * nt1;
       r = launch_gemm<true, DT>(ta, tg, tu, rest_segs, a1, (int)(t1 < sms1 ? t1 : sms1), stream);
@@ -1188,7 +1200,7 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     }
     return DMOE_OK;
   }
-  const int sms = sm_count();
+  const int sms = usable_sms();
   int g1 = sms, g2 = sms;
   if (total_m_host >= 0) {
     const int64_t t1 = (int64_t)total_m_host * nt1, t2 = (int64_t)total_m_host * nt2;
@@ -1207,6 +1219,13 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
 }  // namespace dmoe
 
 using namespace dmoe;
+
+extern "C" int dmoe_grouped_mlp_set_sm_reserve(int sms) {
+  clear_error();
+  DMOE_REQUIRE(sms >= 0 && sms <= 64, "dmoe_grouped_mlp_set_sm_reserve: %d SMs (0..64)", sms);
+  g_sm_reserve.store(sms, std::memory_order_relaxed);
+  return DMOE_OK;
+}
 
 extern "C" size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype) {
   (void)dtype;

@@ -158,6 +158,15 @@ int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, 
                            int32_t* dev_status, void* stream);
 
 /*
+ * Number of SMs (0..64, process-wide, default 0) that later dmoe_grouped_gated_mlp launches
+ * leave free.  No counterpart in the reference.  The grouped MLP is a persistent kernel that
+ * holds each SM it gets until its last tile; where one GPU also serves other streams' short
+ * kernels (an expert-parallel GPU gathers and combines for its own host while it computes
+ * other hosts' experts), a reserve lets those kernels start at once.
+ */
+int dmoe_grouped_mlp_set_sm_reserve(int sms);
+
+/*
  * Weighted combine (gather form): for each token t
  *     out[t] = sum_s w[t, s] * rows[inverse[t*k + s]]       (fp32 accumulation, one store)
  * `rows` [T*k, d] holds the expert outputs in permuted order.  Replaces the per-expert

@@ -1,6 +1,10 @@
 import os
 import sys
 
+# As bench.py does: more hardware work queues per GPU for the expert-parallel processes
+# (inherited by the spawned ranks of the multi-GPU tests); set before CUDA starts.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)

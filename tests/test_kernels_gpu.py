@@ -246,6 +246,25 @@ def test_grouped_mlp_launch_variants(env, monkeypatch):
 
 
 @gpu
+def test_grouped_mlp_with_sm_reserve():
+    """Leaving SMs free shrinks the persistent grid; the results stay the same."""
+    N = _nat()
+    dtype, act = torch.bfloat16, O.ACT_SILU
+    X, wg, wu, wd, experts, ends = _mlp_case(78, 6, 256, 384, [1030, 1000, 300, 129, 0, 256, 511, 385], dtype, act)
+    ref = _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act)
+    try:
+        for reserve in (8, 30):
+            N.set_gemm_sm_reserve(reserve)
+            Y = torch.zeros(X.shape[0], 256, dtype=dtype, device=DEV)
+            N.grouped_gated_mlp(X.to(DEV), wg.to(DEV), wu.to(DEV), wd.to(DEV), experts, ends, act, Y)
+            torch.cuda.synchronize()
+            _status_ok()
+            _assert_close_bf16(Y[:ends[-1]].cpu(), ref[:ends[-1]])
+    finally:
+        N.set_gemm_sm_reserve(0)
+
+
+@gpu
 def test_grouped_mlp_device_segment_table_and_reference_grouped_mm():
     """Device-resident segment table; compared with the reference's own bf16 grouped_mm path."""
     N = _nat()

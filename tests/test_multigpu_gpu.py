@@ -48,24 +48,29 @@ def _worker(rank, world, port, cfg, results):
         dev = torch.device("cuda", rank)
         torch.cuda.set_device(dev)
         T, d, E, k, I = cfg["T"], cfg["d"], cfg["E"], cfg["k"], cfg["I"]
+        steps = cfg.get("steps", 4)
         inp = make_layer_inputs(T * world, d, E, I, cfg["seed"], torch.bfloat16)
         mine = experts_of_rank(E, world, rank)
         stacked = (inp.gate[mine].contiguous().to(dev), inp.up[mine].contiguous().to(dev),
                    inp.down[mine].contiguous().to(dev))
-        x = inp.x[rank * T:(rank + 1) * T]
+        # A different batch every forward, issued back to back: a result read before its
+        # expert outputs landed (or one forward's rows in another's output) shows up here.
+        g = torch.Generator().manual_seed(cfg["seed"] * 100 + rank)
+        xs = [torch.randn(T, d, generator=g).to(torch.bfloat16) for _ in range(steps)]
         cl = ShardedCluster(E, k, d, torch.bfloat16, dev, stacked, io_buffer_size=cfg["io"], number_of_io_buffers=4,
                             activation="silu", renormalize=True, forward_timeout=20000)
         try:
             with torch.no_grad():
                 cl.moe.gate.weight.copy_(inp.w_r.to(dev))
-            ys = [cl.moe(x.to(dev)) for _ in range(3)]
+            xds = [x.to(dev) for x in xs]
+            ys = [cl.moe(x).clone() for x in xds]
             torch.cuda.synchronize()
             N.check_device_status(dev)
-            _, _, logits = N.router(x.to(dev), inp.w_r.to(dev), k, want_logits=True)
-            ref = O.local_experts(x, logits.cpu(), inp.gate, inp.up, inp.down, k, act=O.ACT_SILU, renormalize=True,
-                                  compute_dtype=torch.float32)
             errs = []
-            for y in ys:
+            for x, y in zip(xs, ys):
+                _, _, logits = N.router(x.to(dev), inp.w_r.to(dev), k, want_logits=True)
+                ref = O.local_experts(x, logits.cpu(), inp.gate, inp.up, inp.down, k, act=O.ACT_SILU,
+                                      renormalize=True, compute_dtype=torch.float32)
                 yy = y.float().cpu()
                 errs.append(((yy - ref).norm() / ref.norm()).item())
                 errs.append((yy - ref).abs().max().item() / max(1.0, ref.abs().max().item()))
@@ -110,7 +115,7 @@ def _run(world, cfg, timeout=240):
 
 @gpu
 def test_expert_parallel_two_gpus():
-    _run(2, dict(T=300, d=256, E=8, k=2, I=384, io=1024, seed=21))
+    _run(2, dict(T=1024, d=512, E=8, k=2, I=1024, io=2048, seed=21))
 
 
 @gpu
