@@ -56,6 +56,8 @@ SIGNATURES = {
     "dmoe_permute_rows": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, ctypes.c_int, _vp]),
     "dmoe_grouped_mlp_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "dmoe_grouped_mlp_set_sm_reserve": (ctypes.c_int, [ctypes.c_int]),
+    "dmoe_router_logits": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
+                                          _vp]),
     "dmoe_grouped_gated_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp, _sz, _vp, _vp]),
@@ -226,7 +228,10 @@ class _Timed:
         self.ev = None
         self.work = work
         if _timing is not None:
-            self.stream = torch.cuda.ExternalStream(stream, device=device)
+            # The current stream as torch knows it (the legacy default stream included);
+            # another handle is wrapped.
+            cur = torch.cuda.current_stream(device)
+            self.stream = cur if cur.cuda_stream == stream else torch.cuda.ExternalStream(stream, device=device)
             self.ev = torch.cuda.Event(enable_timing=True)
             self.ev.record(self.stream)
 
@@ -252,6 +257,10 @@ def check_device_status(device: torch.device, reset: bool = True) -> None:
 
 
 # ----------------------------------------------------------------------------- ops
+# From this many experts on, bf16/f16 router logits are a tensor-core GEMM (dmoe_router_logits).
+TC_LOGITS_MIN_EXPERTS = 32
+
+
 def router(x: Optional[torch.Tensor], w_r: Optional[torch.Tensor], top_k: int, *, num_experts: Optional[int] = None,
            mode: int = ROUTER_SOFTMAX, renormalize: bool = False, scale: float = 1.0,
            logit_bias: Optional[torch.Tensor] = None, score_bias: Optional[torch.Tensor] = None, n_group: int = 1,
@@ -278,10 +287,25 @@ def router(x: Optional[torch.Tensor], w_r: Optional[torch.Tensor], top_k: int, *
     else:
         idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
         w = torch.empty(T, top_k, dtype=w_dtype, device=dev)
-    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if (want_logits and logits_in is None) else None
     for b in (logit_bias, score_bias):
         if b is not None and (b.dtype != torch.float32 or b.numel() != E):
             raise DMoEError("router biases must be fp32 [E]")
+    if logits_in is None and x_dtype in (torch.bfloat16, torch.float16) and E >= TC_LOGITS_MIN_EXPERTS \
+            and E % 8 == 0 and d % 8 == 0 and E <= 256:
+        # Many experts: the logits GEMM on the tensor cores, then selection from those logits.
+        logits_in = torch.empty(T, E, dtype=torch.float32, device=dev)
+        tm = _Timed("router_logits", _stream(dev), dev, 2.0 * T * d * E)
+        _check(lib().dmoe_router_logits(x.data_ptr(), w_r.data_ptr(), dtype_code(x_dtype), T, d, E, logits_in.data_ptr(),
+                                        scratch.status(dev).data_ptr(), _stream(dev)), "dmoe_router_logits")
+        tm.done()
+        if logit_bias is not None:
+            logits_in.add_(logit_bias)
+        logit_bias = None
+        x = w_r = None
+        x_dtype, d = torch.float32, 0
+        logits = logits_in if want_logits else None
+    else:
+        logits = torch.empty(T, E, dtype=torch.float32, device=dev) if (want_logits and logits_in is None) else None
     tm = _Timed("router", _stream(dev), dev)
     rc = lib().dmoe_router(_ptr(x) if logits_in is None else None, _ptr(w_r) if logits_in is None else None,
                            dtype_code(x_dtype), _ptr(logit_bias), _ptr(score_bias), _ptr(logits_in), T, d, E, top_k,

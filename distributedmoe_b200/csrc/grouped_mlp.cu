@@ -67,6 +67,7 @@ struct GemmArgs {
   int act;
   int prefetch;     // k-blocks of L2 prefetch ahead of the TMA loads (0: off)
   int32_t* status;
+  int out_f32;      // plain GEMM only: store the fp32 accumulators instead of rounding to DT
 };
 
 // ------------------------------------------------------------------------- PTX wrappers
@@ -504,7 +505,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld32(tbase + j * 32, y);
           const int col0 = ti.nt * BN + j * 32;
-          if (valid) {
+          if (valid && args.out_f32) {
+            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col0 + v * 4 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else if (valid) {
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
@@ -870,7 +877,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld32(tbase + j * 32, y);
           const int col0 = ti.nt * BN + j * 32;
-          if (valid) {
+          if (valid && args.out_f32) {
+            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col0 + v * 4 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else if (valid) {
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
@@ -1215,6 +1228,43 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
   return launch_gemm<false, DT>(th, td, td, segs, a2, g2, stream);
 }
 
+// Router logits on the tensor cores: L[T, E] = X[T, d] · W_r[E, d]^T in fp32 (the plain GEMM
+// with one segment and W_r as a one-expert stack; E plays the output width, d the reduction).
+template <int DT>
+int run_logits(const void* X, const void* W, int T, int d, int E, float* out, int32_t* status, cudaStream_t stream) {
+  static thread_local GemmSegs segs;
+  segs.n_seg = 1;
+  segs.m_rows = T;
+  segs.e_stack = 1;
+  segs.dev_expert = nullptr;
+  segs.dev_end = nullptr;
+  segs.expert[0] = 0;
+  segs.end[0] = T;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)d, (uint64_t)T};
+    const uint32_t box[2] = {BK, BM};
+    int r = make_map(&ta, DT, X, 2, dims, box);
+    if (r) return r;
+  }
+  const int nt = (E + BN - 1) / BN;
+  GemmArgs a{out, E, E, d, nt, raster_mode(2), DMOE_ACT_RELU, 0, status, 1};
+  if (use_2sm(1, T)) {
+    const uint64_t dims[3] = {(uint64_t)d, (uint64_t)E, 1};
+    const uint32_t box[3] = {BK, 128, 1};
+    int r = make_map(&tb, DT, W, 3, dims, box);
+    if (r) return r;
+    return launch_gemm_2sm<false, DT>(ta, tb, tb, segs, a, ((T + BM2 - 1) / BM2) * nt, stream);
+  }
+  const uint64_t dims[3] = {(uint64_t)d, (uint64_t)E, 1};
+  const uint32_t box[3] = {BK, BN, 1};
+  int r = make_map(&tb, DT, W, 3, dims, box);
+  if (r) return r;
+  const int64_t tiles = (int64_t)((T + BM - 1) / BM) * nt;
+  const int sms = usable_sms();
+  return launch_gemm<false, DT>(ta, tb, tb, segs, a, (int)(tiles < sms ? tiles : sms), stream);
+}
+
 }  // namespace
 }  // namespace dmoe
 
@@ -1225,6 +1275,20 @@ extern "C" int dmoe_grouped_mlp_set_sm_reserve(int sms) {
   DMOE_REQUIRE(sms >= 0 && sms <= 64, "dmoe_grouped_mlp_set_sm_reserve: %d SMs (0..64)", sms);
   g_sm_reserve.store(sms, std::memory_order_relaxed);
   return DMOE_OK;
+}
+
+extern "C" int dmoe_router_logits(const void* x, const void* w_r, int dtype, int T, int d, int E, float* logits_out,
+                                  int32_t* dev_status, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_router_logits: dtype must be f16 or bf16");
+  DMOE_REQUIRE(T >= 0 && d > 0 && E > 0 && d % 8 == 0 && E % 8 == 0,
+               "dmoe_router_logits: d=%d and E=%d must be multiples of 8", d, E);
+  if (T == 0) return DMOE_OK;
+  DMOE_REQUIRE(x && w_r && logits_out && dev_status, "dmoe_router_logits: null pointer");
+  DMOE_REQUIRE(aligned16(x) && aligned16(w_r) && aligned16(logits_out), "dmoe_router_logits: 16-byte alignment");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DMOE_BF16) return run_logits<DMOE_BF16>(x, w_r, T, d, E, logits_out, dev_status, s);
+  return run_logits<DMOE_F16>(x, w_r, T, d, E, logits_out, dev_status, s);
 }
 
 extern "C" size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype) {

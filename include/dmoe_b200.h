@@ -82,6 +82,17 @@ int dmoe_router(const void* x, const void* w_r, int x_dtype, const float* logit_
                 void* stream);
 
 /*
+ * Router logits on the tensor cores: logits_out[T, E] = x[T, d] · w_r[E, d]^T in fp32
+ * (fp32 accumulation of the bf16/f16 products; no bias).  Replaces the gate Linear of
+ * MoE/DistMoEBlock.py:134,556 for large expert counts, where a dot product per (token,
+ * expert) on the CUDA cores is the slow part of routing; feed the result to dmoe_router as
+ * logits_in.  d % 8 == 0, E % 8 == 0.  Bounded waits report through *dev_status like the
+ * grouped MLP.
+ */
+int dmoe_router_logits(const void* x, const void* w_r, int dtype, int T, int d, int E, float* logits_out,
+                       int32_t* dev_status, void* stream);
+
+/*
  * Routing plan: per-expert counts, offsets and the permutation of the T*k activations.
  * Replaces the one-hot mask + per-expert torch.where loop of MoE/DistMoEBlock.py:568-605:
  * within an expert, activations are ordered slot-major then by ascending token, exactly as

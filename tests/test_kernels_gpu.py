@@ -88,6 +88,29 @@ def test_router_sigmoid_group_matches_oracle(T):
 
 
 @gpu
+@pytest.mark.parametrize("T,d,E", [(600, 7168, 256), (40, 512, 64), (1, 2048, 128)])
+def test_router_tensor_core_logits(T, d, E):
+    """Many experts: the logits are a tcgen05 GEMM (pair tiles for T >= 128, single-SM tiles
+    below), fp32 accumulation; selection from them is then bit-exact against the oracle."""
+    N = _nat()
+    g = torch.Generator().manual_seed(T + d + E)
+    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    w_r = (torch.randn(E, d, generator=g) * 0.006).to(torch.bfloat16)
+    bias = torch.randn(E, generator=g) * 0.01
+    idx, w, logits = N.router(x.to(DEV), w_r.to(DEV), 8, want_logits=True, mode=N.ROUTER_SIGMOID_GROUP,
+                              renormalize=True, scale=2.5, score_bias=bias.to(DEV), n_group=8, topk_group=4,
+                              w_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _status_ok()
+    ref_logits = x.double() @ w_r.double().t()
+    assert torch.allclose(logits.cpu().double(), ref_logits, rtol=1e-4, atol=1e-4)
+    rw, sel = O.route(logits.cpu(), 8, torch.float32, mode=O.ROUTER_SIGMOID_GROUP, renormalize=True, score_bias=bias,
+                      scale=2.5, n_group=8, topk_group=4)
+    assert torch.equal(idx.cpu(), sel)
+    assert torch.allclose(w.cpu(), rw, rtol=1e-5, atol=1e-6)
+
+
+@gpu
 def test_router_rejects_bad_args():
     N = _nat()
     x = torch.randn(4, 64, device=DEV)
