@@ -295,10 +295,14 @@ def run_reference(args, rank):
 
 
 # ----------------------------------------------------------------------------- GPU (ours)
-def _randn_bf16(shape, std, gen, dev, chunk_rows=16):
+def _randn_bf16(shape, std, gen, dev, chunk_elems=1 << 28):
     """Seeded N(0, std) bf16 tensor made on the GPU a slice at a time (no fp32 copy of the
     whole stack)."""
     out = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    row = 1
+    for n in shape[1:]:
+        row *= n
+    chunk_rows = max(1, chunk_elems // row)
     for i in range(0, shape[0], chunk_rows):
         j = min(shape[0], i + chunk_rows)
         out[i:j] = (torch.randn((j - i,) + tuple(shape[1:]), generator=gen, device=dev) * std).to(torch.bfloat16)

@@ -41,13 +41,15 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const char* __restric
     const int64_t drow = (int64_t)p.dst[lo] + off;
     const uint4* s = reinterpret_cast<const uint4*>(src) + srow * row_vecs;
     uint4* d = reinterpret_cast<uint4*>(dst) + drow * row_vecs;
+    // Eight 16-byte loads in flight per lane before the stores (a 4096-wide bf16 row is
+    // 16 vectors per lane).
     int64_t c = lane;
-    for (; c + 96 < row_vecs; c += 128) {
-      const uint4 v0 = s[c], v1 = s[c + 32], v2 = s[c + 64], v3 = s[c + 96];
-      d[c] = v0;
-      d[c + 32] = v1;
-      d[c + 64] = v2;
-      d[c + 96] = v3;
+    for (; c + 224 < row_vecs; c += 256) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = s[c + 32 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d[c + 32 * u] = v[u];
     }
     for (; c < row_vecs; c += 32) d[c] = s[c];
   }
@@ -84,7 +86,38 @@ __device__ __forceinline__ void store8(void* base, int64_t elem, const float* f)
 
 constexpr int kCombineMaxK = 16;
 
+// One 16-byte chunk (8 elements) of a row, raw: one uint4 for 16-bit types, two for fp32.
 template <int DT>
+struct Chunk {
+  uint4 v[DT == DMOE_F32 ? 2 : 1];
+};
+
+template <int DT>
+__device__ __forceinline__ Chunk<DT> load_chunk(const void* base, int64_t elem) {
+  Chunk<DT> c;
+  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(base) + elem * (DT == DMOE_F32 ? 4 : 2));
+  c.v[0] = p[0];
+  if constexpr (DT == DMOE_F32) c.v[1] = p[1];
+  return c;
+}
+
+template <int DT>
+__device__ __forceinline__ void chunk_to_float(const Chunk<DT>& c, float* f) {
+  if constexpr (DT == DMOE_F32) {
+    f[0] = __uint_as_float(c.v[0].x); f[1] = __uint_as_float(c.v[0].y);
+    f[2] = __uint_as_float(c.v[0].z); f[3] = __uint_as_float(c.v[0].w);
+    f[4] = __uint_as_float(c.v[1].x); f[5] = __uint_as_float(c.v[1].y);
+    f[6] = __uint_as_float(c.v[1].z); f[7] = __uint_as_float(c.v[1].w);
+  } else {
+    unpack8<DT>(c.v[0], f);
+  }
+}
+
+// One warp per token.  KU bounds k at compile time; CU chunks per lane are in flight at once,
+// with all k source rows of each loaded before any arithmetic, so a lane keeps KU x CU
+// 16-byte loads outstanding (HBM wants many bytes in flight per SM, and a token's rows are
+// only k x d x 2 bytes).
+template <int DT, int KU, int CU>
 __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ rows, const int32_t* __restrict__ inverse,
                                                       const void* __restrict__ w, int w_dtype, int T, int k, int d,
                                                       int accumulate, void* __restrict__ out) {
@@ -93,35 +126,61 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ r
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   const int nchunk = d / 8;
   for (int t = warp; t < T; t += nwarps) {
-    int64_t src[kCombineMaxK];
-    float wt[kCombineMaxK];
+    int64_t src[KU];
+    float wt[KU];
 #pragma unroll
-    for (int s = 0; s < kCombineMaxK; ++s) {
+    for (int s = 0; s < KU; ++s) {
       if (s < k) {
         src[s] = (int64_t)inverse[(int64_t)t * k + s] * d;
         wt[s] = load_as_float(w, (int64_t)t * k + s, w_dtype);
       }
     }
-    for (int c = lane; c < nchunk; c += 32) {
-      float acc[8];
-      if (accumulate) {
-        load8<DT>(out, (int64_t)t * d + c * 8, acc);
-      } else {
+    for (int c0 = lane; c0 < nchunk; c0 += 32 * CU) {
+      Chunk<DT> raw[CU][KU];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int u = 0; u < CU; ++u) {
+        const int c = c0 + u * 32;
+#pragma unroll
+        for (int s = 0; s < KU; ++s)
+          if (s < k && c < nchunk) raw[u][s] = load_chunk<DT>(rows, src[s] + (int64_t)c * 8);
       }
 #pragma unroll
-      for (int s = 0; s < kCombineMaxK; ++s) {
-        if (s < k) {
-          float v[8];
-          load8<DT>(rows, src[s] + c * 8, v);
+      for (int u = 0; u < CU; ++u) {
+        const int c = c0 + u * 32;
+        if (c >= nchunk) break;
+        float acc[8];
+        if (accumulate) {
+          load8<DT>(out, (int64_t)t * d + c * 8, acc);
+        } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = fmaf(wt[s], v[j], acc[j]);
+          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
         }
+#pragma unroll
+        for (int s = 0; s < KU; ++s) {
+          if (s < k) {
+            float v[8];
+            chunk_to_float<DT>(raw[u][s], v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(wt[s], v[j], acc[j]);
+          }
+        }
+        store8<DT>(out, (int64_t)t * d + c * 8, acc);
       }
-      store8<DT>(out, (int64_t)t * d + c * 8, acc);
     }
   }
+}
+
+template <int DT>
+void launch_combine(int blocks, cudaStream_t s, const void* rows, const int32_t* inverse, const void* w, int w_dtype,
+                    int T, int k, int d, int accumulate, void* out) {
+  if (k <= 2)
+    combine_kernel<DT, 2, 4><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
+  else if (k <= 4)
+    combine_kernel<DT, 4, 2><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
+  else if (k <= 8)
+    combine_kernel<DT, 8, 1><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
+  else
+    combine_kernel<DT, 16, 1><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
 }
 
 }  // namespace
@@ -174,11 +233,11 @@ extern "C" int dmoe_combine(const void* rows, const int32_t* inverse, const void
   if (blocks > 148 * 8) blocks = 148 * 8;
   cudaStream_t s = as_stream(stream);
   if (dtype == DMOE_BF16)
-    combine_kernel<DMOE_BF16><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
+    launch_combine<DMOE_BF16>(blocks, s, rows, inverse, w, w_dtype, T, k, d, accumulate, out);
   else if (dtype == DMOE_F16)
-    combine_kernel<DMOE_F16><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
+    launch_combine<DMOE_F16>(blocks, s, rows, inverse, w, w_dtype, T, k, d, accumulate, out);
   else
-    combine_kernel<DMOE_F32><<<blocks, 256, 0, s>>>(rows, inverse, w, w_dtype, T, k, d, accumulate, out);
+    launch_combine<DMOE_F32>(blocks, s, rows, inverse, w, w_dtype, T, k, d, accumulate, out);
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }

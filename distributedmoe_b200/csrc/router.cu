@@ -76,7 +76,12 @@ struct RouterArgs {
   float scale;
 };
 
-template <int DT>
+// With W_SMEM the block first copies the router weights (E x d, at most kWSmemMax bytes) into
+// shared memory: every warp then reads them from there instead of re-fetching the whole
+// matrix through L1/L2 for each of its tokens, and the kernel streams only x from HBM.
+constexpr int kWSmemMax = 96 * 1024;
+
+template <int DT, bool W_SMEM>
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a) {
   __shared__ float s_logit[kRouterWarps][kMaxExperts];
   __shared__ float s_gscore[kRouterWarps][32];
@@ -85,6 +90,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
   const int E = a.E;
   constexpr int VE = VecTraits<DT>::kElems;
   const int nvec = a.d / VE;
+  const void* wsrc = a.w_r;
+  if constexpr (W_SMEM) {
+    extern __shared__ uint4 s_w[];
+    const int n16 = (int)((int64_t)a.E * a.d * (DT == DMOE_F32 ? 4 : 2) / 16);
+    const uint4* g = reinterpret_cast<const uint4*>(a.w_r);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) s_w[i] = g[i];
+    __syncthreads();
+    wsrc = s_w;
+  }
 
   for (int t = blockIdx.x * kRouterWarps + warp; t < a.T; t += gridDim.x * kRouterWarps) {
     // ---------------------------------------------------------------- logits
@@ -102,7 +116,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
           for (int i = 0; i < kExpertGroup; ++i) {
             if (e0 + i < E) {
               float wv[VE];
-              load_vec<DT>(a.w_r, (int64_t)(e0 + i) * a.d + (int64_t)c * VE, wv);
+              load_vec<DT>(wsrc, (int64_t)(e0 + i) * a.d + (int64_t)c * VE, wv);
 #pragma unroll
               for (int j = 0; j < VE; ++j) acc[i] = fmaf(xv[j], wv[j], acc[i]);
             }
@@ -240,6 +254,23 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
   }
 }
 
+template <int DT, bool W_SMEM>
+int launch_router(dim3 grid, dim3 block, size_t smem, cudaStream_t s, const RouterArgs& a) {
+  if (W_SMEM) {
+    static int configured_device = -1;
+    int dev = 0;
+    DMOE_CUDA(cudaGetDevice(&dev));
+    if (configured_device != dev) {
+      DMOE_CUDA(cudaFuncSetAttribute(router_kernel<DT, W_SMEM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kWSmemMax));
+      configured_device = dev;
+    }
+  }
+  router_kernel<DT, W_SMEM><<<grid, block, smem, s>>>(a);
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}
+
 }  // namespace
 }  // namespace dmoe
 
@@ -269,15 +300,21 @@ extern "C" int dmoe_router(const void* x, const void* w_r, int x_dtype, const fl
   RouterArgs a{x, w_r, logit_bias, score_bias, logits_in, logits_out, idx_out, w_out, T, d, E, k, mode,
                renormalize, mode == DMOE_ROUTER_SIGMOID_GROUP ? n_group : 1, topk_group, w_dtype, scale};
   int blocks = (T + kRouterWarps - 1) / kRouterWarps;
+  cudaStream_t s = as_stream(stream);
+  const int64_t w_bytes = logits_in ? 0 : (int64_t)E * d * (x_dtype == DMOE_F32 ? 4 : 2);
+  if (logits_in == nullptr && w_bytes <= kWSmemMax) {
+    // Router weights in shared memory: enough blocks for every SM, each reused over tokens.
+    const int per_sm = (int)((227 * 1024) / (w_bytes + 10 * 1024));
+    const int cap = 148 * (per_sm < 1 ? 1 : per_sm);
+    if (blocks > cap) blocks = cap;
+    const dim3 grid(blocks), block(kRouterWarps * 32);
+    if (x_dtype == DMOE_BF16) return launch_router<DMOE_BF16, true>(grid, block, (size_t)w_bytes, s, a);
+    if (x_dtype == DMOE_F16) return launch_router<DMOE_F16, true>(grid, block, (size_t)w_bytes, s, a);
+    return launch_router<DMOE_F32, true>(grid, block, (size_t)w_bytes, s, a);
+  }
   if (blocks > 148 * 16) blocks = 148 * 16;
   const dim3 grid(blocks), block(kRouterWarps * 32);
-  cudaStream_t s = as_stream(stream);
-  if (x_dtype == DMOE_BF16)
-    router_kernel<DMOE_BF16><<<grid, block, 0, s>>>(a);
-  else if (x_dtype == DMOE_F16)
-    router_kernel<DMOE_F16><<<grid, block, 0, s>>>(a);
-  else
-    router_kernel<DMOE_F32><<<grid, block, 0, s>>>(a);
-  DMOE_LAUNCH_CHECK();
-  return DMOE_OK;
+  if (x_dtype == DMOE_BF16) return launch_router<DMOE_BF16, false>(grid, block, 0, s, a);
+  if (x_dtype == DMOE_F16) return launch_router<DMOE_F16, false>(grid, block, 0, s, a);
+  return launch_router<DMOE_F32, false>(grid, block, 0, s, a);
 }
