@@ -113,7 +113,7 @@ WORKLOADS = {
     # DeepSeek-V3-shape layer, 8192 tokens per step in all (strong scaling: T/N per GPU).
     "deepseek": Workload("deepseek-v3-moe-layer", tokens=8192, d=7168, E=256, k=8, I=2048, seed=2, w_std=0.006,
                          router_mode="sigmoid_group", n_group=8, topk_group=4, scale=2.5, score_bias_std=0.01,
-                         shared_inner=2048, strong=True, io_max=16384),
+                         shared_inner=2048, strong=True, io_max=65535),
 }
 
 

@@ -15,6 +15,7 @@ constexpr int kRouterWarps = 8;
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 16;
 constexpr int kExpertGroup = 8;  // experts whose dot products one pass over the row computes
+constexpr int kRowBatch = 4;     // row vectors a lane loads at once
 
 template <int DT>
 struct VecTraits {
@@ -109,16 +110,32 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
         float acc[kExpertGroup];
 #pragma unroll
         for (int i = 0; i < kExpertGroup; ++i) acc[i] = 0.f;
-        for (int c = lane; c < nvec; c += 32) {
-          float xv[VE];
-          load_vec<DT>(a.x, (int64_t)t * a.d + (int64_t)c * VE, xv);
+        // kRowBatch vectors of the token's row per lane are loaded before any arithmetic, so
+        // a lane keeps that many HBM reads in flight instead of one.
+        for (int c0 = lane; c0 < nvec; c0 += 32 * kRowBatch) {
+          float xv[kRowBatch][VE];
 #pragma unroll
-          for (int i = 0; i < kExpertGroup; ++i) {
-            if (e0 + i < E) {
-              float wv[VE];
-              load_vec<DT>(wsrc, (int64_t)(e0 + i) * a.d + (int64_t)c * VE, wv);
+          for (int u = 0; u < kRowBatch; ++u) {
+            const int c = c0 + 32 * u;
+            if (c < nvec) {
+              load_vec<DT>(a.x, (int64_t)t * a.d + (int64_t)c * VE, xv[u]);
+            } else {
 #pragma unroll
-              for (int j = 0; j < VE; ++j) acc[i] = fmaf(xv[j], wv[j], acc[i]);
+              for (int j = 0; j < VE; ++j) xv[u][j] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kRowBatch; ++u) {
+            const int c = c0 + 32 * u;
+            if (c >= nvec) break;
+#pragma unroll
+            for (int i = 0; i < kExpertGroup; ++i) {
+              if (e0 + i < E) {
+                float wv[VE];
+                load_vec<DT>(wsrc, (int64_t)(e0 + i) * a.d + (int64_t)c * VE, wv);
+#pragma unroll
+                for (int j = 0; j < VE; ++j) acc[i] = fmaf(xv[u][j], wv[j], acc[i]);
+              }
             }
           }
         }
