@@ -158,9 +158,12 @@ class DistExpertsBlock(nn.Module):
                 task = ExpertsBlockPipelineTask(tte, self.input_buffers_pool, self.output_buffers_pool, self.expert_layers,
                                                 self.experts_combine_layer, self.expert_streams, self.host_address,
                                                 metadata, self.async_lock, self.metrics_collector, self.activation)
-                tasks.append(asyncio.create_task(task.run(self.experts_block_index, self.host_input_buffers_transfer_descs,
-                                                          self.host_output_buffers_transfer_descs)))
-                tasks[:] = [t for t in tasks if not t.done()]
+                # Run the task here rather than as a new asyncio task (the reference's
+                # MoE/DistExpertsBlock.py:271-276): with stream-ordered transfers it only
+                # enqueues GPU work and never waits for it, so it ends quickly, and the
+                # extra event-loop turn would delay the expert MLP's launch.
+                await task.run(self.experts_block_index, self.host_input_buffers_transfer_descs,
+                               self.host_output_buffers_transfer_descs)
             else:
                 self.logger.warning(f"Unknown header received: {header}")
         pending = [t for t in tasks if not t.done()]

@@ -289,15 +289,14 @@ class DistMoEBlock(nn.Module):
                     name: bytes = metadata[-1][1]
                     task = self.pipeline_tasks.get(name)
                     if task is not None:
-                        async def combine(task=task, name=name):
-                            try:
-                                await task.combine(self.active_pipeline_tasks, self.output_batch, self.combining)
-                            finally:
-                                self.combine_tasks.pop(name, None)
-                                self.dispatch_tasks.pop(name, None)
-                                self.pipeline_tasks.pop(name, None)
-
-                        self.combine_tasks[name] = asyncio.create_task(combine())
+                        # Combined in this handler (the reference starts a task per ack,
+                        # MoE/DistMoEBlock.py:462): the
+                        # combine only enqueues a gather and updates counters.
+                        try:
+                            await task.combine(self.active_pipeline_tasks, self.output_batch, self.combining)
+                        finally:
+                            self.dispatch_tasks.pop(name, None)
+                            self.pipeline_tasks.pop(name, None)
                     else:
                         self.logger.debug(f"stale combine ack for task {name.hex()[:8]}")
                 elif header == P2PHeaders.HostInputBufferUnlocked.value:

@@ -96,7 +96,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
     extern __shared__ uint4 s_w[];
     const int n16 = (int)((int64_t)a.E * a.d * (DT == DMOE_F32 ? 4 : 2) / 16);
     const uint4* g = reinterpret_cast<const uint4*>(a.w_r);
-    for (int i = threadIdx.x; i < n16; i += blockDim.x) s_w[i] = g[i];
+    int i = threadIdx.x;
+    for (; i + 7 * (int)blockDim.x < n16; i += 8 * blockDim.x) {  // eight loads in flight per thread
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = g[i + u * blockDim.x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s_w[i + u * blockDim.x] = v[u];
+    }
+    for (; i < n16; i += blockDim.x) s_w[i] = g[i];
     __syncthreads();
     wsrc = s_w;
   }
