@@ -53,7 +53,7 @@ METRIC = "moe_layer_tokens_per_s"
 # Layer traffic of the grouped MLP (both GEMMs of one launch) for the Mixtral workload, from
 # `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` on the layer (one pass; see
 # profiles/launches_mixtral_moe_layer.md).  None for workloads without a capture.
-MIXTRAL_MLP_TRAFFIC_BYTES = None
+MIXTRAL_MLP_TRAFFIC_BYTES = (1971 + 228 + 1409 + 58) * 10**6  # GEMM1 read+write, GEMM2 read+write
 
 
 class Workload:

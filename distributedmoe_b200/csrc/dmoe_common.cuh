@@ -52,6 +52,10 @@ inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_o
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// SMs the grouped-MLP launches leave free (dmoe_grouped_mlp_set_sm_reserve); short kernels that
+// run beside them size their grids for those SMs.
+int gemm_sm_reserve();
+
 inline int dtype_bytes(int dt) { return dt == DMOE_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == DMOE_F32 || dt == DMOE_F16 || dt == DMOE_BF16; }
 

@@ -1270,6 +1270,10 @@ int run_logits(const void* X, const void* W, int T, int d, int E, float* out, in
 
 using namespace dmoe;
 
+namespace dmoe {
+int gemm_sm_reserve() { return g_sm_reserve.load(std::memory_order_relaxed); }
+}  // namespace dmoe
+
 extern "C" int dmoe_grouped_mlp_set_sm_reserve(int sms) {
   clear_error();
   DMOE_REQUIRE(sms >= 0 && sms <= 64, "dmoe_grouped_mlp_set_sm_reserve: %d SMs (0..64)", sms);

@@ -330,7 +330,10 @@ extern "C" int dmoe_router(const void* x, const void* w_r, int x_dtype, const fl
   if (logits_in == nullptr && w_bytes <= kWSmemMax) {
     // Router weights in shared memory: enough blocks for every SM, each reused over tokens.
     const int per_sm = (int)((227 * 1024) / (w_bytes + 10 * 1024));
-    const int cap = 148 * (per_sm < 1 ? 1 : per_sm);
+    // Each block first stages the weights: with an SM reserve set, the grouped MLP holds the
+    // other SMs, so size the grid for the reserved ones instead of queueing waves of copies.
+    const int reserve = gemm_sm_reserve();
+    const int cap = (reserve > 0 ? reserve : 148) * (per_sm < 1 ? 1 : per_sm);
     if (blocks > cap) blocks = cap;
     const dim3 grid(blocks), block(kRouterWarps * 32);
     if (x_dtype == DMOE_BF16) return launch_router<DMOE_BF16, true>(grid, block, (size_t)w_bytes, s, a);
