@@ -47,6 +47,26 @@ def _ports_collide(table: List[dict]) -> bool:
     return False
 
 
+def exchange_engine_ports(address: str, device_index: int, group: Optional[dist.ProcessGroup] = None) -> List[dict]:
+    """Pick this rank's engine ports (1 host port, then G each of host P2P, host health-check,
+    block port, block P2P, block health-check) and gather every rank's choice; all ranks get
+    the same table.  The first collective sets up the process group's own sockets (NCCL binds
+    its listeners lazily), so it runs before any port is picked; a table with a port used
+    twice on one address is picked again."""
+    G = dist.get_world_size(group)
+    dist.barrier(group=group)
+    for _attempt in range(5):
+        p = free_ports(1 + 5 * G)
+        mine = {"host_port": p[0], "host_p2p": p[1:1 + G], "host_hc": p[1 + G:1 + 2 * G],
+                "eb_port": p[1 + 2 * G:1 + 3 * G], "eb_p2p": p[1 + 3 * G:1 + 4 * G],
+                "eb_hc": p[1 + 4 * G:1 + 5 * G], "address": address, "device": device_index}
+        table: List[dict] = [None] * G  # type: ignore[list-item]
+        dist.all_gather_object(table, mine, group=group)
+        if not _ports_collide(table):  # every rank sees the same table and decides alike
+            return table
+    raise RuntimeError("could not pick distinct engine ports on all ranks")
+
+
 def experts_of_rank(number_of_experts: int, world: int, rank: int) -> List[int]:
     per = number_of_experts // world
     return list(range(rank * per, (rank + 1) * per))
@@ -73,20 +93,8 @@ class ShardedCluster:
         self.group = group
         self.rank, self.world = r, G
         device = torch.device(device)
-        # The first collective sets up the process group's own sockets (NCCL binds its
-        # listeners lazily), so it runs before this rank picks free ports for the engines.
-        dist.barrier(group=group)
-        for _attempt in range(5):
-            p = free_ports(1 + 5 * G)
-            mine = {"host_port": p[0], "host_p2p": p[1:1 + G], "host_hc": p[1 + G:1 + 2 * G],
-                    "eb_port": p[1 + 2 * G:1 + 3 * G], "eb_p2p": p[1 + 3 * G:1 + 4 * G],
-                    "eb_hc": p[1 + 4 * G:1 + 5 * G], "address": address, "device": device.index}
-            table: List[dict] = [None] * G  # type: ignore[list-item]
-            dist.all_gather_object(table, mine, group=group)
-            if not _ports_collide(table):  # every rank sees the same table and decides alike
-                break
-        else:
-            raise RuntimeError("could not pick distinct engine ports on all ranks")
+        table = exchange_engine_ports(address, device.index, group)
+        mine = table[r]
         blocks = [experts_of_rank(number_of_experts, G, g) for g in range(G)]
         eb_devices = [torch.device("cuda", table[g]["device"]) for g in range(G)]
 

@@ -1,0 +1,202 @@
+"""Host-side logic that needs no GPU: segment queues, expert-block selection, the engine's
+descriptor and completion-notice packets, the expert-parallel port exchange over two
+`gloo` ranks, and the benchmark's workload bookkeeping."""
+
+import asyncio
+import os
+import socket
+import struct
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from distributedmoe_b200.MoE.DistMoE import SegmentQueue
+from distributedmoe_b200.MoE.pools.ExpertBlocksPool import ExpertBlocksPool
+
+
+# ----------------------------------------------------------------------------- segment queue
+def test_segment_queue_has_rows_ignores_used_up_segments():
+    q = SegmentQueue([(0, 5)])
+    assert not q.empty() and q.has_rows()
+    l, r = q.get_nowait()
+    q.put_nowait((r, r))  # dispatch re-queues a segment it used up (reference behaviour)
+    assert not q.empty()
+    assert not q.has_rows()
+    q.put_nowait((7, 9))  # an aborted task's rows come back
+    assert q.has_rows()
+    assert q.items() == [(5, 5), (7, 9)]
+
+
+# ----------------------------------------------------------------------------- block pool
+def _run(coro):
+    return asyncio.new_event_loop().run_until_complete(coro)
+
+
+def test_fifo_pool_round_robin_skips_dead_blocks():
+    pool = ExpertBlocksPool([[0, 1], [2, 3], [4, 5]])
+
+    async def take(n):
+        out = []
+        for _ in range(n):
+            b, _md = await pool.aquire()
+            out.append(b)
+            pool.release(b)
+        return out
+
+    assert _run(take(4)) == [0, 1, 2, 0]
+    pool.mark_dead(1)
+    assert _run(take(3)) == [2, 0, 2]
+    pool.mark_alive(1)
+    assert 1 in _run(take(3))
+
+
+def test_least_loaded_pool_prefers_idle_candidates():
+    pool = ExpertBlocksPool([[0], [1], [2]], policy="least_loaded")
+    pool.add_load(0, 100)
+    pool.add_load(1, 10)
+    b, _ = _run(pool.aquire())
+    assert b == 2
+    b, _ = _run(pool.aquire([0, 1]))
+    assert b == 1
+    pool.mark_dead(1)
+    b, _ = _run(pool.aquire([0, 1]))
+    assert b == 0
+    pool.sub_load(0, 1000)
+    assert pool.load[0] == 0
+
+
+def test_unknown_policy_is_rejected():
+    with pytest.raises(ValueError):
+        ExpertBlocksPool([[0]], policy="random")
+
+
+# ----------------------------------------------------------------------------- engine packets
+def _bare_engine(pid=1234):
+    """An NVLink engine object without sockets or a GPU: enough for its packet code."""
+    from distributedmoe_b200.TensorTransferEngine.NVLinkTensorTransferEngine import NVLinkTensorTransferEngine
+    import threading
+
+    e = object.__new__(NVLinkTensorTransferEngine)
+    e.pid = pid
+    e._serialized_size = 2
+    e._lock = threading.Lock()
+    e._notice_events = {}
+    e._pending_notice = {}
+    e._region_owner = {}
+    e.remote_info = {}
+    return e
+
+
+def test_region_descriptors_round_trip():
+    from distributedmoe_b200.TensorTransferEngine.NVLinkTensorTransferEngine import NVLinkRegion
+
+    e = _bare_engine()
+    regions = [NVLinkRegion(e.pid, 3, 0x7F0000001000 + i, 4096 * (i + 1), bytes([i]) * 64, 256 * i, 10 + i,
+                            bytes([200 + i]) * 64) for i in range(3)]
+    back = e.deserialize_descs(e.serialize_descs(regions))
+    assert back == regions
+
+
+def test_completion_notice_packet_names_owner_device_and_regions():
+    from distributedmoe_b200.TensorTransferEngine.NVLinkTensorTransferEngine import NOTICE_HEADER, NVLinkRegion
+
+    e = _bare_engine()
+    e.remote_info = {"127.0.0.1:5000": (4321, 1, "box"), "127.0.0.1:6000": (999, 2, "box")}
+    handle = bytes(range(64))
+    stream_key = 0xABC
+    e._notice_events[stream_key] = (1, 0xDEAD, handle)
+    regions = [NVLinkRegion(4321, 1, 0, 16, b"\0" * 64, 0, tok, b"\0" * 64) for tok in (9, 3, 9)]
+    for r in regions:
+        owner = e._owner_name(r)
+        assert owner == "127.0.0.1:5000"
+        e._pending_notice.setdefault(owner, {}).setdefault(stream_key, set()).add(r.event_token)
+    packets = e._take_notices("127.0.0.1:5000")
+    assert len(packets) == 1 and e._take_notices("127.0.0.1:5000") == []
+    header, body = e.deserialize_p2p_packet(packets[0])
+    assert header == NOTICE_HEADER
+    assert struct.unpack("!h", body[0][1]) == (1,)
+    assert body[1][1] == handle
+    assert [struct.unpack("!Q", raw)[0] for _, raw in body[2:]] == [3, 9]
+    # a region of a process that is no peer of this engine has no owner
+    assert e._owner_name(NVLinkRegion(777, 0, 0, 16, b"\0" * 64, 0, 1, b"\0" * 64)) is None
+
+
+# ----------------------------------------------------------------------------- port exchange
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _port_worker(rank, world, port, results):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from distributedmoe_b200.MoE.sharded_cluster import _ports_collide, exchange_engine_ports
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        table = exchange_engine_ports("127.0.0.1", rank)
+        results.put((rank, table, _ports_collide(table)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_engine_port_exchange_over_two_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_port_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            rank, table, collide = results.get(timeout=120)
+            out[rank] = (table, collide)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert sorted(out) == [0, 1]
+    t0, t1 = out[0][0], out[1][0]
+    assert t0 == t1  # every rank sees the same table
+    assert not out[0][1]
+    for r, row in enumerate(t0):
+        assert row["device"] == r and row["address"] == "127.0.0.1"
+        for key in ("host_p2p", "host_hc", "eb_port", "eb_p2p", "eb_hc"):
+            assert len(row[key]) == world
+    ports = [p for row in t0 for key in ("host_p2p", "host_hc", "eb_port", "eb_p2p", "eb_hc") for p in row[key]]
+    ports += [row["host_port"] for row in t0]
+    assert len(ports) == len(set(ports))
+
+
+# ----------------------------------------------------------------------------- bench workloads
+def test_bench_workloads():
+    import bench
+
+    mix, ds = bench.WORKLOADS["mixtral"], bench.WORKLOADS["deepseek"]
+    # weak scaling: tokens per GPU fixed; strong: the step's tokens split over the GPUs
+    assert mix.tokens_per_rank(8) == 4096 and ds.tokens_per_rank(8) == 1024
+    assert mix.mlp_flops(4096) == 6.0 * 4096 * 2 * 4096 * 14336
+    assert ds.mlp_flops(8192) == pytest.approx(6.0 * 8192 * 8 * 7168 * 2048 + 6.0 * 8192 * 7168 * 2048)
+    # one host's buffers: every activation fits one wave; packet fields stay 16-bit
+    for w in (mix, ds):
+        for world in (1, 2, 4, 8):
+            par = "experts" if world > 1 else "single"
+            size, n = w.io(world, par)
+            assert 256 <= size <= 65535
+            per_host = w.tokens_per_rank(world) * w.k
+            if par == "single":
+                assert size * n >= per_host
+            else:
+                assert n == 2 * world and size >= per_host // world
+            c = w.config(world, par)
+            assert c["io_buffer_size"] == size and c["io_buffers"] == n
+            assert c["tokens_per_gpu"] * world == c["tokens_per_step"]
