@@ -332,3 +332,28 @@ def test_grouped_mlp_mixtral_shape_sampled_rows():
         ref = h @ wd[e].float().t()
         _assert_close_bf16(Y[rows].cpu(), ref.cpu())
         start = en
+
+
+# ----------------------------------------------------------------------------- completion flags
+@gpu
+def test_flag_signal_then_wait_and_bounded_timeout():
+    """A wait whose value is already there returns at once; a wait for a value nothing
+    writes gives up after its limit and reports DMOE_DEVERR_FLAG_TIMEOUT in the status word,
+    leaving the stream and the context usable.  (Signaller and waiter never run as two
+    kernels at the same time on this one GPU: the signal has finished before the wait.)"""
+    N = _nat()
+    dev = torch.device(DEV)
+    flag = torch.zeros(1, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    N.flag_signal(flag.data_ptr(), 5, s)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 5
+    N.flag_wait(flag.data_ptr(), 5, 2_000_000_000, status.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    N.flag_wait(flag.data_ptr(), 6, 2_000_000, status.data_ptr(), s)  # nothing writes 6: 2 ms limit
+    torch.cuda.synchronize()
+    assert int(status.item()) & 0x10
+    y = torch.ones(4, device=dev) * 3  # the context still works
+    assert float(y.sum().item()) == 12.0
