@@ -9,6 +9,7 @@
 
 #include <atomic>
 #include <cstdarg>
+#include <mutex>
 #include <cstdio>
 #include <string>
 
@@ -51,6 +52,25 @@ inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_o
   } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Per-device one-time set-up of a launch site (kernel attributes, occupancy queries), safe
+// when several host threads make their first launch on a device at the same time: `init`
+// runs once per device (< 64) and later calls see its effects.
+struct PerDeviceOnce {
+  std::mutex m;
+  std::atomic<uint64_t> done{0};
+};
+
+template <class F>
+int once_per_device(PerDeviceOnce& o, int dev, F&& init) {
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+  if (bit && (o.done.load(std::memory_order_acquire) & bit)) return DMOE_OK;
+  std::lock_guard<std::mutex> g(o.m);
+  if (bit && (o.done.load(std::memory_order_relaxed) & bit)) return DMOE_OK;
+  const int r = init();
+  if (r == DMOE_OK && bit) o.done.fetch_or(bit, std::memory_order_release);
+  return r;
+}
 
 // SMs the grouped-MLP launches leave free (dmoe_grouped_mlp_set_sm_reserve); short kernels that
 // run beside them size their grids for those SMs.

@@ -1010,14 +1010,15 @@ std::atomic<int> g_sm_reserve{0};
 template <bool GATED, int DT>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
                 const GemmArgs& args, int grid, cudaStream_t stream) {
-  static int configured_device = -1;
+  static PerDeviceOnce once;
   int dev = 0;
   DMOE_CUDA(cudaGetDevice(&dev));
-  if (configured_device != dev) {
+  const int r = once_per_device(once, dev, [] {
     DMOE_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GATED, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemBytes));
-    configured_device = dev;
-  }
+    return DMOE_OK;
+  });
+  if (r) return r;
   grouped_gemm_kernel<GATED, DT><<<grid, kThreads, kSmemBytes, stream>>>(a, b0, b1, segs, args);
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
@@ -1026,10 +1027,11 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
 template <bool GATED, int DT>
 int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
                     const GemmArgs& args, int max_pairs, cudaStream_t stream) {
-  static int configured_device = -1;
-  static int max_clusters = 0;
+  static PerDeviceOnce once;
+  static int max_clusters[64];
   int dev = 0;
   DMOE_CUDA(cudaGetDevice(&dev));
+  DMOE_REQUIRE(dev >= 0 && dev < 64, "grouped MLP: device index %d out of range", dev);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1041,7 +1043,7 @@ int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorM
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (configured_device != dev) {
+  const int r = once_per_device(once, dev, [&] {
     DMOE_CUDA(cudaFuncSetAttribute(grouped_gemm_2sm_kernel<GATED, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemBytes2));
     cfg.gridDim = dim3(2 * 74);
@@ -1050,10 +1052,11 @@ int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorM
       cudaGetLastError();
       n = 64;
     }
-    max_clusters = n;
-    configured_device = dev;
-  }
-  int pairs = max_clusters - (g_sm_reserve.load(std::memory_order_relaxed) + 1) / 2;
+    max_clusters[dev] = n;
+    return DMOE_OK;
+  });
+  if (r) return r;
+  int pairs = max_clusters[dev] - (g_sm_reserve.load(std::memory_order_relaxed) + 1) / 2;
   if (max_pairs >= 0 && max_pairs < pairs) pairs = max_pairs;
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs);

@@ -282,14 +282,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
 template <int DT, bool W_SMEM>
 int launch_router(dim3 grid, dim3 block, size_t smem, cudaStream_t s, const RouterArgs& a) {
   if (W_SMEM) {
-    static int configured_device = -1;
+    static PerDeviceOnce once;
     int dev = 0;
     DMOE_CUDA(cudaGetDevice(&dev));
-    if (configured_device != dev) {
+    const int r = once_per_device(once, dev, [] {
       DMOE_CUDA(cudaFuncSetAttribute(router_kernel<DT, W_SMEM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kWSmemMax));
-      configured_device = dev;
-    }
+      return DMOE_OK;
+    });
+    if (r) return r;
   }
   router_kernel<DT, W_SMEM><<<grid, block, smem, s>>>(a);
   DMOE_LAUNCH_CHECK();
