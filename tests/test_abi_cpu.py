@@ -53,6 +53,34 @@ def test_argument_validation_without_gpu():
     assert rc == 1
 
 
+def test_more_argument_checks_without_gpu():
+    """Every entry point rejects malformed requests with DMOE_ERR_INVALID and a message
+    before touching the GPU."""
+    from distributedmoe_b200 import _native as N
+    lib = N.lib()
+    # tensor-core router logits: d and E must be multiples of 8
+    assert lib.dmoe_router_logits(None, None, 2, 16, 100, 256, None, None, None) == 1
+    assert b"multiples of 8" in lib.dmoe_last_error()
+    assert lib.dmoe_router_logits(None, None, 0, 16, 128, 256, None, None, None) == 1  # fp32 inputs
+    # SM reserve range, then back to 0
+    assert lib.dmoe_grouped_mlp_set_sm_reserve(65) == 1
+    assert lib.dmoe_grouped_mlp_set_sm_reserve(-1) == 1
+    assert lib.dmoe_grouped_mlp_set_sm_reserve(0) == 0
+    # combine: k above the kernel's bound
+    assert lib.dmoe_combine(None, None, None, 2, 8, 17, 64, 2, 0, None, None) == 1
+    # gather: more segments than one launch takes
+    assert lib.dmoe_permute_rows(None, None, 64, None, None, None, None, 5000, None) == 1
+    # completion flag: misaligned flag and an out-of-range timeout
+    assert lib.dmoe_flag_signal(ctypes.c_void_p(12), 1, None) == 1
+    assert lib.dmoe_flag_wait(ctypes.c_void_p(16), 1, 0, None, None) == 1
+    assert lib.dmoe_flag_wait(ctypes.c_void_p(16), 1, 61 * 10**9, None, None) == 1
+    # router: bad mode and a group split that cannot hold k experts
+    assert lib.dmoe_router(None, None, 2, None, None, None, 16, 64, 8, 2, 7, 0, 1.0, 1, 1, None,
+                           ctypes.c_void_p(16), ctypes.c_void_p(16), 2, None) == 1
+    assert lib.dmoe_router(None, None, 2, None, None, None, 16, 64, 8, 4, 1, 0, 1.0, 4, 1, None,
+                           ctypes.c_void_p(16), ctypes.c_void_p(16), 2, None) == 1
+
+
 def test_no_cpu_fallback_in_product():
     """The product never imports the oracle."""
     pkg = os.path.join(ROOT, "distributedmoe_b200")
