@@ -110,6 +110,10 @@ WORKLOADS = {
     # Mixtral-8x7B-shape layer on each GPU (weak scaling over GPUs).
     "mixtral": Workload("mixtral-8x7b-moe-layer", tokens=4096, d=4096, E=8, k=2, I=14336, seed=1, w_std=0.02,
                         io_max=8192, traffic=MIXTRAL_MLP_TRAFFIC_BYTES),
+    # Qwen3-30B-A3B-shape decode step: few tokens (--tokens 16, 64 or 256) in all, 128 experts
+    # (16 per GPU over 8 GPUs); time per step is the figure of merit.
+    "qwen3-decode": Workload("qwen3-30b-a3b-decode-moe-layer", tokens=64, d=2048, E=128, k=8, I=768, seed=3,
+                             w_std=0.02, strong=True, io_max=2048),
     # DeepSeek-V3-shape layer, 8192 tokens per step in all (strong scaling: T/N per GPU).
     "deepseek": Workload("deepseek-v3-moe-layer", tokens=8192, d=7168, E=256, k=8, I=2048, seed=2, w_std=0.006,
                          router_mode="sigmoid_group", n_group=8, topk_group=4, scale=2.5, score_bias_std=0.01,
@@ -478,6 +482,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mixtral", choices=sorted(WORKLOADS))
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per step: per GPU for weak-scaling workloads, in all for the others")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--parallel", default="experts", choices=["experts", "replicas"],
                     help="with N > 1 GPUs: shard the experts over the GPUs, or run one layer per GPU")
@@ -486,6 +492,10 @@ def main():
     ap.add_argument("--gemm-rows", type=int, default=4096)
     ap.add_argument("--gemm-experts", type=int, default=2)
     args = ap.parse_args()
+    if args.tokens is not None:
+        if args.tokens < 1:
+            raise SystemExit("--tokens must be positive")
+        WORKLOADS[args.workload].tokens = args.tokens
     if args.mode == "gemm":
         run_gemm_only(args)
         return

@@ -186,8 +186,10 @@ def test_bench_workloads():
     assert mix.tokens_per_rank(8) == 4096 and ds.tokens_per_rank(8) == 1024
     assert mix.mlp_flops(4096) == 6.0 * 4096 * 2 * 4096 * 14336
     assert ds.mlp_flops(8192) == pytest.approx(6.0 * 8192 * 8 * 7168 * 2048 + 6.0 * 8192 * 7168 * 2048)
+    qwen = bench.WORKLOADS["qwen3-decode"]
+    assert qwen.E == 128 and qwen.k == 8 and qwen.strong
     # one host's buffers: every activation fits one wave; packet fields stay 16-bit
-    for w in (mix, ds):
+    for w in (mix, ds, qwen):
         for world in (1, 2, 4, 8):
             par = "experts" if world > 1 else "single"
             size, n = w.io(world, par)
