@@ -202,3 +202,89 @@ def test_bench_workloads():
             c = w.config(world, par)
             assert c["io_buffer_size"] == size and c["io_buffers"] == n
             assert c["tokens_per_gpu"] * world == c["tokens_per_step"]
+
+
+# ----------------------------------------------------------------------------- health checks
+class _FakePair:
+    """Health-check sockets of one block: pings are recorded; a pong comes back while the
+    block is 'up', nothing while it is 'down'."""
+
+    def __init__(self, engine):
+        from distributedmoe_b200.MoE.DistMoE import P2PHeaders
+
+        self.up = True
+        self.pings = 0
+        self._pong = engine.serialize_p2p_packet(P2PHeaders.Pong.value, [])
+        outer = self
+
+        class _Push:
+            async def send(self, packet):
+                outer.pings += 1
+
+        class _Pull:
+            async def recv(self):
+                while not outer.up:
+                    await asyncio.sleep(0.01)
+                return outer._pong
+
+        self.pusher, self.puller = _Push(), _Pull()
+
+
+class _FakeTask:
+    def __init__(self):
+        self.aborted = False
+        self.dispatch_done = True
+        self.combine_done = False
+        self.used_activations = 5
+
+    def abort(self):
+        self.aborted = True
+
+
+def test_health_checker_marks_a_silent_block_dead_then_alive_and_aborts_its_tasks():
+    """MoE/DistMoEBlock.py:312-414: a block that does not answer a ping within 1 s is marked
+    dead and the tasks dispatched to it are aborted (their activations go back to the
+    queues); when it answers again it is marked alive."""
+    import logging
+    from distributedmoe_b200.MoE.DistMoEBlock import DistMoEBlock
+
+    eng = _bare_engine()
+    blk = object.__new__(DistMoEBlock)
+    pair = _FakePair(eng)
+    blk.monitoring_flag = True
+    blk.disabled_expert_blocks = set()
+    blk.health_check_p2p_pairs = {"eb0": pair}
+    blk.tensor_transfer_engine = eng
+    blk.expert_blocks_pool = ExpertBlocksPool([[0, 1], [2, 3]])
+    blk.logger = logging.getLogger("test.health")
+    task = _FakeTask()
+    blk.pipeline_tasks = {b"t": task}
+    blk.expert_block_tasks = {0: [b"t"]}
+    blk.dispatch_tasks, blk.combine_tasks = {}, {}
+    blk.transferred_activations = [5]
+    blk.active_pipeline_tasks = [1]
+
+    async def scenario():
+        blk.async_lock = asyncio.Lock()
+        blk.combining = asyncio.Event()
+        checker = asyncio.create_task(blk._expert_block_health_checker(0, "eb0"))
+        md = blk.expert_blocks_pool.expert_blocks_metadata[0]
+        await asyncio.sleep(0.15)
+        alive_before = md.is_alive
+        pair.up = False
+        await asyncio.sleep(1.4)
+        dead_after_silence = not md.is_alive
+        pair.up = True
+        await asyncio.sleep(0.3)
+        alive_again = md.is_alive
+        blk.monitoring_flag = False
+        checker.cancel()
+        await asyncio.gather(checker, return_exceptions=True)
+        return alive_before, dead_after_silence, alive_again
+
+    alive_before, dead_after_silence, alive_again = _run(scenario())
+    assert alive_before and dead_after_silence and alive_again
+    assert pair.pings > 3
+    assert task.aborted
+    assert blk.transferred_activations == [0] and blk.active_pipeline_tasks == [0]
+    assert blk.expert_block_tasks[0] == [] and b"t" not in blk.pipeline_tasks
