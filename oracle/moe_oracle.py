@@ -114,6 +114,8 @@ def route(logits: torch.Tensor, top_k: int, out_dtype: torch.dtype, *, mode: int
 # ---------------------------------------------------------------------------------------
 @dataclass
 class RoutePlan:
+    """The per-expert state ``_setup_forward_pass`` builds (``MoE/DistMoEBlock.py:568-605``,
+    ``MoE/DistMoE.py:23-32``), plus the concatenated permuted order."""
     experts_hit: List[int]
     counts: torch.Tensor          # [E] int64
     offsets: torch.Tensor         # [E+1] int64, exclusive prefix of counts
@@ -157,8 +159,8 @@ def route_plan(selected: torch.Tensor, routing_weights: torch.Tensor, num_expert
 
 
 def route_plan_fast(selected: torch.Tensor, num_experts: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Vectorised equivalent of :func:`route_plan` for large inputs: a stable sort of the
-    slot-major flattened (slot, token) list by expert.  Returns (counts, offsets,
+    """Vectorised equivalent of :func:`route_plan` (``MoE/DistMoEBlock.py:568-605``) for large
+    inputs: a stable sort of the slot-major flattened (slot, token) list by expert.  Returns (counts, offsets,
     perm_token, perm_slot)."""
     T, k = selected.shape
     flat = selected.t().reshape(-1)                                   # slot-major order
@@ -184,6 +186,7 @@ def alignment_candidates(io_buffer_size: int) -> List[int]:
 
 @dataclass
 class PackedTask:
+    """One host task's packing (``MoE/PipelineTask.py:137-218``)."""
     block: int
     # (expert, buffer_offset, padded_size, actual_size, expert_offset_l)
     segments: List[Tuple[int, int, int, int, int]]
@@ -302,6 +305,8 @@ def serialize_p2p_packet(header: int, body) -> bytes:
 # expert compute and combine
 # ---------------------------------------------------------------------------------------
 def _act(g: torch.Tensor, act: int) -> torch.Tensor:
+    """The expert activation: ReLU as the reference's expert (``MoE/MoE.py:25-28``), or SiLU
+    (SwiGLU extension)."""
     return F.relu(g) if act == ACT_RELU else F.silu(g)
 
 
@@ -419,7 +424,8 @@ def local_experts(x: torch.Tensor, logits: torch.Tensor, gate_w: torch.Tensor, u
 def combine_from_permuted(y_perm: torch.Tensor, inverse: torch.Tensor, weights: torch.Tensor,
                           out_dtype: torch.dtype) -> torch.Tensor:
     """Gather form of the combine: out[t] = sum_s w[t,s] * y_perm[inverse[t,s]] in fp32, cast
-    once.  Equal to the reference's scatter-add up to summation order."""
+    once.  Equal to the reference's weighted scatter-add (``MoE/PipelineTask.py:326-346``) up
+    to summation order."""
     T, k = inverse.shape
     acc = torch.zeros(T, y_perm.shape[1], dtype=torch.float32)
     for s in range(k):
