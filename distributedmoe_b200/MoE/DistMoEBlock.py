@@ -12,6 +12,15 @@ kernels replace the gate GEMM, softmax, top-k, one-hot mask and the per-expert
 ``torch.where`` loop with its per-expert host synchronisations (``:553-605``).  The host
 reads back only the E per-expert counts, once per forward.  The output is the gather-form
 weighted combine of the permuted expert outputs, issued on the caller's stream.
+
+With the ``NVLinkDirect`` backend and :meth:`setup_direct_plane`, a forward is device-driven
+instead: router -> routing plan -> count exchange -> gather into the receivers' buffers over
+NVLink -> one grouped MLP per GPU over every host's rows -> epoch flags -> combine by peer
+loads, all on the caller's stream with no host synchronisation.  Every rank of the group
+runs one forward per step.  Block choice (alive blocks only, FIFO rotation or an even split
+over replicas) and dead-block exclusion keep the pool's semantics; rows of an expert with no
+alive block are left out of the sum, as the reference's partial result leaves out the
+tasks that never came back (``:716-718``).
 """
 
 from __future__ import annotations
@@ -22,7 +31,7 @@ import struct
 import threading
 import timeit
 from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Tuple
+from typing import Callable, Dict, List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -31,6 +40,7 @@ import zmq.asyncio
 
 from distributedmoe_b200 import _native as N
 from distributedmoe_b200.MoE.DistMoE import ExpertMetaData, P2PHeaders, SegmentQueue
+from distributedmoe_b200.MoE.instances import InstanceTable
 from distributedmoe_b200.MoE.PipelineTask import ForwardState, HostPipelineTask
 from distributedmoe_b200.MoE.pools.BuffersPool import BuffersPool
 from distributedmoe_b200.MoE.pools.ExpertBlocksPool import ExpertBlocksPool
@@ -61,12 +71,15 @@ class DistMoEBlockConfig:
     forward_timeout: int
     host_health_check_ports: List[int]
     remote_health_check_ports: List[int]
-    # ---- options this build adds (defaults reproduce the reference) ----
+    # ---- options this build adds; each default reproduces the reference except
+    # router_fp32_logits, which defaults to fp32 logits (the reference's gate computes them in
+    # the model dtype, and that rounding can change the top-k picks of near-ties) ----
     # expert activation: "relu" (reference, MoE/MoE.py:25) or "silu" (SwiGLU)
     activation: str = "relu"
     # divide the top-k routing weights by their sum (the reference does not)
     renormalize: bool = False
-    # router logits in fp32 (False: in the model dtype, as the reference's gate computes them)
+    # router logits in fp32 (False: in the model dtype, as the reference's gate computes them;
+    # True is the one default that differs from the reference)
     router_fp32_logits: bool = True
     # "softmax" (reference) or "sigmoid_group" (DeepSeek-V3 style)
     router_mode: str = "softmax"
@@ -152,6 +165,7 @@ class DistMoEBlock(nn.Module):
         self.monitoring_flag = True
         self.monitoring_tasks: List[asyncio.Task] = []
         self.disabled_expert_blocks: set = set()
+        self._ep: Optional[dict] = None  # device-driven data plane (setup_direct_plane)
         self.setup_monitoring()
         self.logger.info(f"DistMoEBlock initialized - Experts: {self.number_of_experts}, "
                          f"Blocks: {self.number_of_expert_blocks}, Device: {self.device}")
@@ -319,11 +333,11 @@ class DistMoEBlock(nn.Module):
             self.monitoring_tasks.append(self.event_loop.create_task(self._expert_block_p2p_handler(b, remote_name)))
 
     # ------------------------------------------------------------------ forward
-    def _route(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    def _route(self, x: torch.Tensor, w_dtype: Optional[torch.dtype] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         cfg = self.config
         mode = N.ROUTER_SOFTMAX if cfg.router_mode == "softmax" else N.ROUTER_SIGMOID_GROUP
         kw = dict(mode=mode, renormalize=cfg.renormalize, scale=cfg.routed_scaling_factor, n_group=cfg.n_group,
-                  topk_group=cfg.topk_group, w_dtype=self.dtype,
+                  topk_group=cfg.topk_group, w_dtype=w_dtype or self.dtype,
                   score_bias=None if self.score_bias is None else self.score_bias.float().contiguous())
         g = self.gate
         plain_linear = isinstance(g, nn.Linear) and g.weight.dtype == x.dtype and g.weight.is_contiguous()
@@ -421,7 +435,8 @@ class DistMoEBlock(nn.Module):
         side = self._shared_stream
         side.wait_stream(cur)
         with torch.cuda.stream(side):
-            N.grouped_gated_mlp(x, g, u, dn, [0], [x.shape[0]], ACTIVATIONS[self.config.activation], self.output_batch)
+            N.grouped_gated_mlp(x, g, u, dn, [0], [x.shape[0]], ACTIVATIONS[self.config.activation], self.output_batch,
+                                op_name="shared_expert_mlp")
             done = torch.cuda.Event()
             done.record(side)
         x.record_stream(side)
@@ -530,7 +545,118 @@ class DistMoEBlock(nn.Module):
         return self.output_batch.reshape(shape)
 
     def forward(self, input_batch: torch.Tensor, using_grouped_gemm: bool = True, using_alignment: bool = False) -> torch.Tensor:
+        if self._ep is not None:
+            return self._direct_forward(input_batch)
         return self.event_loop.run_until_complete(self.async_forward(input_batch, using_grouped_gemm, using_alignment))
+
+    # ------------------------------------------------------------------ device-driven data plane
+    def setup_direct_plane(self, world: int, rank: int, block_ranks: List[int], local_stack, capacity: int,
+                           exchange: Callable[[bytes], List[bytes]], max_tokens: int,
+                           wait_timeout_ms: Optional[int] = None) -> None:
+        """Switch forward() to the device-driven exchange (``NVLinkDirect`` backend only).
+
+        world, rank: this host's group (one rank per GPU, every rank calls forward once per
+        step); block_ranks[b]: the rank holding expert block b; local_stack: this rank's
+        (gate [S, I, d], up [S, I, d], down [S, d, I]) for its blocks in index order (S = its
+        expert instances); capacity: receive rows per GPU (at least the rows all hosts can
+        send it: world * max_tokens * top_k covers any routing); exchange(mine) returns every
+        rank's window descriptor in rank order; max_tokens: tokens per forward of this host."""
+        tte = self.tensor_transfer_engine
+        if not getattr(tte, "direct", False):
+            raise RuntimeError("the device-driven data plane needs the NVLinkDirect backend")
+        E, k, d = self.number_of_experts, self.top_k, self.hidden_features
+        inst = InstanceTable.from_blocks(self.expert_blocks, block_ranks, world, E)
+        n_local = inst.local_count(rank)
+        g, u, dn = local_stack
+        if g.dim() != 3 or g.shape[0] != n_local or g.shape[2] != d or u.shape != g.shape \
+                or dn.shape != (n_local, d, g.shape[1]):
+            raise ValueError(f"rank {rank} holds {n_local} expert instances: its stack must be gate/up "
+                             f"[{n_local}, I, {d}] and down [{n_local}, {d}, I]")
+        if self.dtype not in (torch.bfloat16, torch.float16):
+            raise NotImplementedError("the device-driven data plane computes in bf16 or fp16")
+        dev = self.device
+        with torch.cuda.device(dev):
+            tte.open_window(capacity, d, self.dtype, inst.n_inst, dev)
+            descs = exchange(tte.window_descriptor())
+            win = tte.attach_windows(descs, rank)
+            i32 = dict(dtype=torch.int32, device=dev)
+            R = N.EP_MAX_REPLICAS
+            policy = N.EP_POLICY_SPLIT if self.config.expert_block_policy == "least_loaded" else N.EP_POLICY_ROTATE
+            timeout_ms = wait_timeout_ms if wait_timeout_ms is not None else min(self.forward_timeout, 5000)
+            self._ep = {
+                "world": world, "rank": rank, "inst": inst, "win": win, "cap": capacity, "policy": policy,
+                "n_local": n_local, "stack": (g, u, dn), "max_tokens": max_tokens, "epoch": 0,
+                "timeout_ns": int(timeout_ms) * 1_000_000,
+                "inst_rank": torch.tensor(inst.inst_rank, **i32),
+                "inst_slot": torch.tensor(inst.inst_slot, **i32),
+                "inst_first": torch.tensor(inst.inst_first, **i32),
+                "alive": torch.zeros(E + E * R, **i32), "alive_key": None,
+                "part_n": torch.zeros(E, **i32), "part_inst": torch.zeros(E * R, **i32),
+                "part_start": torch.zeros(E * (R + 1), **i32), "dest_off": torch.zeros(inst.n_inst, **i32),
+                "seg_expert": torch.zeros(max(n_local, 1), **i32), "seg_end": torch.zeros(max(n_local, 1), **i32),
+                "done": torch.zeros(1, **i32), "ret": torch.empty(max(max_tokens * k, 1), **i32),
+            }
+            torch.cuda.synchronize(dev)
+
+    def _direct_alive(self) -> None:
+        """Upload the per-expert alive instances when the pool's alive flags changed."""
+        ep = self._ep
+        key = tuple(md.is_alive for md in self.expert_blocks_pool.expert_blocks_metadata)
+        if key != ep["alive_key"]:
+            n, inst = ep["inst"].alive_arrays(key)
+            ep["alive"].copy_(torch.tensor(n + inst, dtype=torch.int32).pin_memory(), non_blocking=True)
+            ep["alive_key"] = key
+
+    def _direct_forward(self, input_batch: torch.Tensor) -> torch.Tensor:
+        ep = self._ep
+        assert input_batch.dtype == self.dtype and input_batch.device == self.device
+        shape = input_batch.shape
+        if input_batch.dim() not in (2, 3) or shape[-1] != self.hidden_features:
+            raise RuntimeError(f"Wrong input batch shape: {shape} with hidden size: {self.hidden_features}")
+        x = input_batch.reshape(-1, self.hidden_features).contiguous()
+        T, E, k = x.shape[0], self.number_of_experts, self.top_k
+        if T > ep["max_tokens"]:
+            raise ValueError(f"{T} tokens exceed the {ep['max_tokens']} this data plane was sized for")
+        if self.metrics_collector is not None:
+            self.metrics_collector.start_forward_pass()
+        dev = self.device
+        ep["epoch"] += 1
+        epoch, win, cap, tmo = ep["epoch"], ep["win"], ep["cap"], ep["timeout_ns"]
+        out = torch.empty(x.shape, dtype=self.dtype, device=dev)
+        self.output_batch = out
+        shared = self.shared_expert is not None and T > 0
+        shared_done = self._launch_shared_expert(x) if shared else None
+        self._direct_alive()
+        R = N.EP_MAX_REPLICAS
+        table = (ep["alive"][:E], ep["alive"][E:], ep["inst_rank"], ep["inst_slot"], ep["inst_first"])
+        placement = (ep["part_n"], ep["part_inst"], ep["part_start"], ep["dest_off"])
+        if T > 0:
+            idx, w = self._route(x, w_dtype=torch.float32)
+            plan = N.route_plan(idx, None, E, want_slot=False, want_weight=False)
+            counts, offsets, perm_token, inverse = plan["counts"], plan["offsets"], plan["perm_token"], plan["inverse"]
+        else:
+            counts = offsets = perm_token = inverse = w = None
+        inst = ep["inst"]
+        N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, epoch, tmo,
+                  placement + (ep["seg_expert"], ep["seg_end"]))
+        N.ep_dispatch(win, x, T, k, E, offsets, perm_token, placement, ep["inst_rank"], cap, ep["ret"], ep["done"],
+                      epoch)
+        # This GPU's expert instances, once, over every host's rows (the expert blocks' part).
+        N.ep_wait(win, N.EP_FLAG_DATA, epoch, tmo, dev)
+        if ep["n_local"] > 0:
+            g, u, dn = ep["stack"]
+            tte = self.tensor_transfer_engine
+            N.grouped_gated_mlp(tte.recv, g, u, dn, ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]],
+                                ACTIVATIONS[self.config.activation], tte.out, m_rows=cap)
+        N.ep_signal(win, N.EP_FLAG_RESULTS, epoch, dev)
+        N.ep_wait(win, N.EP_FLAG_RESULTS, epoch, tmo, dev)
+        if T > 0:
+            if shared_done is not None:
+                torch.cuda.current_stream(dev).wait_event(shared_done)
+            N.ep_combine(win, inverse, ep["ret"], w, T, k, out, accumulate=shared)
+        if self.metrics_collector is not None:
+            self.metrics_collector.end_forward_pass()
+        return out.reshape(shape)
 
     # ------------------------------------------------------------------ shutdown
     def close(self) -> None:

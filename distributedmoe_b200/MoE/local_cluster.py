@@ -45,7 +45,12 @@ class LocalCluster:
                  dtype: torch.dtype, moe_device: torch.device, eb_devices: Sequence[torch.device],
                  expert_layers: Optional[List[list]] = None, stacked: Optional[list] = None,
                  io_buffer_size: int = 8192, number_of_io_buffers: int = 4, forward_timeout: int = 60000,
-                 p2p_timeout_ms: int = 3000, **options):
+                 p2p_timeout_ms: int = 3000, backend: TensorTransferEngineBackend = TensorTransferEngineBackend.NVLinkIPC,
+                 max_tokens: Optional[int] = None, **options):
+        """backend NVLinkDirect runs forward() as the device-driven exchange with world 1: every
+        block must sit on the host's GPU; the blocks' stacks are concatenated (block order)
+        into the one weight stack the grouped MLP reads; max_tokens (default io_buffer_size *
+        number_of_io_buffers // top_k) sizes the receive window."""
         nb = len(expert_blocks)
         ports = free_ports(1 + 5 * nb)
         host_port, rest = ports[0], ports[1:]
@@ -54,8 +59,11 @@ class LocalCluster:
         eb_p2p = rest[2 * nb:3 * nb]
         host_hc = rest[3 * nb:4 * nb]
         eb_hc = rest[4 * nb:5 * nb]
+        direct = backend == TensorTransferEngineBackend.NVLinkDirect
+        if direct and any(torch.device(d) != torch.device(moe_device) for d in eb_devices):
+            raise ValueError("the single-process device-driven plane needs every block on the host's GPU")
         self.config = DistMoEBlockConfig(
-            backend=TensorTransferEngineBackend.NVLinkIPC, number_of_experts=number_of_experts,
+            backend=backend, number_of_experts=number_of_experts,
             expert_blocks=expert_blocks, number_of_io_buffers=number_of_io_buffers, io_buffer_size=io_buffer_size,
             top_k=top_k, hidden_features=hidden_features, dtype=dtype, moe_device=torch.device(moe_device),
             eb_devices=[torch.device(d) for d in eb_devices], forward_timeout=forward_timeout,
@@ -91,6 +99,16 @@ class LocalCluster:
             transfer_protocol=TransferProtocol.NVLINK, ib_device_names="")
         with torch.cuda.device(self.config.moe_device):
             self.moe = DistMoEBlock(self.config, host_cfg)
+            if direct:
+                if stacked is not None:
+                    stacks = stacked
+                else:
+                    from distributedmoe_b200.MoE.DistExpertsBlock import stack_expert_weights
+                    stacks = [stack_expert_weights(expert_layers[b], self.config.moe_device, dtype) for b in range(nb)]
+                local = stacks[0] if nb == 1 else tuple(torch.cat([st[i] for st in stacks]).contiguous()
+                                                        for i in range(3))
+                mt = max_tokens if max_tokens is not None else max(1, io_buffer_size * number_of_io_buffers // top_k)
+                self.moe.setup_direct_plane(1, 0, [0] * nb, local, mt * top_k, lambda mine: [mine], mt)
 
     def __enter__(self) -> DistMoEBlock:
         return self.moe

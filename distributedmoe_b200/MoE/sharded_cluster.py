@@ -8,11 +8,22 @@ Every rank g owns the experts ``[g*E/G, (g+1)*E/G)`` (its stacked weights) and r
   weights.
 
 So there are G x G expert-block objects in total, and no single host GPU funnels all
-traffic (a star with one host would be bound by that GPU's NVLink egress).  Hosts
-and blocks talk through the NVLink transfer engine: metadata over ZeroMQ between
-processes, activations over NVLink through CUDA-IPC peer buffers (completion notices
-order the accesses).  ``torch.distributed`` (any backend) is used once, to exchange the
-ports of all engines, plus barriers at set-up and shut-down; the data path has no
+traffic (a star with one host would be bound by that GPU's NVLink egress).
+
+Two data planes:
+
+* ``NVLinkDirect`` (default): every rank's forward is device-driven.  The hosts exchange
+  per-expert row counts, their gather kernels store rows straight into the owning GPU's
+  receive window over NVLink (each expert's rows from all hosts contiguous), each GPU runs
+  ONE grouped MLP over everything it received, and each host's combine reads its results
+  back through peer pointers; epoch flags order the steps.  The expert blocks keep answering
+  health checks; no per-task message is sent.  Every rank must call forward once per step.
+* ``NVLinkIPC``: the reference's task protocol, metadata over ZeroMQ between processes and
+  activations copied over NVLink between CUDA-IPC buffers (completion notices order the
+  accesses); one grouped MLP per host task.
+
+``torch.distributed`` (any backend) is used at set-up only: to exchange the engines' ports
+and window descriptors, plus barriers at set-up and shut-down; the data path has no
 collective.
 """
 
@@ -80,28 +91,50 @@ class ShardedCluster:
 
     def __init__(self, number_of_experts: int, top_k: int, hidden_features: int, dtype: torch.dtype,
                  device: torch.device, stacked, group: Optional[dist.ProcessGroup] = None,
-                 io_buffer_size: int = 8192, number_of_io_buffers: int = 2, forward_timeout: int = 60000,
-                 p2p_timeout_ms: int = 3000, address: str = "127.0.0.1", gemm_sm_reserve: int = 8, **options):
-        options.setdefault("dispatch_all_blocks", True)  # one task per GPU's block at once
-        # Each GPU computes other hosts' experts while its own host gathers and combines: keep
-        # a few SMs out of the persistent grouped-MLP launches for those short kernels.
+                 io_buffer_size: Optional[int] = None, number_of_io_buffers: Optional[int] = None,
+                 forward_timeout: int = 60000, p2p_timeout_ms: int = 3000, address: str = "127.0.0.1",
+                 gemm_sm_reserve: Optional[int] = None,
+                 backend: TensorTransferEngineBackend = TensorTransferEngineBackend.NVLinkDirect,
+                 max_tokens: int = 8192, blocks: Optional[List[List[int]]] = None, **options):
+        """stacked: this rank's weight stack for the experts of its block, in block order.
+        blocks[g]: the experts of rank g's block (default: the contiguous E/G of rank g); an
+        expert listed by two ranks is replicated.  max_tokens: tokens per forward of one host
+        (sizes the NVLinkDirect receive windows: G * max_tokens * top_k rows per GPU)."""
+        direct = backend == TensorTransferEngineBackend.NVLinkDirect
+        if direct:
+            # The task buffers only serve the metadata hand-shake: keep them small.
+            io_buffer_size = io_buffer_size or 256
+            number_of_io_buffers = number_of_io_buffers or 1
+            gemm_sm_reserve = 0 if gemm_sm_reserve is None else gemm_sm_reserve
+        else:
+            io_buffer_size = io_buffer_size or 8192
+            number_of_io_buffers = number_of_io_buffers or 2
+            options.setdefault("dispatch_all_blocks", True)  # one task per GPU's block at once
+            # Each GPU computes other hosts' experts while its own host gathers and combines:
+            # keep a few SMs out of the persistent grouped-MLP launches for those short kernels.
+            gemm_sm_reserve = 8 if gemm_sm_reserve is None else gemm_sm_reserve
         N.set_gemm_sm_reserve(gemm_sm_reserve)
         G = dist.get_world_size(group)
         r = dist.get_rank(group)
-        if number_of_experts % G:
-            raise ValueError("number_of_experts must divide evenly over the ranks")
+        if blocks is None:
+            if number_of_experts % G:
+                raise ValueError("number_of_experts must divide evenly over the ranks")
+            blocks = [experts_of_rank(number_of_experts, G, g) for g in range(G)]
+        if len(blocks) != G:
+            raise ValueError("one expert block per rank")
         self.group = group
         self.rank, self.world = r, G
         device = torch.device(device)
         table = exchange_engine_ports(address, device.index, group)
         mine = table[r]
-        blocks = [experts_of_rank(number_of_experts, G, g) for g in range(G)]
         eb_devices = [torch.device("cuda", table[g]["device"]) for g in range(G)]
+        if direct and len({(row["address"], row["device"]) for row in table}) != G:
+            raise ValueError("the device-driven exchange needs one GPU per rank")
 
         def config_of_host(h: int) -> DistMoEBlockConfig:
             # host h's view: block g lives on rank g and uses the ports rank g opened for host h
             return DistMoEBlockConfig(
-                backend=TensorTransferEngineBackend.NVLinkIPC, number_of_experts=number_of_experts,
+                backend=backend, number_of_experts=number_of_experts,
                 expert_blocks=blocks, number_of_io_buffers=number_of_io_buffers, io_buffer_size=io_buffer_size,
                 top_k=top_k, hidden_features=hidden_features, dtype=dtype, moe_device=eb_devices[h],
                 eb_devices=eb_devices, forward_timeout=forward_timeout,
@@ -146,6 +179,16 @@ class ShardedCluster:
             rows = torch.zeros(256, hidden_features, dtype=dtype, device=device)
             N.grouped_gated_mlp(rows, g, u, dn, [0], [256], N.ACT_SILU, torch.empty_like(rows))
             torch.cuda.synchronize(device)
+            if direct:
+                def exchange(desc: bytes) -> List[bytes]:
+                    out: List[bytes] = [b""] * G
+                    dist.all_gather_object(out, desc, group=group)
+                    return out
+
+                self.moe.setup_direct_plane(G, r, list(range(G)), stacked, G * max_tokens * top_k, exchange,
+                                            max_tokens)
+        self.direct = direct
+        self.device = device
         dist.barrier(group=group)  # every host and block of every rank is up before the first forward
 
     def __enter__(self) -> DistMoEBlock:
@@ -155,6 +198,11 @@ class ShardedCluster:
         self.close()
 
     def close(self) -> None:
+        # With the device-driven plane a peer's combine may still read this rank's window:
+        # every rank's GPU work ends before any rank releases its window.
+        if self.direct:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
         # Stop this rank's host (which stops its G blocks on all ranks), then wait until every
         # host has done the same before joining this rank's blocks.
         self.moe.close()

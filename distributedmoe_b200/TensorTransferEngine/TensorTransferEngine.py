@@ -6,7 +6,8 @@ per remote, the 2-byte framed packet format, the synchronous/asynchronous metada
 ``wait_for_transfer_efficient`` and the abstract backend methods.
 
 What changes: the backend enum gains ``NVLinkIPC`` (CUDA IPC peer buffers over NVLink /
-NVSwitch), and the base class no longer imports a transfer library.  The completion monitor
+NVSwitch) and ``NVLinkDirect`` (the same plus a kernel-driven exchange window), and the
+base class no longer imports a transfer library.  The completion monitor
 sleeps while nothing is in flight instead of polling every millisecond, and waiters poll
 their own transfer, so a finished copy is seen within microseconds.
 """
@@ -41,33 +42,38 @@ class TensorTransferEngineBackend(Enum):
     MoonCake = "MoonCake"
     NIXL = "NIXL"
     NVLinkIPC = "NVLinkIPC"
+    # NVLinkIPC plus the device-driven exchange: senders' kernels write rows into the
+    # receivers' buffers over NVLink and epoch flags replace the per-task messages.
+    NVLinkDirect = "NVLinkDirect"
 
 
 @dataclass
 class TensorTransferEngineConfig:
-    # Host part (DistMoEBlock): host, port (for TTE initialization), P2P ports for the P2P communication.
+    # This engine's own endpoint: the address and port that name it, and one local port per
+    # remote on which it pushes metadata packets to that remote.
     host_address: str
     host_port: int
     host_p2p_ports: List[int]
 
-    # Remote parts (DistExpertBlock x N): host, port, P2P ports.
+    # The peers, one entry per remote engine: their addresses, the ports that name them, and
+    # the ports on which they push metadata to this engine.
     remote_addresses: List[str]
     remote_ports: List[int]
     remote_p2p_ports: List[int]
 
-    # P2P send/receive timeout duration in milliseconds.
+    # How long (ms) a metadata send or receive may block before it fails.
     p2p_timeout_duration: int
 
-    # Type of interaction between host and remote while handshaking.
+    # Which side speaks first in the start-up exchange of identities.
     handshake_type: HandshakeType
 
-    # Transfer protocol (via RDMA/NVLink).
+    # Link family the backend moves data over (RDMA or NVLink).
     transfer_protocol: TransferProtocol
 
-    # IB device names for RDMA (unused by the NVLink backend).
+    # InfiniBand adapters for RDMA backends; the NVLink backend ignores it.
     ib_device_names: str
 
-    # MoonCake metadata fields (unused by the NVLink backend).
+    # Settings of MoonCake's metadata service; the NVLink backend ignores them.
     metadata_schema: Optional[str] = None
     metadata_host: Optional[str] = None
     metadata_port: Optional[int] = None

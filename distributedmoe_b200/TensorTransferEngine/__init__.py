@@ -22,4 +22,11 @@ def create_transfer_engine(backend, config):
         from distributedmoe_b200.TensorTransferEngine.NVLinkTensorTransferEngine import NVLinkTensorTransferEngine
 
         return NVLinkTensorTransferEngine(config)
-    raise NotImplementedError(f"transfer backend {backend} is not available in this build; use NVLinkIPC")
+    if backend == TensorTransferEngineBackend.NVLinkDirect:
+        from distributedmoe_b200.TensorTransferEngine.NVLinkDirectTensorTransferEngine import (
+            NVLinkDirectTensorTransferEngine,
+        )
+
+        return NVLinkDirectTensorTransferEngine(config)
+    raise NotImplementedError(f"transfer backend {backend} is not available in this build; use NVLinkIPC "
+                              "or NVLinkDirect")

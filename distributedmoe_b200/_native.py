@@ -29,7 +29,15 @@ DEVERR_NAMES = {
     0x8: "grouped GEMM teardown wait timed out",
     0x10: "completion flag wait timed out",
     0x20: "invalid segment table (clamped)",
+    0x40: "expert-parallel flag wait timed out (a rank fell behind)",
+    0x80: "expert-parallel receive buffer overflow (rows dropped)",
 }
+
+# Expert-parallel exchange (include/dmoe_b200.h, DMOE_EP_*).
+EP_MAX_RANKS, EP_MAX_REPLICAS, EP_MAX_INSTANCES = 16, 4, 1024
+EP_POLICY_ROTATE, EP_POLICY_SPLIT = 0, 1
+EP_FLAG_COUNTS, EP_FLAG_DATA, EP_FLAG_RESULTS = 0, 1, 2
+
 
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
@@ -39,6 +47,14 @@ _i64 = ctypes.c_int64
 _u64 = ctypes.c_uint64
 _f32 = ctypes.c_float
 _sz = ctypes.c_size_t
+
+
+class EpWindow(ctypes.Structure):
+    """``dmoe_ep_window``: every rank's flags, count matrix, receive and output rows, as
+    this process addresses them (its own memory, or CUDA-IPC mappings of the peers')."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("flags", _vp * EP_MAX_RANKS), ("counts", _vp * EP_MAX_RANKS),
+                ("recv", _vp * EP_MAX_RANKS), ("out", _vp * EP_MAX_RANKS)]
 
 # name -> (restype, argtypes); mirrors include/dmoe_b200.h
 SIGNATURES = {
@@ -70,6 +86,16 @@ SIGNATURES = {
     "dmoe_copy": (ctypes.c_int, [_vp, _vp, _sz, _vp]),
     "dmoe_flag_signal": (ctypes.c_int, [_vp, _u64, _vp]),
     "dmoe_flag_wait": (ctypes.c_int, [_vp, _u64, _u64, _vp, _vp]),
+    "dmoe_ep_flags_bytes": (_sz, []),
+    "dmoe_ep_counts_bytes": (_sz, [ctypes.c_int]),
+    "dmoe_ep_plan": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _i64,
+                                    _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "dmoe_ep_dispatch": (ctypes.c_int, [_vp, _vp, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp,
+                                        _vp, _vp, _vp, _i64, _vp, _vp, _u64, _vp, _vp]),
+    "dmoe_ep_wait": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _u64, _vp, _vp]),
+    "dmoe_ep_signal": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _vp]),
+    "dmoe_ep_combine": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_int, _vp, _vp]),
     "dmoe_event_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
     "dmoe_event_destroy": (ctypes.c_int, [_vp]),
     "dmoe_event_record": (ctypes.c_int, [_vp, _vp]),
@@ -373,7 +399,8 @@ def permute_rows(src: torch.Tensor, dst: torch.Tensor, seg_src: Sequence[int], s
 
 
 def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
-                      seg_expert, seg_end, act: int, Y: torch.Tensor, m_rows: Optional[int] = None) -> None:
+                      seg_expert, seg_end, act: int, Y: torch.Tensor, m_rows: Optional[int] = None,
+                      op_name: str = "grouped_gated_mlp") -> None:
     """Grouped expert MLP over row segments.  seg_expert/seg_end: Python int sequences (host
     table) or int32 CUDA tensors (device table)."""
     _require_cuda(X, Y)
@@ -381,12 +408,15 @@ def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
         raise DMoEError("X and Y must be [rows, d]")
     if not (X.dtype == w_gate.dtype == Y.dtype):
         raise DMoEError("grouped MLP operands must share one dtype")
-    grouped_gated_mlp_ptrs(X.data_ptr(), Y.data_ptr(), X.shape[0] if m_rows is None else m_rows, w_gate, w_up, w_down,
-                           seg_expert, seg_end, act)
+    m = X.shape[0] if m_rows is None else m_rows
+    if m > X.shape[0] or m > Y.shape[0]:
+        raise DMoEError("m_rows exceeds the rows of X or Y")
+    grouped_gated_mlp_ptrs(X.data_ptr(), Y.data_ptr(), m, w_gate, w_up, w_down, seg_expert, seg_end, act, op_name)
 
 
 def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Tensor, w_up: torch.Tensor,
-                           w_down: torch.Tensor, seg_expert, seg_end, act: int) -> None:
+                           w_down: torch.Tensor, seg_expert, seg_end, act: int,
+                           op_name: str = "grouped_gated_mlp") -> None:
     """Same as :func:`grouped_gated_mlp` on raw device pointers (rows of d elements of the
     weights' dtype), e.g. a transfer-engine buffer of another block on this GPU."""
     dev = _require_cuda(w_gate, w_up, w_down)
@@ -414,7 +444,7 @@ def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Te
                     rows += end - start
                 start = end
             work = 6.0 * rows * d * I
-    tm = _Timed("grouped_gated_mlp", _stream(dev), dev, work)
+    tm = _Timed(op_name, _stream(dev), dev, work)
     rc = lib().dmoe_grouped_gated_mlp(x_ptr, w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
                                       se, sn, n_seg, on_dev, m_rows, act, y_ptr, ws.data_ptr(), ws.numel(),
                                       scratch.status(dev).data_ptr(), _stream(dev))
@@ -526,6 +556,84 @@ def flag_signal(flag_ptr: int, value: int, stream: int) -> None:
 
 def flag_wait(flag_ptr: int, value: int, timeout_ns: int, status_ptr: int, stream: int) -> None:
     _check(lib().dmoe_flag_wait(flag_ptr, value, timeout_ns, status_ptr, stream), "dmoe_flag_wait")
+
+
+# ----------------------------------------------------------------------------- expert-parallel exchange
+def ep_flags_bytes() -> int:
+    return int(lib().dmoe_ep_flags_bytes())
+
+
+def ep_counts_bytes(n_inst: int) -> int:
+    return int(lib().dmoe_ep_counts_bytes(int(n_inst)))
+
+
+def ep_window(world: int, rank: int, flags: Sequence[int], counts: Sequence[int], recv: Sequence[int],
+              out: Sequence[int]) -> EpWindow:
+    w = EpWindow()
+    w.world, w.rank = int(world), int(rank)
+    for g in range(world):
+        w.flags[g], w.counts[g], w.recv[g], w.out[g] = flags[g], counts[g], recv[g], out[g]
+    return w
+
+
+def ep_plan(win: EpWindow, counts_e: Optional[torch.Tensor], E: int, n_inst: int, policy: int, table, cap: int,
+            epoch: int, timeout_ns: int, out, stream: Optional[int] = None) -> None:
+    """Count exchange and placement.  table: (alive_n, alive_inst, inst_rank, inst_slot,
+    inst_first) int32 device tensors; out: (part_n, part_inst, part_start, dest_off,
+    seg_expert, seg_end) int32 device tensors."""
+    alive_n, alive_inst, inst_rank, inst_slot, inst_first = table
+    part_n, part_inst, part_start, dest_off, seg_expert, seg_end = out
+    dev = alive_n.device
+    st = stream if stream is not None else _stream(dev)
+    tm = _Timed("ep_plan", st, dev)
+    rc = lib().dmoe_ep_plan(ctypes.byref(win), _ptr(counts_e), E, n_inst, policy, alive_n.data_ptr(),
+                            alive_inst.data_ptr(), inst_rank.data_ptr(), inst_slot.data_ptr(), inst_first.data_ptr(),
+                            int(cap), int(epoch), int(timeout_ns), part_n.data_ptr(), part_inst.data_ptr(),
+                            part_start.data_ptr(), dest_off.data_ptr(), seg_expert.data_ptr(), seg_end.data_ptr(),
+                            scratch.status(dev).data_ptr(), st)
+    _check(rc, "dmoe_ep_plan")
+    tm.done()
+
+
+def ep_dispatch(win: EpWindow, x: torch.Tensor, T: int, k: int, E: int, offsets: Optional[torch.Tensor],
+                perm_token: Optional[torch.Tensor], placement, inst_rank: torch.Tensor, cap: int,
+                ret: torch.Tensor, done: torch.Tensor, epoch: int, stream: Optional[int] = None) -> None:
+    """Gather rows into their receivers' buffers (peer stores) and raise the data flags.
+    placement: (part_n, part_inst, part_start, dest_off) from :func:`ep_plan`."""
+    part_n, part_inst, part_start, dest_off = placement
+    dev = inst_rank.device
+    st = stream if stream is not None else _stream(dev)
+    tm = _Timed("ep_dispatch", st, dev)
+    rc = lib().dmoe_ep_dispatch(ctypes.byref(win), _ptr(x), x.shape[-1] * x.element_size(), T, k, E, _ptr(offsets),
+                                _ptr(perm_token), part_n.data_ptr(), part_inst.data_ptr(), part_start.data_ptr(),
+                                inst_rank.data_ptr(), dest_off.data_ptr(), int(cap), ret.data_ptr(), done.data_ptr(),
+                                int(epoch), scratch.status(dev).data_ptr(), st)
+    _check(rc, "dmoe_ep_dispatch")
+    tm.done()
+
+
+def ep_wait(win: EpWindow, kind: int, epoch: int, timeout_ns: int, device: torch.device,
+            stream: Optional[int] = None) -> None:
+    st = stream if stream is not None else _stream(device)
+    _check(lib().dmoe_ep_wait(ctypes.byref(win), kind, int(epoch), int(timeout_ns), scratch.status(device).data_ptr(),
+                              st), "dmoe_ep_wait")
+
+
+def ep_signal(win: EpWindow, kind: int, epoch: int, device: torch.device, stream: Optional[int] = None) -> None:
+    st = stream if stream is not None else _stream(device)
+    _check(lib().dmoe_ep_signal(ctypes.byref(win), kind, int(epoch), st), "dmoe_ep_signal")
+
+
+def ep_combine(win: EpWindow, inverse: Optional[torch.Tensor], ret: torch.Tensor, w: Optional[torch.Tensor],
+               T: int, k: int, out: torch.Tensor, accumulate: bool = False, stream: Optional[int] = None) -> None:
+    dev = out.device
+    st = stream if stream is not None else _stream(dev)
+    tm = _Timed("ep_combine", st, dev)
+    rc = lib().dmoe_ep_combine(ctypes.byref(win), _ptr(inverse), ret.data_ptr(), _ptr(w),
+                               dtype_code(w.dtype) if w is not None else F32, T, k, out.shape[-1],
+                               dtype_code(out.dtype), int(accumulate), out.data_ptr(), st)
+    _check(rc, "dmoe_ep_combine")
+    tm.done()
 
 
 def launch_count() -> int:

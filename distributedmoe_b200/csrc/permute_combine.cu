@@ -131,8 +131,11 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ r
 #pragma unroll
     for (int s = 0; s < KU; ++s) {
       if (s < k) {
-        src[s] = (int64_t)inverse[(int64_t)t * k + s] * d;
-        wt[s] = load_as_float(w, (int64_t)t * k + s, w_dtype);
+        // A negative position marks an activation without an expert row (an invalid expert
+        // index in the plan): it is neither loaded nor added.
+        const int32_t pos = inverse[(int64_t)t * k + s];
+        src[s] = pos < 0 ? -1 : (int64_t)pos * d;
+        wt[s] = pos < 0 ? 0.f : load_as_float(w, (int64_t)t * k + s, w_dtype);
       }
     }
     for (int c0 = lane; c0 < nchunk; c0 += 32 * CU) {
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ r
         const int c = c0 + u * 32;
 #pragma unroll
         for (int s = 0; s < KU; ++s)
-          if (s < k && c < nchunk) raw[u][s] = load_chunk<DT>(rows, src[s] + (int64_t)c * 8);
+          if (s < k && c < nchunk && src[s] >= 0) raw[u][s] = load_chunk<DT>(rows, src[s] + (int64_t)c * 8);
       }
 #pragma unroll
       for (int u = 0; u < CU; ++u) {
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ r
         }
 #pragma unroll
         for (int s = 0; s < KU; ++s) {
-          if (s < k) {
+          if (s < k && src[s] >= 0) {
             float v[8];
             chunk_to_float<DT>(raw[u][s], v);
 #pragma unroll

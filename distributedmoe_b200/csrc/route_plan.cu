@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter(const int64_t* idx,
     const int leader = __ffs(peers) - 1;
     if (e >= 0 && lane == leader) s_wcnt[warp * E + e] = __popc(peers);
     __syncthreads();
+    if (valid && e < 0 && inverse) inverse[(int64_t)t * k + s] = -1;  // no expert: the combine skips it
     if (e >= 0) {
       int pos = s_run[e] + rank_in_warp;
       for (int w2 = 0; w2 < warp; ++w2) pos += s_wcnt[w2 * E + e];
@@ -149,9 +150,15 @@ int32_t* plan_scratch_address(int* rc) {
   static int32_t* addr[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  if (e != cudaSuccess) {
     set_error("dmoe_route_plan_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
     *rc = DMOE_ERR_CUDA;
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("dmoe_route_plan_noalloc: device index %d is outside the %d devices this entry point serves", dev,
+              kMaxDevices);
+    *rc = DMOE_ERR_INVALID;
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);

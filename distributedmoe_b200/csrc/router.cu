@@ -51,13 +51,23 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Arg-max over the warp of (value, index): larger value wins, equal values -> lower index.
+// Selection order of (value, index): NaN ranks above every number (torch.topk treats NaN
+// as the largest value), then larger values, then the lower index.  Every available expert
+// beats the empty candidate (-inf, 0x7fffffff), so each pick is an index in [0, E).
+__device__ __forceinline__ bool ranks_before(float v, int i, float ov, int oi) {
+  const bool n = v != v, on = ov != ov;
+  if (n != on) return n;
+  if (!n && v != ov) return v > ov;
+  return i < oi;
+}
+
+// Arg-max over the warp of (value, index) in the order of ranks_before.
 __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, v, o);
     const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (ov > v || (ov == v && oi < i)) {
+    if (ranks_before(ov, oi, v, i)) {
       v = ov;
       i = oi;
     }
@@ -228,7 +238,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
         float v = gv;
         int i = lane < a.n_group ? lane : 0x7fffffff;
         warp_argmax(v, i);
-        kept |= 1u << i;
+        if (i < 32) kept |= 1u << i;
         if (lane == i) gv = -INFINITY;
       }
 #pragma unroll
@@ -248,7 +258,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
-        if ((avail >> j & 1u) && (sel_val[j] > v || (sel_val[j] == v && e < idx))) {
+        if ((avail >> j & 1u) && ranks_before(sel_val[j], e, v, idx)) {
           v = sel_val[j];
           idx = e;
         }

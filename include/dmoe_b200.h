@@ -51,6 +51,8 @@ extern "C" {
 #define DMOE_DEVERR_TIMEOUT_TEARDOWN 0x8
 #define DMOE_DEVERR_FLAG_TIMEOUT 0x10
 #define DMOE_DEVERR_BAD_SEGMENT 0x20
+#define DMOE_DEVERR_EP_TIMEOUT 0x40  /* an expert-parallel flag wait gave up (a rank fell behind) */
+#define DMOE_DEVERR_EP_OVERFLOW 0x80 /* rows beyond a receive buffer's capacity were dropped */
 
 /* Library identity: returns a static version string. */
 const char* dmoe_version(void);
@@ -103,7 +105,8 @@ int dmoe_router_logits(const void* x, const void* w_r, int dtype, int T, int d, 
  *  counts       [E] int32, offsets [E+1] int32 (exclusive prefix of counts)
  *  perm_token   [T*k] int32 token of each permuted activation
  *  perm_slot    [T*k] int32 slot of each permuted activation (may be NULL)
- *  inverse      [T*k] int32 permuted position of (token t, slot s) at t*k+s (may be NULL)
+ *  inverse      [T*k] int32 permuted position of (token t, slot s) at t*k+s (may be NULL);
+ *               -1 for an activation whose expert index is outside [0, E)
  *  perm_weight  [T*k] weight of each permuted activation in w_dtype (NULL if w is NULL)
  *  workspace    dmoe_route_plan_workspace_size(T, k, E) bytes of device scratch
  *  Limits: 1 <= E <= 1024, T*k < 2^31.
@@ -180,7 +183,8 @@ int dmoe_grouped_mlp_set_sm_reserve(int sms);
 /*
  * Weighted combine (gather form): for each token t
  *     out[t] = sum_s w[t, s] * rows[inverse[t*k + s]]       (fp32 accumulation, one store)
- * `rows` [T*k, d] holds the expert outputs in permuted order.  Replaces the per-expert
+ * `rows` [T*k, d] holds the expert outputs in permuted order; an activation whose inverse
+ * entry is negative adds nothing.  Replaces the per-expert
  * weighted scatter_add_ of HostPipelineTask.combine (MoE/PipelineTask.py:326-346), which
  * accumulates in the model dtype; results agree up to summation order and rounding.
  *  If accumulate != 0, out[t] (dtype) is added to the sum (shared-expert / residual input).
@@ -234,6 +238,92 @@ int dmoe_ipc_event_open(const uint8_t* handle64, int device, void** event_out);
  */
 int dmoe_flag_signal(uint64_t* flag, uint64_t value, void* stream);
 int dmoe_flag_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, int32_t* dev_status, void* stream);
+
+/*
+ * Expert-parallel exchange over NVLink peer memory (the NVLinkDirect transfer backend).
+ * No single reference function: these replace, for ranks that run one forward per step in
+ * lockstep, the per-task protocol of the reference's NIXL/MoonCake path --
+ *   DispatchSubmit metadata (MoE/PipelineTask.py:262-270) -> dmoe_ep_plan (count exchange),
+ *   gather + READ of the input buffer (MoE/PipelineTask.py:231-252,459;
+ *     MoE/pools/BuffersPool.py:55-71) -> dmoe_ep_dispatch (peer stores into the receiver),
+ *   WRITE of the expert output + HostOutputBufferUnlocked (MoE/PipelineTask.py:555-565;
+ *     MoE/pools/BuffersPool.py:73-90) -> dmoe_ep_signal / dmoe_ep_wait (epoch flags),
+ *   HostPipelineTask.combine (MoE/PipelineTask.py:306-370) -> dmoe_ep_combine (peer loads).
+ * Between dmoe_ep_wait(DATA) and dmoe_ep_signal(RESULTS) each rank runs ONE
+ * dmoe_grouped_gated_mlp over its receive buffer with the device segment table that
+ * dmoe_ep_plan wrote (seg_expert, seg_end; n_seg = the rank's instance count).
+ *
+ * Window: per rank, in its own GPU memory and mapped into every rank (CUDA IPC):
+ *   flags   dmoe_ep_flags_bytes() of uint64 epochs [kind][sender], zero-initialised
+ *   counts  dmoe_ep_counts_bytes(n_inst) of int32 [2][DMOE_EP_MAX_RANKS][n_inst]
+ *   recv    [cap, d] rows other ranks dispatch to (instance-major, then sender rank)
+ *   out     [cap, d] the grouped MLP's output rows of recv
+ * The table passed to every call lists all ranks' windows as this process addresses them.
+ * Instances (an expert's weights on one rank) are numbered rank-major; rank r's instances
+ * are [inst_first[r], inst_first[r+1]) in the order of its weight stack (inst_slot).
+ * Epochs: one per forward, equal on all ranks, starting at 1, increasing.  With world == 1
+ * no flags are touched.  Every wait is bounded by timeout_ns and reports
+ * DMOE_DEVERR_EP_TIMEOUT; the rows of a rank that did not answer are left out.
+ * A rank's waits are only ever satisfied by other GPUs: every rank must be its own GPU.
+ */
+#define DMOE_EP_MAX_RANKS 16
+#define DMOE_EP_MAX_REPLICAS 4
+#define DMOE_EP_MAX_INSTANCES 1024
+#define DMOE_EP_POLICY_ROTATE 0 /* all of an expert's rows to one alive instance, rotating per step and rank */
+#define DMOE_EP_POLICY_SPLIT 1  /* an expert's rows split evenly over its alive instances */
+#define DMOE_EP_FLAG_COUNTS 0
+#define DMOE_EP_FLAG_DATA 1
+#define DMOE_EP_FLAG_RESULTS 2
+
+typedef struct dmoe_ep_window {
+  int32_t world, rank;
+  void* flags[DMOE_EP_MAX_RANKS];
+  void* counts[DMOE_EP_MAX_RANKS];
+  void* recv[DMOE_EP_MAX_RANKS];
+  void* out[DMOE_EP_MAX_RANKS];
+} dmoe_ep_window;
+
+size_t dmoe_ep_flags_bytes(void);
+size_t dmoe_ep_counts_bytes(int n_inst);
+
+/*
+ * Count exchange and placement (one CTA).  counts_e [E]: this rank's rows per expert (the
+ * routing plan's counts; NULL for an empty batch).  alive_n [E] / alive_inst
+ * [E][DMOE_EP_MAX_REPLICAS]: the instances this sender may use (its ExpertBlocksPool's
+ * alive blocks, MoE/pools/ExpertBlocksPool.py:37-71); an expert with none has its rows
+ * dropped.  Writes part_n [E], part_inst [E][R], part_start [E][R+1], dest_off [n_inst]
+ * (first receive row of this rank's rows of each instance on the owner) and this rank's
+ * grouped-MLP table seg_expert / seg_end [its instance count].
+ */
+int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, int E, int n_inst, int policy,
+                 const int32_t* alive_n, const int32_t* alive_inst, const int32_t* inst_rank, const int32_t* inst_slot,
+                 const int32_t* inst_first, int64_t cap, uint64_t epoch, uint64_t timeout_ns, int32_t* part_n,
+                 int32_t* part_inst, int32_t* part_start, int32_t* dest_off, int32_t* seg_expert, int32_t* seg_end,
+                 int32_t* dev_status, void* stream);
+
+/*
+ * Gather x[perm_token[p]] of every permuted activation p into its receiver's recv buffer
+ * (peer stores), record ret[p] = (rank << 27) | row (-1: dropped), then raise the DATA flag
+ * of this rank on every rank.  done: a zeroed uint32 of this rank's scratch.
+ */
+int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_t row_bytes, int T, int k, int E,
+                     const int32_t* offsets, const int32_t* perm_token, const int32_t* part_n, const int32_t* part_inst,
+                     const int32_t* part_start, const int32_t* inst_rank, const int32_t* dest_off, int64_t cap,
+                     int32_t* ret, uint32_t* done, uint64_t epoch, int32_t* dev_status, void* stream);
+
+/* Wait (bounded) until every other rank raised its flag of `kind` to `epoch` on this rank. */
+int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t epoch, uint64_t timeout_ns, int32_t* dev_status,
+                 void* stream);
+
+/* Raise this rank's flag of `kind` to `epoch` on every rank after the stream's prior work. */
+int dmoe_ep_signal(const dmoe_ep_window* win, int kind, uint64_t epoch, void* stream);
+
+/*
+ * out[t] = (out[t] if accumulate) + sum_s w[t,s] * out_rows_of(ret[inverse[t*k+s]]), reading
+ * each row from its owner's `out` buffer (peer loads), fp32 accumulation, one store.
+ */
+int dmoe_ep_combine(const dmoe_ep_window* win, const int32_t* inverse, const int32_t* ret, const void* w, int w_dtype,
+                    int T, int k, int d, int dtype, int accumulate, void* out, void* stream);
 
 /* Number of kernels this library launched in this process (for launch accounting). */
 uint64_t dmoe_launch_count(void);

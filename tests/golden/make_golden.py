@@ -1,7 +1,8 @@
 """Generate golden vectors by running the reference's own code on CPU.
 
-Usage (in a container where the reference is mounted):
-    python tests/golden/make_golden.py [/path/to/reference]
+Usage (in a container where the reference's source tree is available):
+    python tests/golden/make_golden.py /path/to/reference
+    DISTRIBUTEDMOE_REFERENCE=/path/to/reference python tests/golden/make_golden.py
 
 The reference (slivanovich/DistributedMoE) is pure Python.  Its transfer libraries (nixl,
 mooncake) are absent here, so they are replaced by empty stub modules; its data path is
@@ -300,7 +301,9 @@ def run_config(cfg):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DISTRIBUTEDMOE_REFERENCE")
+    if not ref:
+        raise SystemExit("usage: make_golden.py /path/to/reference  (or set DISTRIBUTEDMOE_REFERENCE)")
     _install_stubs(os.path.join(ref, "src", "python"))
     cwd = os.getcwd()
     os.chdir("/tmp")  # the reference's logging may create ./logs

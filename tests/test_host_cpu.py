@@ -184,11 +184,10 @@ def test_bench_workloads():
     mix, ds = bench.WORKLOADS["mixtral"], bench.WORKLOADS["deepseek"]
     # weak scaling: tokens per GPU fixed; strong: the step's tokens split over the GPUs
     assert mix.tokens_per_rank(8) == 4096 and ds.tokens_per_rank(8) == 1024
-    assert mix.mlp_flops(4096) == 6.0 * 4096 * 2 * 4096 * 14336
-    assert ds.mlp_flops(8192) == pytest.approx(6.0 * 8192 * 8 * 7168 * 2048 + 6.0 * 8192 * 7168 * 2048)
+    assert mix.mlp_flops(4096 * 2) == 6.0 * 4096 * 2 * 4096 * 14336
     qwen = bench.WORKLOADS["qwen3-decode"]
     assert qwen.E == 128 and qwen.k == 8 and qwen.strong
-    # one host's buffers: every activation fits one wave; packet fields stay 16-bit
+    # one host's task buffers: every activation fits one wave; packet fields stay 16-bit
     for w in (mix, ds, qwen):
         for world in (1, 2, 4, 8):
             par = "experts" if world > 1 else "single"
@@ -199,9 +198,23 @@ def test_bench_workloads():
                 assert size * n >= per_host
             else:
                 assert n == 2 * world and size >= per_host // world
-            c = w.config(world, par)
+            c = w.config(world, par, "tasks")
             assert c["io_buffer_size"] == size and c["io_buffers"] == n
             assert c["tokens_per_gpu"] * world == c["tokens_per_step"]
+            c = w.config(world, par, "direct")
+            assert c["transfer_engine"] == "NVLinkDirect" and "io_buffer_size" not in c
+            blocks, ranks = w.blocks(world)
+            assert ranks == list(range(world)) and sorted(e for b in blocks for e in b) == list(range(w.E))
+    # skewed fault tolerance: every expert in exactly two blocks, on two different GPUs
+    ft = bench.WORKLOADS["skewed-ft"]
+    for world in (1, 2, 4, 8):
+        blocks, ranks = ft.blocks(world)
+        for e in range(ft.E):
+            holders = [b for b, experts in enumerate(blocks) if e in experts]
+            assert len(holders) == 2
+            if world > 1:
+                assert ranks[holders[0]] != ranks[holders[1]]
+    assert ft.tokens_per_rank(8) == 2048 and ft.fail_block == 3
 
 
 # ----------------------------------------------------------------------------- health checks
