@@ -78,6 +78,13 @@ def exchange_engine_ports(address: str, device_index: int, group: Optional[dist.
     raise RuntimeError("could not pick distinct engine ports on all ranks")
 
 
+def gather_window_descriptors(mine: bytes, group: Optional[dist.ProcessGroup] = None) -> List[bytes]:
+    """Every rank's NVLinkDirect window descriptor, in rank order (one all-gather at set-up)."""
+    out: List[bytes] = [b""] * dist.get_world_size(group)
+    dist.all_gather_object(out, mine, group=group)
+    return out
+
+
 def experts_of_rank(number_of_experts: int, world: int, rank: int) -> List[int]:
     per = number_of_experts // world
     return list(range(rank * per, (rank + 1) * per))
@@ -180,13 +187,8 @@ class ShardedCluster:
             N.grouped_gated_mlp(rows, g, u, dn, [0], [256], N.ACT_SILU, torch.empty_like(rows))
             torch.cuda.synchronize(device)
             if direct:
-                def exchange(desc: bytes) -> List[bytes]:
-                    out: List[bytes] = [b""] * G
-                    dist.all_gather_object(out, desc, group=group)
-                    return out
-
-                self.moe.setup_direct_plane(G, r, list(range(G)), stacked, G * max_tokens * top_k, exchange,
-                                            max_tokens)
+                self.moe.setup_direct_plane(G, r, list(range(G)), stacked, G * max_tokens * top_k,
+                                            lambda mine: gather_window_descriptors(mine, group), max_tokens)
         self.direct = direct
         self.device = device
         dist.barrier(group=group)  # every host and block of every rank is up before the first forward

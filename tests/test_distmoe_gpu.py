@@ -121,3 +121,52 @@ def test_local_sparse_moe_block_matches_oracle():
     _, _, logits = N.router(inp.x.to(DEV), inp.w_r.to(DEV), k, want_logits=True)
     ref = O.local_experts(inp.x, logits.cpu(), inp.gate, inp.up, inp.down, k, act=O.ACT_SILU, compute_dtype=torch.float32)
     assert _rel_l2(y.view(T, d).float().cpu(), ref) < 1e-2
+
+
+@gpu
+def test_forward_timeout_returns_partial_result(monkeypatch):
+    """A block that silently drops its task (no output, no acknowledgement, but still answers
+    health checks) makes the host wait until forward_timeout and return the partial result:
+    every token keeps the contributions of the experts whose tasks came back and loses those
+    of the silent block's experts (the reference's SLA path, MoE/DistMoEBlock.py:709-718)."""
+    import time
+
+    from distributedmoe_b200 import _native as N
+    from distributedmoe_b200.MoE import PipelineTask as PT
+    from distributedmoe_b200.MoE.local_cluster import LocalCluster
+
+    real_run = PT.ExpertsBlockPipelineTask.run
+
+    async def run(self, experts_block_index, *a, **kw):
+        if experts_block_index == 1:
+            self.close()
+            return  # the task is lost: nothing computed, nothing acknowledged
+        return await real_run(self, experts_block_index, *a, **kw)
+
+    monkeypatch.setattr(PT.ExpertsBlockPipelineTask, "run", run)
+    T, d, E, k, I = 400, 128, 8, 2, 256
+    inp = make_layer_inputs(T, d, E, I, 21, torch.bfloat16)
+    layers = _layers(inp, E, torch.bfloat16)
+    blocks = [[0, 1, 2, 3], [4, 5, 6, 7]]
+    cl = LocalCluster(E, blocks, k, d, torch.bfloat16, DEV, [DEV, DEV],
+                      expert_layers=[[layers[e] for e in b] for b in blocks], io_buffer_size=1024,
+                      number_of_io_buffers=4, activation="silu", renormalize=True, forward_timeout=1500)
+    try:
+        with torch.no_grad():
+            cl.moe.gate.weight.copy_(inp.w_r.to(DEV))
+        t0 = time.monotonic()
+        y = cl.moe(inp.x.to(DEV))
+        waited = time.monotonic() - t0
+        torch.cuda.synchronize()
+        N.check_device_status(DEV)
+    finally:
+        cl.close()
+    assert waited >= 1.0, "the host returned before its forward timeout"
+    _, _, logits = N.router(inp.x.to(DEV), inp.w_r.to(DEV), k, want_logits=True)
+    down = inp.down.clone()
+    down[4:] = 0  # the silent block's experts contribute nothing
+    ref = O.local_experts(inp.x, logits.cpu(), inp.gate, inp.up, down, k, act=O.ACT_SILU, renormalize=True,
+                          compute_dtype=torch.float32)
+    yy = y.float().cpu()
+    assert _rel_l2(yy, ref) < 1e-2
+    assert (yy - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())

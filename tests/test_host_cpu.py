@@ -301,3 +301,202 @@ def test_health_checker_marks_a_silent_block_dead_then_alive_and_aborts_its_task
     assert task.aborted
     assert blk.transferred_activations == [0] and blk.active_pipeline_tasks == [0]
     assert blk.expert_block_tasks[0] == [] and b"t" not in blk.pipeline_tasks
+
+
+# ----------------------------------------------------------------------------- wire format
+class _FakeStream:
+    cuda_stream = 0
+
+    def wait_event(self, ev):
+        pass
+
+
+class _FakeBuffer:
+    def __init__(self, i):
+        self.id = i.to_bytes(length=2, byteorder="big")
+        self.cuda_stream = _FakeStream()
+        self.data = None
+
+    def begin_use(self, s):
+        pass
+
+    def end_use(self, s):
+        pass
+
+
+class _FakePool:
+    def __init__(self, size, first_id):
+        self.buffer_size = size
+        self._next = first_id
+
+    async def acquire(self):
+        self._next += 1
+        return self._next, _FakeBuffer(self._next)
+
+    def release(self, i):
+        pass
+
+
+class _CaptureEngine:
+    def __init__(self, blocks):
+        self.remote_names = [f"block-{b}" for b in range(blocks)]
+        self.sent = []
+
+    async def async_send_metadata_to(self, remote_name, header, body):
+        self.sent.append((remote_name, header, body))
+
+
+class _FakeEvent:
+    def record(self, s=None):
+        pass
+
+
+@pytest.mark.parametrize("name", ["tiny_e8k2", "split_2blocks", "align_pad", "topk1", "replicas", "e16k4_sparse",
+                                  "plumbing"])
+def test_product_dispatch_packets_match_reference_bytes(name, monkeypatch):
+    """The product's own HostPipelineTask.dispatch (not the oracle's encoder) produces, wave
+    by wave, the reference's DispatchSubmit packets byte for byte (golden packets recorded
+    from the reference's code), apart from the random task name and the buffer ids."""
+    from distributedmoe_b200 import _native as N
+    from distributedmoe_b200.MoE.DistMoE import ExpertMetaData, SegmentQueue
+    from distributedmoe_b200.MoE.PipelineTask import ForwardState, HostPipelineTask
+    from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import TensorTransferEngine
+
+    g = torch.load(os.path.join(os.path.dirname(__file__), "golden", name + ".pt"), weights_only=False)
+    cfg = g["config"]
+    E, blocks, io, k, T = cfg["E"], cfg["blocks"], cfg["io"], cfg["k"], cfg["T"]
+    monkeypatch.setattr(N, "permute_rows", lambda *a, **kw: None)
+    monkeypatch.setattr(torch.cuda, "Event", _FakeEvent)
+    counts = [0] * E
+    for e, pe in g["per_expert"].items():
+        counts[e] = pe["tokens"].numel()
+    plan = {"perm_token": torch.zeros(max(sum(counts), 1), dtype=torch.int32)}
+    md = {}
+    base = 0
+    for e in range(E):
+        md[e] = ExpertMetaData([b for b in range(len(blocks)) if e in blocks[b]], 0, None, None, 0, SegmentQueue())
+        if counts[e]:
+            md[e].bind(plan, base, counts[e])
+        base += counts[e]
+    hit = [e for e in range(E) if counts[e]]
+    pool = ExpertBlocksPool(blocks)
+    engine = _CaptureEngine(len(blocks))
+    fs = ForwardState(None, plan, [0] * (E + 1), None, None, None)
+    candidates = list(range(io // 1024, io, io // 1024)) + [io] if cfg["align"] else None
+    transferred, active = [0], [0]
+    tasks_of_block = {}
+
+    async def waves():
+        lock = asyncio.Lock()
+        while transferred[0] < k * T:
+            n = max(-(-(k * T - transferred[0]) // io), 1)
+            for _ in range(n):  # a wave's tasks run in creation order
+                t = HostPipelineTask(engine, _FakePool(io, 0), _FakePool(io, 100), hit, pool, md, lock,
+                                     forward_state=fs)
+                await t.dispatch(None, active, transferred, tasks_of_block, candidates, True)
+
+    asyncio.new_event_loop().run_until_complete(waves())
+    sent = [(r, TensorTransferEngine.serialize_p2p_packet(None, h, body)) for r, h, body in engine.sent]
+    assert len(sent) == len(g["tasks"])
+    for (remote, pkt), ref in zip(sent, g["tasks"]):
+        assert remote == f"block-{ref['block']}"
+        assert pkt[:6] == ref["packet"][:6]            # header 1038, item count, name length
+        assert pkt[14:-8] == ref["packet"][14:-8]      # grouped-gemm flag, expert count, segments
+        assert len(pkt) == len(ref["packet"])          # same two 2-byte buffer ids at the end
+
+
+# ----------------------------------------------------------------------------- direct plane host logic
+def test_instance_table_layout_and_alive_lists():
+    from distributedmoe_b200.MoE.instances import InstanceTable
+    blocks = [[0, 1], [2, 3], [1, 2], [3, 0]]
+    t = InstanceTable.from_blocks(blocks, [0, 1, 0, 1], 2, 4)
+    # rank-major, each rank's blocks in index order, each block's experts in list order
+    assert t.inst_rank == [0, 0, 0, 0, 1, 1, 1, 1]
+    assert t.inst_expert == [0, 1, 1, 2, 2, 3, 3, 0]
+    assert t.inst_slot == [0, 1, 2, 3, 0, 1, 2, 3]
+    assert t.inst_first == [0, 4, 8] and t.local_blocks(0) == [0, 2] and t.local_blocks(1) == [1, 3]
+    n, inst = t.alive_arrays([True, True, True, True])
+    R = 4
+    assert n == [2, 2, 2, 2]
+    assert inst[0 * R:0 * R + 2] == [0, 7] and inst[1 * R:1 * R + 2] == [1, 2]
+    n, inst = t.alive_arrays([True, False, True, True])  # block 1 (experts 2, 3 on rank 1) lost
+    assert n == [2, 2, 1, 1] and inst[2 * R] == 3 and inst[3 * R] == 6
+    with pytest.raises(ValueError):
+        InstanceTable.from_blocks([[0, 1]] * 5, [0] * 5, 1, 2)  # five replicas of an expert
+    with pytest.raises(ValueError):
+        InstanceTable.from_blocks([[0, 9]], [0], 1, 4)
+
+
+def test_placement_restatement_properties():
+    """oracle/ep_placement.py: every sender's rows of an instance form one contiguous run of
+    the owner's buffer, senders in rank order, instances in stack order, nothing overlaps, and
+    each owner's segment table ends where its rows end."""
+    import random
+
+    from oracle import ep_placement as P
+    rng = random.Random(0)
+    E, G = 6, 3
+    inst_rank = [0, 0, 0, 1, 1, 2, 2, 2]
+    inst_first = [0, 3, 5, 8]
+    inst_expert = [0, 1, 2, 3, 4, 5, 0, 1]
+    for policy in (P.POLICY_ROTATE, P.POLICY_SPLIT):
+        for epoch in (1, 2, 7):
+            counts = [[rng.randrange(0, 50) for _ in range(E)] for _ in range(G)]
+            alive = [[[i for i, e2 in enumerate(inst_expert) if e2 == e] for e in range(E)] for _ in range(G)]
+            alive[1][0] = alive[1][0][:1]  # rank 1 sees one of expert 0's replicas as dead
+            res = P.placement(counts, alive, inst_rank, inst_first, policy, epoch, cap=10**6)
+            for g in range(G):
+                used = set()
+                for r in range(G):
+                    for i in range(inst_first[g], inst_first[g + 1]):
+                        rows = range(res["dest_off"][r][i], res["dest_off"][r][i] + res["M"][r][i])
+                        assert not used & set(rows)
+                        used |= set(rows)
+                assert used == set(range(sum(res["tot"][inst_first[g]:inst_first[g + 1]])))
+                assert res["seg_end"][g][-1] == len(used)
+            for r in range(G):
+                for e in range(E):
+                    assert sum(hi - lo for _i, lo, hi in res["parts"][r][e]) == counts[r][e]
+                dest = P.destinations(counts[r], res["parts"][r], inst_rank, res["dest_off"][r], 10**6)
+                assert len(dest) == sum(counts[r]) and all(g >= 0 for g, _ in dest)
+
+
+def _window_worker(rank, world, port, results):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from distributedmoe_b200.MoE.instances import InstanceTable
+    from distributedmoe_b200.MoE.sharded_cluster import gather_window_descriptors
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        descs = gather_window_descriptors(struct.pack("!Q", 1000 + rank) + bytes([rank]) * 5)
+        t = InstanceTable.from_blocks([[0, 1], [1, 2], [2, 0]][:world], list(range(world)), world, 3)
+        results.put((rank, descs, t.inst_rank, t.inst_slot, t.inst_first))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_window_descriptors_and_instance_tables_agree_over_two_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_window_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            rank, *rest = results.get(timeout=120)
+            out[rank] = rest
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert out[0] == out[1]
+    descs = out[0][0]
+    assert [struct.unpack("!Q", d[:8])[0] for d in descs] == [1000, 1001]

@@ -357,3 +357,46 @@ def test_flag_signal_then_wait_and_bounded_timeout():
     assert int(status.item()) & 0x10
     y = torch.ones(4, device=dev) * 3  # the context still works
     assert float(y.sum().item()) == 12.0
+
+
+@gpu
+def test_router_nan_logits_pick_valid_experts():
+    """A NaN logit ranks first (torch.topk's order) and every pick stays in [0, E), in both
+    router modes; a NaN token's weights are NaN, the other tokens are unaffected."""
+    from distributedmoe_b200 import _native as N
+    T, E, k = 64, 32, 4
+    g = torch.Generator(device=DEV).manual_seed(3)
+    logits = torch.randn(T, E, generator=g, device=DEV)
+    logits[5, 7] = float("nan")
+    logits[9, :] = float("nan")
+    for mode, kw in ((N.ROUTER_SOFTMAX, {}), (N.ROUTER_SIGMOID_GROUP, dict(n_group=4, topk_group=2))):
+        idx, w, _ = N.router(None, None, k, logits_in=logits.contiguous(), mode=mode, renormalize=True,
+                             w_dtype=torch.float32, **kw)
+        torch.cuda.synchronize()
+        assert idx.min().item() >= 0 and idx.max().item() < E
+        assert idx[5, 0].item() == 7
+        assert torch.isnan(w[9]).all()
+        ok = [t for t in range(T) if t not in (5, 9)]
+        assert torch.isfinite(w[ok]).all()
+
+
+@gpu
+def test_layer_with_a_nan_token_keeps_other_tokens_finite():
+    """A NaN in one token's activations reaches only that token's output row: its rows are
+    routed to valid experts and every expert row and plan entry stays in bounds."""
+    from distributedmoe_b200 import _native as N
+    from distributedmoe_b200.MoE.MoE import moe_layer_forward
+    T, d, E, k, I = 200, 128, 8, 2, 256
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn(T, d, generator=g, device=DEV).to(torch.bfloat16)
+    x[17, 3] = float("nan")
+    w_r = (torch.randn(E, d, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    gate = (torch.randn(E, I, d, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    up = (torch.randn(E, I, d, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    down = (torch.randn(E, d, I, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    y = moe_layer_forward(x, w_r, gate, up, down, k, activation=N.ACT_SILU, renormalize=True)
+    torch.cuda.synchronize()
+    N.check_device_status(DEV)
+    assert torch.isnan(y[17]).all()
+    rest = torch.cat([y[:17], y[18:]])
+    assert torch.isfinite(rest).all()

@@ -87,3 +87,19 @@ def test_combine_from_permuted_matches_per_expert_scatter():
         rows = y_perm[b:b + int(plan.counts[e])].double()
         ref.index_add_(0, plan.token_indexes[e], rows * plan.weights[e].double())
     assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-5)
+
+
+def test_nan_logit_row_routes_to_valid_experts():
+    """A token whose logits hold a NaN still gets k expert indices in [0, E) from torch.topk
+    (the softmax spreads the NaN over the whole row, so which k it picks is not specified);
+    its weights are NaN and only its own output row turns NaN."""
+    E, k = 8, 2
+    logits = torch.randn(4, E)
+    logits[1, 3] = float("nan")
+    logits[2, :] = float("nan")
+    w, sel = O.route(logits, k, torch.float32)
+    assert sel.min().item() >= 0 and sel.max().item() < E
+    assert torch.isnan(w[1]).all() and torch.isnan(w[2]).all()
+    assert torch.isfinite(w[0]).all() and torch.isfinite(w[3]).all()
+    plan = O.route_plan(sel, w, E)
+    assert sorted(plan.inverse.flatten().tolist()) == list(range(4 * k))
