@@ -473,6 +473,52 @@ def _op_stats(krecs, name, steps):
     return {"launches_per_step": len(recs) / steps, "ms_per_launch": statistics.mean(ms), "ms_total": sum(ms)}
 
 
+def _e2e_pipelined(moe, x_host, dev, stream, steps, dist) -> float:
+    """ms per step of `steps` forwards fed from pinned host memory and read back to pinned
+    host memory, with the copies on their own streams (double-buffered on both sides)."""
+    copy_in = torch.cuda.Stream(device=dev)
+    copy_out = torch.cuda.Stream(device=dev)
+    xd = [torch.empty(x_host.shape, dtype=x_host.dtype, device=dev) for _ in range(2)]
+    y_host = [torch.empty(x_host.shape, dtype=x_host.dtype).pin_memory() for _ in range(2)]
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]  # the layer finished reading xd[i]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+
+    def run(n, t0=None):
+        for i in range(2):
+            used[i].record(stream)
+            out_done[i].record(copy_out)
+        if t0 is not None:
+            t0.record(stream)
+        copy_in.wait_stream(stream)
+        copy_out.wait_stream(stream)
+        for s in range(n):
+            b = s % 2
+            copy_in.wait_event(used[b])
+            with torch.cuda.stream(copy_in):
+                xd[b].copy_(x_host, non_blocking=True)
+                in_done[b].record(copy_in)
+            stream.wait_event(in_done[b])
+            y = moe(xd[b])
+            used[b].record(stream)
+            copy_out.wait_event(used[b])
+            copy_out.wait_event(out_done[b])  # y_host[b] is free again
+            with torch.cuda.stream(copy_out):
+                y_host[b].copy_(y, non_blocking=True)
+                out_done[b].record(copy_out)
+            y.record_stream(copy_out)
+        stream.wait_stream(copy_out)
+
+    run(2)
+    _barrier(dist, dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    run(steps, t0)
+    t1.record(stream)
+    _barrier(dist, dev)
+    return _max_over_ranks(dist, t0.elapsed_time(t1) / steps, dev)
+
+
 def run_ours(args, dist, rank, world, local_rank):
     from distributedmoe_b200 import _native as N
 
@@ -527,6 +573,8 @@ def run_ours(args, dist, rank, world, local_rank):
         N.check_device_status(dev)
 
         # ---------------------------------------------------------- e2e: pinned host in/out
+        # Serial: every step copies its tokens in, runs the layer and copies the result out
+        # on one stream.
         for _ in range(2):
             y = moe(x_host.to(dev, non_blocking=True))
             y_host.copy_(y, non_blocking=True)
@@ -540,7 +588,11 @@ def run_ours(args, dist, rank, world, local_rank):
             y_host.copy_(y, non_blocking=True)
         e1.record(stream)
         _barrier(dist, dev)
-        e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / args.steps, dev)
+        e2e_serial_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / args.steps, dev)
+        # Pipelined (a serving loop): the same copies on two copy streams, so step i+1's H2D
+        # and step i-1's D2H overlap step i's layer (PCIe runs both directions at once).
+        # Every copy of every step is inside the timed region.
+        e2e_ms = _e2e_pipelined(moe, x_host, dev, stream, args.steps, dist)
         N.check_device_status(dev)
 
         ft_report = None
@@ -616,7 +668,11 @@ def run_ours(args, dist, rank, world, local_rank):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": w.config(world, parallel, args.data_plane), "impl": "ours",
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": total_tokens * D * 2, "d2h_bytes_per_step": total_tokens * D * 2},
+                "h2d_bytes_per_step": total_tokens * D * 2, "d2h_bytes_per_step": total_tokens * D * 2,
+                "copies": "pinned host in/out every step; H2D of step i+1 and D2H of step i-1 on two copy "
+                          "streams overlapping step i",
+                "serial": {"value": total_tokens / (e2e_serial_ms * 1e-3), "ms_per_step": e2e_serial_ms,
+                           "copies": "H2D, layer, D2H back to back on one stream"}},
         "gpu_launches": launches,
         "roofline": roof,
         "op_us": op_us,

@@ -11,6 +11,7 @@
 //   2. plan_scan    : counts, offsets, and base[c][e] = offsets[e] + sum_{c'<c} hist[c'][e]
 //   3. plan_scatter : each chunk ranks its activations stably (warp match + per-warp
 //                     prefix) and writes perm_token / perm_slot / inverse / perm_weight.
+#include <cstdlib>
 #include <mutex>
 
 #include "dmoe_common.cuh"
@@ -136,6 +137,130 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter(const int64_t* idx,
   }
 }
 
+// Small plans (T*k <= kSingleMax, E <= kSingleMaxE) in one CTA of 1024 threads, one launch
+// instead of three: the expert of every activation is read once into shared memory (int16)
+// while the histogram builds; one block-wide scan gives counts and offsets; then rounds of
+// 1024 consecutive activations (in the slot-major order f = s*T + t) are ranked stably:
+// within a warp by __match_any_sync, across the round's warps by a per-expert scan of the
+// per-warp counts, and across rounds by a running position per expert.  The order is the
+// multi-CTA path's, element for element.
+constexpr int kSingleMax = 32768;
+constexpr int kSingleMaxE = 256;
+constexpr int kSingleThreads = 1024;
+
+__global__ void __launch_bounds__(kSingleThreads, 1)
+    plan_single(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E, int32_t* counts,
+                int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse, void* perm_weight) {
+  extern __shared__ __align__(16) int32_t sm[];
+  int32_t* s_run = sm;                          // [E] running position of each expert
+  int32_t* s_wc = sm + kSingleMaxE;             // [32][E] per-warp counts, then their prefixes
+  int16_t* s_e = reinterpret_cast<int16_t*>(s_wc + 32 * E);  // [n] expert of each activation (-1: none)
+  __shared__ int32_t s_warp[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = T * k;
+  for (int e = tid; e < E; e += kSingleThreads) s_run[e] = 0;
+  __syncthreads();
+  // 1. experts of all activations (eight loads in flight per thread) and the histogram
+  for (int f0 = tid; f0 < n; f0 += 8 * kSingleThreads) {
+    int64_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = f0 + u * kSingleThreads;
+      v[u] = -1;
+      if (f < n) {
+        const int s = f / T, t = f - (f / T) * T;
+        v[u] = idx[(int64_t)t * k + s];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = f0 + u * kSingleThreads;
+      if (f < n) {
+        const int e = (v[u] >= 0 && v[u] < E) ? (int)v[u] : -1;
+        s_e[f] = (int16_t)e;
+        if (e >= 0) atomicAdd(&s_run[e], 1);
+      }
+    }
+  }
+  __syncthreads();
+  // 2. counts and exclusive offsets (E <= 1024: one expert per thread)
+  const int32_t c = tid < E ? s_run[tid] : 0;
+  int32_t incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t wv = s_warp[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, wv, o);
+      if (lane >= o) wv += u;
+    }
+    s_warp[lane] = wv;
+  }
+  __syncthreads();
+  const int32_t excl = incl - c + (warp > 0 ? s_warp[warp - 1] : 0);
+  if (tid < E) {
+    counts[tid] = c;
+    offsets[tid] = excl;
+    s_run[tid] = excl;
+    if (tid == E - 1) offsets[E] = excl + c;
+  }
+  // 3. stable ranks, one round of 1024 consecutive activations at a time
+  for (int r0 = 0; r0 < n; r0 += kSingleThreads) {
+    for (int i = tid; i < 32 * E; i += kSingleThreads) s_wc[i] = 0;
+    __syncthreads();
+    const int f = r0 + tid;
+    const int e = f < n ? (int)s_e[f] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && lane == __ffs(peers) - 1) s_wc[warp * E + e] = __popc(peers);
+    __syncthreads();
+    // per expert: exclusive scan of the 32 warps' counts, offset by the running position
+    for (int ee = warp; ee < E; ee += 32) {
+      const int32_t wc = s_wc[lane * E + ee];
+      int32_t in = wc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t u = __shfl_up_sync(0xffffffffu, in, o);
+        if (lane >= o) in += u;
+      }
+      const int32_t run = s_run[ee];
+      s_wc[lane * E + ee] = run + in - wc;
+      __syncwarp();
+      if (lane == 31) s_run[ee] = run + in;
+    }
+    __syncthreads();
+    if (f < n) {
+      const int s = f / T, t = f - (f / T) * T;
+      if (e >= 0) {
+        const int pos = s_wc[warp * E + e] + rank_in_warp;
+        perm_token[pos] = t;
+        if (perm_slot) perm_slot[pos] = s;
+        if (inverse) inverse[(int64_t)t * k + s] = pos;
+        if (perm_weight) store_from_float(perm_weight, pos, load_as_float(w, (int64_t)t * k + s, w_dtype), w_dtype);
+      } else if (inverse) {
+        inverse[(int64_t)t * k + s] = -1;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+size_t plan_single_smem(int T, int k, int E) {
+  return (size_t)(kSingleMaxE + 32 * E) * sizeof(int32_t) + (((size_t)T * k * sizeof(int16_t) + 15) & ~size_t(15));
+}
+
+bool plan_single_eligible(int T, int k, int E) {
+  const char* v = getenv("DMOE_PLAN_SINGLE");
+  if (v && v[0] == '0') return false;
+  return (int64_t)T * k <= kSingleMax && E <= kSingleMaxE;
+}
+
 // Scratch of dmoe_route_plan_noalloc: the per-chunk histogram matrix lives in this
 // library-owned device array instead of caller memory.  Every GPU that loads the library
 // holds it until the process exits.
@@ -197,6 +322,21 @@ extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, i
   DMOE_REQUIRE(workspace_bytes >= dmoe_route_plan_workspace_size(T, k, E), "dmoe_route_plan: workspace too small");
   cudaStream_t s = as_stream(stream);
   const int64_t n = (int64_t)T * k;
+  if (plan_single_eligible(T, k, E)) {
+    static PerDeviceOnce once;
+    int dev = 0;
+    DMOE_CUDA(cudaGetDevice(&dev));
+    const int r = once_per_device(once, dev, [] {
+      DMOE_CUDA(cudaFuncSetAttribute(plan_single, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)plan_single_smem(kSingleMax, 1, kSingleMaxE)));
+      return DMOE_OK;
+    });
+    if (r) return r;
+    plan_single<<<1, kSingleThreads, plan_single_smem(T, k, E), s>>>(idx, w, w_dtype, T, k, E, counts, offsets,
+                                                                      perm_token, perm_slot, inverse, perm_weight);
+    DMOE_LAUNCH_CHECK();
+    return DMOE_OK;
+  }
   const int chunks = n > 0 ? (int)((n + kChunk - 1) / kChunk) : 0;
   int32_t* hist = reinterpret_cast<int32_t*>(workspace);
   if (chunks > 0) {

@@ -6,6 +6,8 @@
 // One warp owns one token: the dot products with the E router rows are split over the
 // lanes in 16-byte chunks of the token's row and reduced with shuffles; selection is k
 // rounds of a warp arg-max (ties resolve to the lower expert index).
+#include <cstdlib>
+
 #include "dmoe_common.cuh"
 
 namespace dmoe {
@@ -289,6 +291,205 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
   }
 }
 
+// ------------------------------------------------------------------------- few experts
+// Softmax router for E <= 16 experts and 16-bit inputs (the Mixtral-style router).  One
+// persistent CTA per SM; its warps split the hidden dimension (warp w owns V runs of 512
+// contiguous bytes of every row) and each lane keeps its columns of all E router rows in
+// registers for the whole kernel, so the weights are read once per CTA.  Tiles of
+// consecutive tokens (contiguous in x) stream into a 4-stage shared-memory ring through
+// bulk async copies that complete on mbarriers: several tiles are in flight per SM
+// independent of the register budget.  Per tile, each warp reduces its E partial dot
+// products per token, and one thread per token sums the warps' partials in a fixed order,
+// adds the logit bias and does the softmax and top-k (same order as the warp kernel: NaN
+// first, then larger, then lower index).
+constexpr int kSmallStages = 4;
+constexpr int kSmallStageBytes = 32 * 1024;
+constexpr int kSmallMaxTile = 16;
+constexpr uint64_t kSmallWaitNs = 2000000000ull;
+
+template <int DT, int EP, int V>
+__global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a, int tile_t, int n_tiles) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int nw = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row_bytes = (int64_t)a.d * 2;
+  uint8_t* ring = smem_raw;
+  float* s_part = reinterpret_cast<float*>(smem_raw + kSmallStages * kSmallStageBytes);  // [2][tile][nw][EP]
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_part + 2 * tile_t * nw * EP);
+
+  uint4 wreg[EP][V];
+#pragma unroll
+  for (int e = 0; e < EP; ++e)
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int64_t col = ((int64_t)(warp * V + j) * 32 + lane) * 8;
+      wreg[e][j] = e < a.E ? *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.w_r) + ((int64_t)e * a.d + col) * 2)
+                           : make_uint4(0, 0, 0, 0);
+    }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSmallStages; ++s) bar_init(&full[s], 1);
+    fence_async_shared();
+  }
+  __syncthreads();
+
+  auto issue = [&](int i) {
+    const int tile = blockIdx.x + i * gridDim.x;
+    const int t0 = tile * tile_t;
+    const int nt = min(tile_t, a.T - t0);
+    const int s = i % kSmallStages;
+    const uint32_t bytes = (uint32_t)(nt * row_bytes);
+    bar_expect_tx(&full[s], bytes);
+    bulk_load(ring + s * kSmallStageBytes, reinterpret_cast<const char*>(a.x) + t0 * row_bytes, bytes, &full[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kSmallStages && blockIdx.x + i * gridDim.x < n_tiles; ++i) issue(i);
+
+  for (int i = 0; blockIdx.x + i * gridDim.x < n_tiles; ++i) {
+    const int tile = blockIdx.x + i * gridDim.x;
+    const int t0 = tile * tile_t;
+    const int nt = min(tile_t, a.T - t0);
+    const int s = i % kSmallStages;
+    const uint32_t ph = (uint32_t)(i / kSmallStages) & 1u;
+    bool ok = bar_try_wait(&full[s], ph);
+    if (!ok) {
+      const uint64_t w0 = global_timer_ns();
+      while (!(ok = bar_try_wait(&full[s], ph)))
+        if (global_timer_ns() - w0 > kSmallWaitNs) break;
+    }
+    // A copy from valid memory does not fail; should one never land, every thread leaves
+    // together instead of waiting forever.
+    if (__syncthreads_or(!ok)) return;
+    const uint8_t* st = ring + s * kSmallStageBytes;
+    float* part = s_part + (i & 1) * tile_t * nw * EP;
+    for (int r = 0; r < nt; ++r) {
+      float acc[EP];
+#pragma unroll
+      for (int e = 0; e < EP; ++e) acc[e] = 0.f;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const int64_t col = ((int64_t)(warp * V + j) * 32 + lane) * 8;
+        float xf[8];
+        unpack8<DT>(*reinterpret_cast<const uint4*>(st + r * row_bytes + col * 2), xf);
+#pragma unroll
+        for (int e = 0; e < EP; ++e) {
+          float wf[8];
+          unpack8<DT>(wreg[e][j], wf);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[e] = fmaf(xf[q], wf[q], acc[e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < EP; ++e) acc[e] = warp_sum(acc[e]);
+      if (lane == 0)
+#pragma unroll
+        for (int e = 0; e < EP; ++e) part[(r * nw + warp) * EP + e] = acc[e];
+    }
+    __syncthreads();  // the stage is consumed and the partials are visible
+    if (threadIdx.x == 0 && blockIdx.x + (i + kSmallStages) * gridDim.x < n_tiles) {
+      fence_async_shared();
+      issue(i + kSmallStages);
+    }
+    if (threadIdx.x < nt) {
+      const int t = t0 + threadIdx.x;
+      float l[EP], p[EP];
+      float m = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < EP; ++e) {
+        float v = 0.f;
+        for (int w = 0; w < nw; ++w) v += part[(threadIdx.x * nw + w) * EP + e];
+        if (e < a.E) {
+          if (a.logit_bias) v += a.logit_bias[e];
+          if (a.logits_out) a.logits_out[(int64_t)t * a.E + e] = v;
+          m = fmaxf(m, v);
+        }
+        l[e] = v;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int e = 0; e < EP; ++e) {
+        p[e] = e < a.E ? expf(l[e] - m) : 0.f;
+        sum += p[e];
+      }
+      uint32_t used = 0;
+      float wsum = 0.f;
+      float pw[kMaxTopK];
+      int pe[kMaxTopK];
+      for (int r = 0; r < a.k; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        float bp = 0.f;
+#pragma unroll
+        for (int e = 0; e < EP; ++e)
+          if (e < a.E && !(used >> e & 1u) && ranks_before(l[e], e, bv, bi)) {
+            bv = l[e];
+            bi = e;
+            bp = p[e] / sum;
+          }
+        used |= 1u << bi;
+        pe[r] = bi;
+        pw[r] = bp;
+        wsum += bp;
+      }
+      for (int r = 0; r < a.k; ++r) {
+        float w = a.renormalize ? pw[r] / wsum : pw[r];
+        w *= a.scale;
+        a.idx_out[(int64_t)t * a.k + r] = pe[r];
+        store_from_float(a.w_out, (int64_t)t * a.k + r, w, a.w_dtype);
+      }
+    }
+  }
+}
+
+template <int DT, int EP, int V>
+int launch_router_small(int grid, int threads, size_t smem, cudaStream_t s, const RouterArgs& a, int tile_t,
+                        int n_tiles) {
+  static PerDeviceOnce once;
+  int dev = 0;
+  DMOE_CUDA(cudaGetDevice(&dev));
+  const int r = once_per_device(once, dev, [&] {
+    DMOE_CUDA(cudaFuncSetAttribute(router_small_kernel<DT, EP, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+    return DMOE_OK;
+  });
+  if (r) return r;
+  router_small_kernel<DT, EP, V><<<grid, threads, smem, s>>>(a, tile_t, n_tiles);
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}
+
+// The few-expert kernel applies when the softmax router computes its own logits from 16-bit
+// x, d is a multiple of 256, and the lane's weight registers (E x V vectors) stay within what
+// a 512-thread CTA holds without spilling: E <= 8 with d <= 4096, or E <= 4 with d <= 8192.
+bool router_small_eligible(int x_dtype, int mode, const float* logits_in, int E, int d) {
+  if (logits_in != nullptr || mode != DMOE_ROUTER_SOFTMAX) return false;
+  if (x_dtype != DMOE_BF16 && x_dtype != DMOE_F16) return false;
+  if (d % 256 != 0 || !((E <= 8 && d <= 4096) || (E <= 4 && d <= 8192 && d % 512 == 0))) return false;
+  const char* v = getenv("DMOE_ROUTER_SMALL");
+  return !(v && v[0] == '0');
+}
+
+template <int DT>
+int run_router_small_dt(const RouterArgs& a, cudaStream_t s) {
+  const int V = a.d <= 4096 ? 1 : 2;
+  const int nw = a.d / (256 * V);
+  const int64_t row_bytes = (int64_t)a.d * 2;
+  int tile_t = (int)(kSmallStageBytes / row_bytes);
+  if (tile_t > kSmallMaxTile) tile_t = kSmallMaxTile;
+  const int n_tiles = (a.T + tile_t - 1) / tile_t;
+  const int EP = a.E <= 4 ? 4 : 8;
+  const int grid = n_tiles < 148 ? n_tiles : 148;
+  const size_t smem = (size_t)kSmallStages * kSmallStageBytes + (size_t)2 * tile_t * nw * EP * sizeof(float) +
+                      kSmallStages * sizeof(uint64_t);
+  const int threads = nw * 32;
+  if (EP == 8) return launch_router_small<DT, 8, 1>(grid, threads, smem, s, a, tile_t, n_tiles);
+  if (V == 1) return launch_router_small<DT, 4, 1>(grid, threads, smem, s, a, tile_t, n_tiles);
+  return launch_router_small<DT, 4, 2>(grid, threads, smem, s, a, tile_t, n_tiles);
+}
+
+int run_router_small(int x_dtype, const RouterArgs& a, cudaStream_t s) {
+  return x_dtype == DMOE_BF16 ? run_router_small_dt<DMOE_BF16>(a, s) : run_router_small_dt<DMOE_F16>(a, s);
+}
+
 template <int DT, bool W_SMEM>
 int launch_router(dim3 grid, dim3 block, size_t smem, cudaStream_t s, const RouterArgs& a) {
   if (W_SMEM) {
@@ -335,6 +536,7 @@ extern "C" int dmoe_router(const void* x, const void* w_r, int x_dtype, const fl
   if (T == 0) return DMOE_OK;
   RouterArgs a{x, w_r, logit_bias, score_bias, logits_in, logits_out, idx_out, w_out, T, d, E, k, mode,
                renormalize, mode == DMOE_ROUTER_SIGMOID_GROUP ? n_group : 1, topk_group, w_dtype, scale};
+  if (router_small_eligible(x_dtype, mode, logits_in, E, d)) return run_router_small(x_dtype, a, as_stream(stream));
   int blocks = (T + kRouterWarps - 1) / kRouterWarps;
   cudaStream_t s = as_stream(stream);
   const int64_t w_bytes = logits_in ? 0 : (int64_t)E * d * (x_dtype == DMOE_F32 ? 4 : 2);

@@ -121,8 +121,12 @@ def test_router_rejects_bad_args():
 # ----------------------------------------------------------------------------- plan
 @gpu
 @pytest.mark.parametrize("T,k,E", [(1, 1, 1), (1, 2, 8), (37, 2, 8), (5, 4, 16), (4096, 2, 8), (8192, 8, 256),
-                                   (3000, 8, 1024), (100, 1, 4), (16, 8, 128)])
-def test_route_plan_bit_exact(T, k, E):
+                                   (4096, 8, 256), (16384, 2, 8), (3000, 8, 1024), (100, 1, 4), (16, 8, 128)])
+@pytest.mark.parametrize("single", ["1", "0"])
+def test_route_plan_bit_exact(T, k, E, single, monkeypatch):
+    """Both plan paths (one CTA for up to 32768 activations and E <= 256, three launches
+    otherwise; DMOE_PLAN_SINGLE=0 forces the latter) give the oracle's plan bit for bit."""
+    monkeypatch.setenv("DMOE_PLAN_SINGLE", single)
     N = _nat()
     g = torch.Generator().manual_seed(T + 31 * k + E)
     # distinct experts per token, like top-k
@@ -139,6 +143,54 @@ def test_route_plan_bit_exact(T, k, E):
     inv[pt * k + ps] = torch.arange(T * k)
     assert torch.equal(res["inverse"].cpu().long(), inv)
     assert torch.equal(res["perm_weight"].cpu(), w[pt, ps])
+
+
+@gpu
+@pytest.mark.parametrize("single", ["1", "0"])
+def test_route_plan_invalid_experts_are_left_out(single, monkeypatch):
+    """Indices outside [0, E) get no position: counts cover only valid ones, inverse is -1."""
+    monkeypatch.setenv("DMOE_PLAN_SINGLE", single)
+    N = _nat()
+    T, k, E = 3000, 2, 8
+    g = torch.Generator().manual_seed(9)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    idx[7, 1] = -1
+    idx[100, 0] = E
+    res = N.route_plan(idx.to(DEV), None, E, want_weight=False)
+    torch.cuda.synchronize()
+    valid = (idx >= 0) & (idx < E)
+    assert res["counts"].sum().item() == int(valid.sum())
+    inv = res["inverse"].cpu().view(T, k)
+    assert inv[7, 1].item() == -1 and inv[100, 0].item() == -1
+    assert sorted(inv[valid].tolist()) == list(range(int(valid.sum())))
+    pt = res["perm_token"].cpu()[:int(valid.sum())]
+    off = res["offsets"].cpu()
+    for e in range(E):
+        toks = pt[off[e]:off[e + 1]]
+        assert bool((idx[toks.long()] == e).any(dim=1).all())
+
+
+@gpu
+@pytest.mark.parametrize("T,d,E,k", [(4096, 4096, 8, 2), (4097, 4096, 8, 2), (33, 2048, 6, 3), (500, 8192, 4, 2),
+                                     (17, 256, 2, 1)])
+def test_router_few_experts_ring_kernel(T, d, E, k):
+    """The few-expert router (weights in registers, token tiles through a bulk-copy ring):
+    logits within fp32 summation error of the oracle's, selection bit-exact from them, with
+    a logit bias, renormalisation and a scale; also the Mixtral shape."""
+    N = _nat()
+    g = torch.Generator().manual_seed(T + d + E)
+    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    w_r = (torch.randn(E, d, generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(E, generator=g)
+    idx, w, logits = N.router(x.to(DEV), w_r.to(DEV), k, want_logits=True, logit_bias=bias.to(DEV),
+                              renormalize=True, scale=1.5, w_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ref_logits = O.router_logits(x, w_r, fp32_logits=True, logit_bias=bias)
+    mag = x.float().abs() @ w_r.float().abs().t()
+    assert bool(((logits.cpu() - ref_logits).abs() <= 2 * d * 2.0 ** -24 * mag + 1e-6).all())
+    rw, sel = O.route(logits.cpu(), k, torch.float32, renormalize=True, scale=1.5)
+    assert torch.equal(idx.cpu(), sel)
+    assert torch.allclose(w.cpu(), rw, rtol=1e-6, atol=1e-7)
 
 
 @gpu

@@ -1,9 +1,13 @@
 """Expert-parallel layer across GPUs (one process per GPU), against the oracle.
 
 Each rank hosts its own tokens; block g of every host holds the experts of GPU g, so every
-forward moves activations between GPUs over NVLink (CUDA-IPC buffers, completion notices).
-Needs at least 2 GPUs; skipped otherwise.  Processes are spawned (CUDA starts after the fork)
-and joined with a time limit.
+forward moves activations between GPUs over NVLink.  Both data planes: the device-driven
+NVLinkDirect exchange (peer stores into the owners' receive windows, one grouped MLP per
+GPU, peer-load combine, epoch flags) and the task protocol (CUDA-IPC buffers, completion
+notices).  The fault-tolerance case replicates every expert on two GPUs and disables a block
+on every host half-way; the rows go to the surviving replicas.  Needs at least 2 GPUs;
+skipped otherwise.  Processes are spawned (CUDA starts after the fork) and joined with a time
+limit; NVLS is off (NCCL is not used, the group is gloo).
 """
 
 import os
@@ -39,6 +43,7 @@ def _worker(rank, world, port, cfg, results):
         from datetime import timedelta
         from distributedmoe_b200 import _native as N
         from distributedmoe_b200.MoE.sharded_cluster import ShardedCluster, experts_of_rank
+        from distributedmoe_b200.TensorTransferEngine import TensorTransferEngineBackend as B
         from oracle import moe_oracle as O
         from oracle.synthetic import make_layer_inputs
 
@@ -50,24 +55,41 @@ def _worker(rank, world, port, cfg, results):
         T, d, E, k, I = cfg["T"], cfg["d"], cfg["E"], cfg["k"], cfg["I"]
         steps = cfg.get("steps", 4)
         inp = make_layer_inputs(T * world, d, E, I, cfg["seed"], torch.bfloat16)
-        mine = experts_of_rank(E, world, rank)
+        blocks = cfg.get("blocks")
+        if blocks is not None:
+            blocks = blocks(world)
+        mine = blocks[rank] if blocks is not None else experts_of_rank(E, world, rank)
         stacked = (inp.gate[mine].contiguous().to(dev), inp.up[mine].contiguous().to(dev),
                    inp.down[mine].contiguous().to(dev))
         # A different batch every forward, issued back to back: a result read before its
         # expert outputs landed (or one forward's rows in another's output) shows up here.
         g = torch.Generator().manual_seed(cfg["seed"] * 100 + rank)
-        xs = [torch.randn(T, d, generator=g).to(torch.bfloat16) for _ in range(steps)]
-        cl = ShardedCluster(E, k, d, torch.bfloat16, dev, stacked, io_buffer_size=cfg["io"], number_of_io_buffers=4,
-                            activation="silu", renormalize=True, forward_timeout=20000)
+        if cfg.get("ragged"):
+            sizes = [(T, T // 2, 0, T, 7), (T // 3, 0, T, 1, T)][rank % 2][:steps]
+        else:
+            sizes = [T] * steps
+        xs = [torch.randn(n, d, generator=g).to(torch.bfloat16) for n in sizes]
+        backend = B.NVLinkDirect if cfg.get("backend", "direct") == "direct" else B.NVLinkIPC
+        extra = {} if backend == B.NVLinkDirect else dict(io_buffer_size=cfg["io"], number_of_io_buffers=4)
+        cl = ShardedCluster(E, k, d, torch.bfloat16, dev, stacked, activation="silu", renormalize=True,
+                            forward_timeout=20000, backend=backend, max_tokens=T, blocks=blocks,
+                            expert_block_policy=cfg.get("policy", "fifo"), **extra)
         try:
             with torch.no_grad():
                 cl.moe.gate.weight.copy_(inp.w_r.to(dev))
             xds = [x.to(dev) for x in xs]
-            ys = [cl.moe(x).clone() for x in xds]
+            ys = []
+            for i, x in enumerate(xds):
+                if i == cfg.get("lose_at", -1):
+                    cl.moe.disable_experts_block(cfg["lose_block"])
+                ys.append(cl.moe(x).clone())
             torch.cuda.synchronize()
             N.check_device_status(dev)
             errs = []
             for x, y in zip(xs, ys):
+                if x.shape[0] == 0:
+                    assert y.shape == (0, d)
+                    continue
                 _, _, logits = N.router(x.to(dev), inp.w_r.to(dev), k, want_logits=True)
                 ref = O.local_experts(x, logits.cpu(), inp.gate, inp.up, inp.down, k, act=O.ACT_SILU,
                                       renormalize=True, compute_dtype=torch.float32)
@@ -113,15 +135,47 @@ def _run(world, cfg, timeout=240):
         assert max(errs[1::2]) < 2e-2, f"rank {rank} max-abs {errs}"
 
 
-@gpu
-def test_expert_parallel_two_gpus():
-    _run(2, dict(T=1024, d=512, E=8, k=2, I=1024, io=2048, seed=21))
+def _replicas(world):
+    """Every rank holds its own share of the experts and the next rank's share."""
+    E = 8
+    share = [list(range(g * E // world, (g + 1) * E // world)) for g in range(world)]
+    return [share[g] + share[(g + 1) % world] for g in range(world)]
 
 
 @gpu
-def test_expert_parallel_all_gpus_split_tasks():
+@pytest.mark.parametrize("backend", ["direct", "tasks"])
+def test_expert_parallel_two_gpus(backend):
+    _run(2, dict(T=1024, d=512, E=8, k=2, I=1024, io=2048, seed=21, backend=backend))
+
+
+@gpu
+def test_expert_parallel_two_gpus_direct_ragged_batches():
+    """Different token counts per rank (one rank sends an empty batch) on the direct plane."""
+    _run(2, dict(T=333, d=256, E=8, k=2, I=512, io=1024, seed=23, backend="direct", steps=5, ragged=True))
+
+
+@gpu
+@pytest.mark.parametrize("policy", ["least_loaded", "fifo"])
+def test_expert_parallel_two_gpus_replicas_block_lost(policy):
+    _run(2, dict(T=800, d=256, E=8, k=2, I=512, io=2048, seed=24, backend="direct", blocks=_replicas,
+                 policy=policy, lose_at=2, lose_block=1, steps=5))
+
+
+@gpu
+@pytest.mark.parametrize("backend", ["direct", "tasks"])
+def test_expert_parallel_all_gpus_split_tasks(backend):
     n = torch.cuda.device_count()
     if n < 4:
         pytest.skip("needs 4 GPUs")
     world = 8 if n >= 8 else 4
-    _run(world, dict(T=700, d=256, E=16, k=4, I=256, io=1024, seed=22))
+    _run(world, dict(T=700, d=256, E=16, k=4, I=256, io=1024, seed=22, backend=backend))
+
+
+@gpu
+def test_expert_parallel_all_gpus_replicas_block_lost():
+    n = torch.cuda.device_count()
+    if n < 4:
+        pytest.skip("needs 4 GPUs")
+    world = 8 if n >= 8 else 4
+    _run(world, dict(T=1024, d=256, E=8, k=2, I=512, io=2048, seed=25, backend="direct", blocks=_replicas,
+                     policy="least_loaded", lose_at=2, lose_block=3, steps=5))
