@@ -384,7 +384,7 @@ class Layer:
     (LocalCluster on one GPU, ShardedCluster over ranks) and this rank's input tokens."""
 
     def __init__(self, w: Workload, dev: torch.device, world: int = 1, rank: int = 0, parallel: str = "single",
-                 data_plane: str = "direct", x_seed_offset: int = 0):
+                 data_plane: str = "direct", x_seed_offset: int = 0, cuda_graphs: bool = False):
         from distributedmoe_b200.MoE.local_cluster import LocalCluster
         from distributedmoe_b200.MoE.sharded_cluster import ShardedCluster
         from distributedmoe_b200.TensorTransferEngine import TensorTransferEngineBackend as B
@@ -412,6 +412,8 @@ class Layer:
         if ep:
             mine = blocks[rank]
             self.stack = expert_weights(w, mine, dev)
+            if data_plane == "direct":
+                opts["cuda_graphs"] = cuda_graphs
             self.cluster = ShardedCluster(w.E, w.k, D, torch.bfloat16, dev, self.stack, backend=backend,
                                           max_tokens=self.T, blocks=blocks, **opts,
                                           **({} if data_plane == "direct" else dict(zip(
@@ -426,6 +428,8 @@ class Layer:
                 stacks.append(tuple(t if len(blocks) == 1 else t.index_select(0, idx).contiguous() for t in full))
             self.stack = full
             io_size, io_buffers = w.io(1, "single")
+            if data_plane == "direct":
+                opts["cuda_graphs"] = cuda_graphs
             self.cluster = LocalCluster(w.E, blocks, w.k, D, torch.bfloat16, dev, [dev] * len(blocks),
                                         stacked=stacks, io_buffer_size=io_size, number_of_io_buffers=io_buffers,
                                         backend=backend, max_tokens=self.T, **opts)
@@ -528,7 +532,9 @@ def run_ours(args, dist, rank, world, local_rank):
     parallel = args.parallel if world > 1 else "single"
     if parallel == "experts" and w.E % world:
         raise SystemExit(f"--parallel experts needs a GPU count that divides {w.E}")
-    layer = Layer(w, dev, world, rank, parallel, args.data_plane)
+    graphs = args.cuda_graphs == "on" or (args.cuda_graphs == "auto" and w.name.endswith("decode-moe-layer"))
+    graphs = graphs and args.data_plane == "direct"
+    layer = Layer(w, dev, world, rank, parallel, args.data_plane, cuda_graphs=graphs)
     moe, x, T, D = layer.moe, layer.x, layer.T, w.d
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(T, D, dtype=torch.bfloat16).pin_memory()
@@ -666,7 +672,7 @@ def run_ours(args, dist, rank, world, local_rank):
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong" if (w.strong and parallel == "experts") else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": w.config(world, parallel, args.data_plane), "impl": "ours",
+        "config": dict(w.config(world, parallel, args.data_plane), cuda_graphs=graphs), "impl": "ours",
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": total_tokens * D * 2, "d2h_bytes_per_step": total_tokens * D * 2,
                 "copies": "pinned host in/out every step; H2D of step i+1 and D2H of step i-1 on two copy "
@@ -715,6 +721,70 @@ def run_gemm_only(args):
                       "tflops": 6.0 * rows * D * w.I / (ms * 1e-3) / 1e12}), flush=True)
 
 
+def run_movers(args):
+    """Kernel-only mode for profiling the bandwidth-bound kernels of one forward on one GPU,
+    without expert weights: router, routing plan, exchange placement, gather into the
+    receive window, combine, at the workload's token count.  Prints one JSON line with the
+    CUDA-event time and algorithmic GB/s per kernel (not a bench line)."""
+    from distributedmoe_b200 import _native as N
+    from distributedmoe_b200.MoE.instances import InstanceTable
+
+    w = WORKLOADS[args.workload]
+    dev = torch.device("cuda", 0)
+    T, D, E, k = w.tokens, w.d, w.E, w.k
+    gen = torch.Generator(device=dev).manual_seed(w.seed)
+    x = _randn_bf16((T, D), 1.0, gen, dev)
+    w_r = _randn_bf16((E, D), w.w_std, gen, dev)
+    score_bias = torch.randn(E, generator=gen, device=dev) * w.score_bias_std if w.score_bias_std else None
+    n = T * k
+    recv = torch.empty(n, D, dtype=torch.bfloat16, device=dev)
+    rows = _randn_bf16((n, D), 1.0, gen, dev)
+    flags = torch.zeros(N.ep_flags_bytes() // 8, dtype=torch.int64, device=dev)
+    win = N.ep_window(1, 0, [flags.data_ptr()], [0], [recv.data_ptr()], [rows.data_ptr()])
+    inst = InstanceTable.from_blocks([list(range(E))], [0], 1, E)
+    alive_n, alive_inst = inst.alive_arrays([True])
+    i32 = dict(dtype=torch.int32, device=dev)
+    R = N.EP_MAX_REPLICAS
+    table = (torch.tensor(alive_n, **i32), torch.tensor(alive_inst, **i32), torch.tensor(inst.inst_rank, **i32),
+             torch.tensor(inst.inst_slot, **i32), torch.tensor(inst.inst_first, **i32))
+    place = (torch.zeros(E, **i32), torch.zeros(E * R, **i32), torch.zeros(E * (R + 1), **i32),
+             torch.zeros(E, **i32))
+    segs = (torch.zeros(E, **i32), torch.zeros(E, **i32))
+    ret, done = torch.empty(n, **i32), torch.zeros(1, **i32)
+    out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    mode = N.ROUTER_SIGMOID_GROUP if w.router_mode == "sigmoid_group" else N.ROUTER_SOFTMAX
+
+    def one():
+        idx, wts, _ = N.router(x, w_r, k, mode=mode, renormalize=True, scale=w.scale, score_bias=score_bias,
+                               n_group=w.n_group, topk_group=w.topk_group, w_dtype=torch.float32)
+        plan = N.route_plan(idx, None, E, want_slot=False, want_weight=False)
+        N.ep_plan(win, plan["counts"], E, E, N.EP_POLICY_ROTATE, table, n, 10**9, place + segs)
+        N.ep_dispatch(win, x, T, k, E, plan["offsets"], plan["perm_token"], place, table[2], n, ret, done)
+        N.ep_combine(win, plan["inverse"], ret, wts, T, k, out)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    N.enable_kernel_timing(True)
+    for _ in range(args.steps):
+        one()
+    recs = N.kernel_records()
+    N.enable_kernel_timing(False)
+    N.check_device_status(dev)
+    _, _, hbm, src = _peaks()
+    nbytes = {"router": T * D * 2 + E * D * 2 + n * 12, "ep_dispatch": 2 * n * D * 2 + n * 8,
+              "ep_combine": n * D * 2 + T * D * 2 + n * 12}
+    res = {}
+    for name, r in recs.items():
+        us = statistics.median(m for m, _ in r) * 1e3
+        res[name] = {"us": us}
+        if name in nbytes:
+            res[name]["gbs"] = nbytes[name] / (us * 1e-6) / 1e9
+            res[name]["frac_of_hbm"] = res[name]["gbs"] / hbm
+    print(json.dumps({"mode": "movers", "workload": w.name, "tokens": T, "hbm_peak_gbs": hbm, "peak_kind": src,
+                      "ops": res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -727,10 +797,13 @@ def main():
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per step: per GPU for weak-scaling workloads, in all for the others")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cuda-graphs", default="auto", choices=["auto", "on", "off"],
+                    help="replay each forward from a captured CUDA graph (auto: for the decode workload)")
     ap.add_argument("--parallel", default="experts", choices=["experts", "replicas"],
                     help="with N > 1 GPUs: shard the experts over the GPUs, or run one layer per GPU")
-    ap.add_argument("--mode", default="layer", choices=["layer", "gemm"],
-                    help="gemm: time only the grouped expert MLP (for kernel profiling)")
+    ap.add_argument("--mode", default="layer", choices=["layer", "gemm", "movers"],
+                    help="gemm: time only the grouped expert MLP; movers: only the router, plan, gather and "
+                         "combine (for kernel profiling)")
     ap.add_argument("--gemm-rows", type=int, default=4096)
     ap.add_argument("--gemm-experts", type=int, default=2)
     args = ap.parse_args()
@@ -740,6 +813,9 @@ def main():
         WORKLOADS[args.workload].tokens = args.tokens
     if args.mode == "gemm":
         run_gemm_only(args)
+        return
+    if args.mode == "movers":
+        run_movers(args)
         return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -439,8 +439,9 @@ class DistMoEBlock(nn.Module):
                                 op_name="shared_expert_mlp")
             done = torch.cuda.Event()
             done.record(side)
-        x.record_stream(side)
-        self.output_batch.record_stream(side)
+        if not torch.cuda.is_current_stream_capturing():  # a captured graph owns its buffers
+            x.record_stream(side)
+            self.output_batch.record_stream(side)
         return done
 
     def _blocks_with_pending_work(self) -> int:
@@ -552,7 +553,7 @@ class DistMoEBlock(nn.Module):
     # ------------------------------------------------------------------ device-driven data plane
     def setup_direct_plane(self, world: int, rank: int, block_ranks: List[int], local_stack, capacity: int,
                            exchange: Callable[[bytes], List[bytes]], max_tokens: int,
-                           wait_timeout_ms: Optional[int] = None) -> None:
+                           wait_timeout_ms: Optional[int] = None, cuda_graphs: bool = False) -> None:
         """Switch forward() to the device-driven exchange (``NVLinkDirect`` backend only).
 
         world, rank: this host's group (one rank per GPU, every rank calls forward once per
@@ -560,7 +561,10 @@ class DistMoEBlock(nn.Module):
         (gate [S, I, d], up [S, I, d], down [S, d, I]) for its blocks in index order (S = its
         expert instances); capacity: receive rows per GPU (at least the rows all hosts can
         send it: world * max_tokens * top_k covers any routing); exchange(mine) returns every
-        rank's window descriptor in rank order; max_tokens: tokens per forward of this host."""
+        rank's window descriptor in rank order; max_tokens: tokens per forward of this host.
+        cuda_graphs: capture the forward once per token count (after one eager forward of
+        that count) and replay it; the input is copied into a static buffer and the result
+        copied out, so callers see ordinary tensors."""
         tte = self.tensor_transfer_engine
         if not getattr(tte, "direct", False):
             raise RuntimeError("the device-driven data plane needs the NVLinkDirect backend")
@@ -585,7 +589,7 @@ class DistMoEBlock(nn.Module):
             timeout_ms = wait_timeout_ms if wait_timeout_ms is not None else min(self.forward_timeout, 5000)
             self._ep = {
                 "world": world, "rank": rank, "inst": inst, "win": win, "cap": capacity, "policy": policy,
-                "n_local": n_local, "stack": (g, u, dn), "max_tokens": max_tokens, "epoch": 0,
+                "n_local": n_local, "stack": (g, u, dn), "max_tokens": max_tokens,
                 "timeout_ns": int(timeout_ms) * 1_000_000,
                 "inst_rank": torch.tensor(inst.inst_rank, **i32),
                 "inst_slot": torch.tensor(inst.inst_slot, **i32),
@@ -595,6 +599,8 @@ class DistMoEBlock(nn.Module):
                 "part_start": torch.zeros(E * (R + 1), **i32), "dest_off": torch.zeros(inst.n_inst, **i32),
                 "seg_expert": torch.zeros(max(n_local, 1), **i32), "seg_end": torch.zeros(max(n_local, 1), **i32),
                 "done": torch.zeros(1, **i32), "ret": torch.empty(max(max_tokens * k, 1), **i32),
+                "cuda_graphs": cuda_graphs, "graphs": {},
+                "x_static": torch.zeros(max_tokens, d, dtype=self.dtype, device=dev) if cuda_graphs else None,
             }
             torch.cuda.synchronize(dev)
 
@@ -614,20 +620,48 @@ class DistMoEBlock(nn.Module):
         if input_batch.dim() not in (2, 3) or shape[-1] != self.hidden_features:
             raise RuntimeError(f"Wrong input batch shape: {shape} with hidden size: {self.hidden_features}")
         x = input_batch.reshape(-1, self.hidden_features).contiguous()
-        T, E, k = x.shape[0], self.number_of_experts, self.top_k
+        T = x.shape[0]
         if T > ep["max_tokens"]:
             raise ValueError(f"{T} tokens exceed the {ep['max_tokens']} this data plane was sized for")
-        if self.metrics_collector is not None:
+        if not ep["cuda_graphs"]:
+            return self._direct_step(x).reshape(shape)
+        self._direct_alive()  # any upload of the alive table happens outside the graph
+        g = ep["graphs"].get(T)
+        if g is None:
+            out = self._direct_step(x)  # this step runs eagerly; the capture runs no kernel
+            self._direct_capture(T)
+            return out.reshape(shape)
+        xs, out_static, graph, launches = g
+        xs.copy_(x)
+        graph.replay()
+        N.count_graph_replay(launches)
+        return out_static.clone().reshape(shape)
+
+    def _direct_capture(self, T: int) -> None:
+        """Capture the forward of T tokens from the static input buffer."""
+        ep = self._ep
+        xs = ep["x_static"][:T]
+        graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(self.device)
+        before = N.launch_count()
+        with torch.cuda.graph(graph):
+            out = self._direct_step(xs)
+        ep["graphs"][T] = (xs, out, graph, N.launch_count() - before)
+
+    def _direct_step(self, x: torch.Tensor) -> torch.Tensor:
+        ep = self._ep
+        T, E, k = x.shape[0], self.number_of_experts, self.top_k
+        capturing = torch.cuda.is_current_stream_capturing()
+        if self.metrics_collector is not None and not capturing:
             self.metrics_collector.start_forward_pass()
         dev = self.device
-        ep["epoch"] += 1
-        epoch, win, cap, tmo = ep["epoch"], ep["win"], ep["cap"], ep["timeout_ns"]
+        win, cap, tmo = ep["win"], ep["cap"], ep["timeout_ns"]
         out = torch.empty(x.shape, dtype=self.dtype, device=dev)
         self.output_batch = out
         shared = self.shared_expert is not None and T > 0
         shared_done = self._launch_shared_expert(x) if shared else None
-        self._direct_alive()
-        R = N.EP_MAX_REPLICAS
+        if not capturing:
+            self._direct_alive()
         table = (ep["alive"][:E], ep["alive"][E:], ep["inst_rank"], ep["inst_slot"], ep["inst_first"])
         placement = (ep["part_n"], ep["part_inst"], ep["part_start"], ep["dest_off"])
         if T > 0:
@@ -637,26 +671,24 @@ class DistMoEBlock(nn.Module):
         else:
             counts = offsets = perm_token = inverse = w = None
         inst = ep["inst"]
-        N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, epoch, tmo,
-                  placement + (ep["seg_expert"], ep["seg_end"]))
-        N.ep_dispatch(win, x, T, k, E, offsets, perm_token, placement, ep["inst_rank"], cap, ep["ret"], ep["done"],
-                      epoch)
+        N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, tmo, placement + (ep["seg_expert"], ep["seg_end"]))
+        N.ep_dispatch(win, x, T, k, E, offsets, perm_token, placement, ep["inst_rank"], cap, ep["ret"], ep["done"])
         # This GPU's expert instances, once, over every host's rows (the expert blocks' part).
-        N.ep_wait(win, N.EP_FLAG_DATA, epoch, tmo, dev)
+        N.ep_wait(win, N.EP_FLAG_DATA, tmo, dev)
         if ep["n_local"] > 0:
             g, u, dn = ep["stack"]
             tte = self.tensor_transfer_engine
             N.grouped_gated_mlp(tte.recv, g, u, dn, ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]],
                                 ACTIVATIONS[self.config.activation], tte.out, m_rows=cap)
-        N.ep_signal(win, N.EP_FLAG_RESULTS, epoch, dev)
-        N.ep_wait(win, N.EP_FLAG_RESULTS, epoch, tmo, dev)
+        N.ep_signal(win, N.EP_FLAG_RESULTS, dev)
+        N.ep_wait(win, N.EP_FLAG_RESULTS, tmo, dev)
         if T > 0:
             if shared_done is not None:
                 torch.cuda.current_stream(dev).wait_event(shared_done)
             N.ep_combine(win, inverse, ep["ret"], w, T, k, out, accumulate=shared)
-        if self.metrics_collector is not None:
+        if self.metrics_collector is not None and not capturing:
             self.metrics_collector.end_forward_pass()
-        return out.reshape(shape)
+        return out
 
     # ------------------------------------------------------------------ shutdown
     def close(self) -> None:

@@ -102,11 +102,14 @@ class ShardedCluster:
                  forward_timeout: int = 60000, p2p_timeout_ms: int = 3000, address: str = "127.0.0.1",
                  gemm_sm_reserve: Optional[int] = None,
                  backend: TensorTransferEngineBackend = TensorTransferEngineBackend.NVLinkDirect,
-                 max_tokens: int = 8192, blocks: Optional[List[List[int]]] = None, **options):
+                 max_tokens: int = 8192, blocks: Optional[List[List[int]]] = None, cuda_graphs: bool = False,
+                 **options):
         """stacked: this rank's weight stack for the experts of its block, in block order.
         blocks[g]: the experts of rank g's block (default: the contiguous E/G of rank g); an
         expert listed by two ranks is replicated.  max_tokens: tokens per forward of one host
-        (sizes the NVLinkDirect receive windows: G * max_tokens * top_k rows per GPU)."""
+        (sizes the NVLinkDirect receive windows: G * max_tokens * top_k rows per GPU).
+        cuda_graphs: replay each token count's forward from a captured CUDA graph (every rank
+        captures at the same step; capturing runs no kernel, so the ranks stay in step)."""
         direct = backend == TensorTransferEngineBackend.NVLinkDirect
         if direct:
             # The task buffers only serve the metadata hand-shake: keep them small.
@@ -188,7 +191,8 @@ class ShardedCluster:
             torch.cuda.synchronize(device)
             if direct:
                 self.moe.setup_direct_plane(G, r, list(range(G)), stacked, G * max_tokens * top_k,
-                                            lambda mine: gather_window_descriptors(mine, group), max_tokens)
+                                            lambda mine: gather_window_descriptors(mine, group), max_tokens,
+                                            cuda_graphs=cuda_graphs)
         self.direct = direct
         self.device = device
         dist.barrier(group=group)  # every host and block of every rank is up before the first forward

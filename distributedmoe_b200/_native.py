@@ -89,11 +89,11 @@ SIGNATURES = {
     "dmoe_ep_flags_bytes": (_sz, []),
     "dmoe_ep_counts_bytes": (_sz, [ctypes.c_int]),
     "dmoe_ep_plan": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _i64,
-                                    _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+                                    _u64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dmoe_ep_dispatch": (ctypes.c_int, [_vp, _vp, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp,
-                                        _vp, _vp, _vp, _i64, _vp, _vp, _u64, _vp, _vp]),
-    "dmoe_ep_wait": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _u64, _vp, _vp]),
-    "dmoe_ep_signal": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _vp]),
+                                        _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "dmoe_ep_wait": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _vp, _vp]),
+    "dmoe_ep_signal": (ctypes.c_int, [_vp, ctypes.c_int, _vp]),
     "dmoe_ep_combine": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_int, _vp, _vp]),
     "dmoe_event_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
@@ -253,7 +253,7 @@ class _Timed:
         self.name = name
         self.ev = None
         self.work = work
-        if _timing is not None:
+        if _timing is not None and not torch.cuda.is_current_stream_capturing():
             # The current stream as torch knows it (the legacy default stream included);
             # another handle is wrapped.
             cur = torch.cuda.current_stream(device)
@@ -577,10 +577,10 @@ def ep_window(world: int, rank: int, flags: Sequence[int], counts: Sequence[int]
 
 
 def ep_plan(win: EpWindow, counts_e: Optional[torch.Tensor], E: int, n_inst: int, policy: int, table, cap: int,
-            epoch: int, timeout_ns: int, out, stream: Optional[int] = None) -> None:
-    """Count exchange and placement.  table: (alive_n, alive_inst, inst_rank, inst_slot,
-    inst_first) int32 device tensors; out: (part_n, part_inst, part_start, dest_off,
-    seg_expert, seg_end) int32 device tensors."""
+            timeout_ns: int, out, stream: Optional[int] = None) -> None:
+    """Count exchange and placement (advances the window's epoch counter).  table: (alive_n,
+    alive_inst, inst_rank, inst_slot, inst_first) int32 device tensors; out: (part_n,
+    part_inst, part_start, dest_off, seg_expert, seg_end) int32 device tensors."""
     alive_n, alive_inst, inst_rank, inst_slot, inst_first = table
     part_n, part_inst, part_start, dest_off, seg_expert, seg_end = out
     dev = alive_n.device
@@ -588,7 +588,7 @@ def ep_plan(win: EpWindow, counts_e: Optional[torch.Tensor], E: int, n_inst: int
     tm = _Timed("ep_plan", st, dev)
     rc = lib().dmoe_ep_plan(ctypes.byref(win), _ptr(counts_e), E, n_inst, policy, alive_n.data_ptr(),
                             alive_inst.data_ptr(), inst_rank.data_ptr(), inst_slot.data_ptr(), inst_first.data_ptr(),
-                            int(cap), int(epoch), int(timeout_ns), part_n.data_ptr(), part_inst.data_ptr(),
+                            int(cap), int(timeout_ns), part_n.data_ptr(), part_inst.data_ptr(),
                             part_start.data_ptr(), dest_off.data_ptr(), seg_expert.data_ptr(), seg_end.data_ptr(),
                             scratch.status(dev).data_ptr(), st)
     _check(rc, "dmoe_ep_plan")
@@ -597,7 +597,7 @@ def ep_plan(win: EpWindow, counts_e: Optional[torch.Tensor], E: int, n_inst: int
 
 def ep_dispatch(win: EpWindow, x: torch.Tensor, T: int, k: int, E: int, offsets: Optional[torch.Tensor],
                 perm_token: Optional[torch.Tensor], placement, inst_rank: torch.Tensor, cap: int,
-                ret: torch.Tensor, done: torch.Tensor, epoch: int, stream: Optional[int] = None) -> None:
+                ret: torch.Tensor, done: torch.Tensor, stream: Optional[int] = None) -> None:
     """Gather rows into their receivers' buffers (peer stores) and raise the data flags.
     placement: (part_n, part_inst, part_start, dest_off) from :func:`ep_plan`."""
     part_n, part_inst, part_start, dest_off = placement
@@ -607,21 +607,20 @@ def ep_dispatch(win: EpWindow, x: torch.Tensor, T: int, k: int, E: int, offsets:
     rc = lib().dmoe_ep_dispatch(ctypes.byref(win), _ptr(x), x.shape[-1] * x.element_size(), T, k, E, _ptr(offsets),
                                 _ptr(perm_token), part_n.data_ptr(), part_inst.data_ptr(), part_start.data_ptr(),
                                 inst_rank.data_ptr(), dest_off.data_ptr(), int(cap), ret.data_ptr(), done.data_ptr(),
-                                int(epoch), scratch.status(dev).data_ptr(), st)
+                                scratch.status(dev).data_ptr(), st)
     _check(rc, "dmoe_ep_dispatch")
     tm.done()
 
 
-def ep_wait(win: EpWindow, kind: int, epoch: int, timeout_ns: int, device: torch.device,
-            stream: Optional[int] = None) -> None:
+def ep_wait(win: EpWindow, kind: int, timeout_ns: int, device: torch.device, stream: Optional[int] = None) -> None:
     st = stream if stream is not None else _stream(device)
-    _check(lib().dmoe_ep_wait(ctypes.byref(win), kind, int(epoch), int(timeout_ns), scratch.status(device).data_ptr(),
-                              st), "dmoe_ep_wait")
+    _check(lib().dmoe_ep_wait(ctypes.byref(win), kind, int(timeout_ns), scratch.status(device).data_ptr(), st),
+           "dmoe_ep_wait")
 
 
-def ep_signal(win: EpWindow, kind: int, epoch: int, device: torch.device, stream: Optional[int] = None) -> None:
+def ep_signal(win: EpWindow, kind: int, device: torch.device, stream: Optional[int] = None) -> None:
     st = stream if stream is not None else _stream(device)
-    _check(lib().dmoe_ep_signal(ctypes.byref(win), kind, int(epoch), st), "dmoe_ep_signal")
+    _check(lib().dmoe_ep_signal(ctypes.byref(win), kind, st), "dmoe_ep_signal")
 
 
 def ep_combine(win: EpWindow, inverse: Optional[torch.Tensor], ret: torch.Tensor, w: Optional[torch.Tensor],
@@ -636,5 +635,18 @@ def ep_combine(win: EpWindow, inverse: Optional[torch.Tensor], ret: torch.Tensor
     tm.done()
 
 
+_graph_launches = 0
+_graph_lock = threading.Lock()
+
+
+def count_graph_replay(launches: int) -> None:
+    """Account the library kernels of one CUDA-graph replay (captured launches run again
+    without passing through the C entry points that count them)."""
+    global _graph_launches
+    with _graph_lock:
+        _graph_launches += int(launches)
+
+
 def launch_count() -> int:
-    return int(lib().dmoe_launch_count())
+    """Library kernels launched in this process: direct launches plus graph replays."""
+    return int(lib().dmoe_launch_count()) + _graph_launches

@@ -27,8 +27,11 @@
 // contiguous grouped-MLP segment holding every host's tokens for that expert.
 //
 // Flags are monotonic 64-bit epochs (one per forward, equal on every rank).  A rank's flag
-// array holds [kind][sender] for three kinds: counts, data, results.  All waits are bounded
-// by time and report through the status word; nothing traps.
+// array holds [kind][sender] for three kinds (counts, data, results) and, after them, the
+// rank's own epoch counter: ep_plan advances it at the start of every forward and the later
+// kernels of the forward read it, so a forward takes no per-step argument from the host (a
+// captured CUDA graph replays correctly).  All waits are bounded by time and report through
+// the status word; nothing traps.
 #include "dmoe_common.cuh"
 
 namespace dmoe {
@@ -38,6 +41,9 @@ constexpr int kMaxRanks = DMOE_EP_MAX_RANKS;
 constexpr int kMaxReplicas = DMOE_EP_MAX_REPLICAS;
 constexpr int kMaxInstances = DMOE_EP_MAX_INSTANCES;
 constexpr int kFlagKinds = 3;
+constexpr int kEpochSlot = kFlagKinds * kMaxRanks;  // index of the epoch counter in a flag array
+
+__device__ __forceinline__ uint64_t current_epoch(const uint64_t* my_flags) { return my_flags[kEpochSlot]; }
 
 struct EpPeers {
   int world, rank;
@@ -85,7 +91,7 @@ struct EpPlanArgs {
   const int32_t* inst_slot;  // [n_inst] position in the owner's weight stack
   const int32_t* inst_first; // [world + 1]
   int64_t cap;               // receive rows of every rank
-  uint64_t epoch, timeout_ns;
+  uint64_t timeout_ns;
   int32_t* status;
   // outputs (this rank's device scratch)
   int32_t* part_n;           // [E] parts the expert's rows are split into this step (0: dropped)
@@ -102,9 +108,17 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const EpPlanArgs a) {
   __shared__ int32_t s_scan[kMaxInstances];
   __shared__ int32_t s_warp[32];
   __shared__ int s_arrived[kMaxRanks];
+  __shared__ uint64_t s_epoch;
   const int tid = threadIdx.x;
   const int G = a.peers.world, me = a.peers.rank, n_inst = a.n_inst;
-  const int parity = (int)(a.epoch & 1ull);
+  if (tid == 0) {
+    uint64_t* counter = a.peers.flags[me] + kEpochSlot;
+    s_epoch = *counter + 1;
+    *counter = s_epoch;  // this forward's epoch; the later kernels of the forward read it
+  }
+  __syncthreads();
+  const uint64_t epoch = s_epoch;
+  const int parity = (int)(epoch & 1ull);
 
   for (int i = tid; i < n_inst; i += blockDim.x) s_mine[i] = 0;
   __syncthreads();
@@ -130,7 +144,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const EpPlanArgs a) {
         ps[np] = n;
       } else {
         np = 1;
-        const int inst = a.alive_inst[e * kMaxReplicas + (int)((a.epoch + (uint64_t)me) % (uint64_t)na)];
+        const int inst = a.alive_inst[e * kMaxReplicas + (int)((epoch + (uint64_t)me) % (uint64_t)na)];
         ps[0] = 0;
         ps[1] = n;
         pi[0] = inst;
@@ -149,9 +163,9 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const EpPlanArgs a) {
     }
     __threadfence_system();
     __syncthreads();
-    if (tid < G) st_release_sys(a.peers.flags[tid] + 0 * kMaxRanks + me, a.epoch);
+    if (tid < G) st_release_sys(a.peers.flags[tid] + 0 * kMaxRanks + me, epoch);
     if (tid < G) {
-      const bool ok = tid == me || wait_flag(a.peers.flags[me] + 0 * kMaxRanks + tid, a.epoch, a.timeout_ns);
+      const bool ok = tid == me || wait_flag(a.peers.flags[me] + 0 * kMaxRanks + tid, epoch, a.timeout_ns);
       s_arrived[tid] = ok ? 1 : 0;
       if (!ok) atomicOr(a.status, DMOE_DEVERR_EP_TIMEOUT);
     }
@@ -240,13 +254,50 @@ struct EpDispatchArgs {
   int64_t cap;
   int32_t* ret;              // [n] (rank << 27 | row) of each activation, -1 when dropped
   uint32_t* done;            // CTA completion counter (zero between launches)
-  uint64_t epoch;
   int32_t* status;
 };
 
 constexpr int kRowShift = 27;
 
+// Per-expert placement as the gather reads it: where the expert's rows start in the
+// permuted order, how its rows split into parts, and each part's (rank, receive row of the
+// expert's row 0 of that part).  Kept in shared memory when E <= kTableMaxE, so a row's
+// destination costs a few shared-memory reads instead of a chain of dependent global loads.
+constexpr int kTableMaxE = 256;
+
+struct ExpertPlacement {
+  int32_t start[kMaxReplicas + 1];  // part q holds the expert's rows [start[q], start[q+1])
+  int32_t rank[kMaxReplicas];
+  int32_t base[kMaxReplicas];       // receive row = base[q] + row index within the expert
+  int32_t np;
+};
+
+__device__ __forceinline__ void load_placement(const EpDispatchArgs& a, int e, ExpertPlacement& pl) {
+  int np = a.part_n[e];
+  if (np > kMaxReplicas) np = kMaxReplicas;
+  pl.np = 0;
+  for (int q = 0; q <= np; ++q) pl.start[q] = a.part_start[e * (kMaxReplicas + 1) + q];
+  for (int q = 0; q < np; ++q) {
+    const int inst = a.part_inst[e * kMaxReplicas + q];
+    const int r = a.inst_rank[inst];
+    if (r < 0 || r >= a.peers.world) return;  // a malformed table: the expert's rows are dropped
+    pl.rank[q] = r;
+    pl.base[q] = a.dest_off[inst] - pl.start[q];
+  }
+  pl.np = np;
+}
+
+template <bool TABLE>
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a) {
+  __shared__ int32_t s_off[TABLE ? kTableMaxE + 1 : 1];
+  __shared__ ExpertPlacement s_pl[TABLE ? kTableMaxE : 1];
+  if constexpr (TABLE) {
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+      s_off[e] = a.offsets[e];
+      load_placement(a, e, s_pl[e]);
+    }
+    __syncthreads();
+  }
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -254,40 +305,41 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
     int lo = 0, hi = a.E - 1;  // expert of permuted position p: last e with offsets[e] <= p
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (a.offsets[mid] <= p) lo = mid; else hi = mid - 1;
+      if ((TABLE ? s_off[mid] : a.offsets[mid]) <= p) lo = mid; else hi = mid - 1;
     }
     const int e = lo;
-    const int i = (int)(p - a.offsets[e]);
-    const int np = a.part_n[e];
+    const int i = (int)(p - (TABLE ? s_off[e] : a.offsets[e]));
+    ExpertPlacement local;
+    const ExpertPlacement* pl = &local;
+    if constexpr (TABLE) {
+      pl = &s_pl[e];
+    } else {
+      load_placement(a, e, local);
+    }
+    const int np = pl->np;
     int q = -1;
     for (int t = 0; t < np; ++t)
-      if (a.part_start[e * (kMaxReplicas + 1) + t] <= i) q = t;
+      if (pl->start[t] <= i) q = t;
     // Positions past the plan's last expert row (activations without a valid expert) and
     // experts without an alive instance are dropped.
-    if (np > 0 && i >= a.part_start[e * (kMaxReplicas + 1) + np]) q = -1;
+    if (np > 0 && i >= pl->start[np]) q = -1;
     int32_t code = -1;
     if (q >= 0) {
-      const int inst = a.part_inst[e * kMaxReplicas + q];
-      const int r = a.inst_rank[inst];
-      if (r < 0 || r >= a.peers.world) q = -1;  // a malformed table: drop rather than write anywhere
-    }
-    if (q >= 0) {
-      const int inst = a.part_inst[e * kMaxReplicas + q];
-      const int r = a.inst_rank[inst];
-      const int64_t row = (int64_t)a.dest_off[inst] + (i - a.part_start[e * (kMaxReplicas + 1) + q]);
+      const int r = pl->rank[q];
+      const int64_t row = (int64_t)pl->base[q] + i;
       if (row < a.cap) {
         code = (int32_t)(((uint32_t)r << kRowShift) | (uint32_t)row);
-        const uint4* s = reinterpret_cast<const uint4*>(a.x) + (int64_t)a.perm_token[p] * a.row_vecs;
+        const uint4* src = reinterpret_cast<const uint4*>(a.x) + (int64_t)a.perm_token[p] * a.row_vecs;
         uint4* d = reinterpret_cast<uint4*>(a.peers.recv[r]) + row * a.row_vecs;
         int64_t c = lane;
         for (; c + 224 < a.row_vecs; c += 256) {
           uint4 v[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = s[c + 32 * u];
+          for (int u = 0; u < 8; ++u) v[u] = src[c + 32 * u];
 #pragma unroll
           for (int u = 0; u < 8; ++u) d[c + 32 * u] = v[u];
         }
-        for (; c < a.row_vecs; c += 32) d[c] = s[c];
+        for (; c < a.row_vecs; c += 32) d[c] = src[c];
       } else if (lane == 0) {
         atomicOr(a.status, DMOE_DEVERR_EP_OVERFLOW);
       }
@@ -303,22 +355,26 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
     if (prev == gridDim.x - 1) {
       __threadfence_system();
       *a.done = 0;
-      if (a.peers.world > 1)
-        for (int g = 0; g < a.peers.world; ++g) st_release_sys(a.peers.flags[g] + 1 * kMaxRanks + a.peers.rank, a.epoch);
+      if (a.peers.world > 1) {
+        const uint64_t epoch = current_epoch(a.peers.flags[a.peers.rank]);
+        for (int g = 0; g < a.peers.world; ++g) st_release_sys(a.peers.flags[g] + 1 * kMaxRanks + a.peers.rank, epoch);
+      }
     }
   }
 }
 
 // ------------------------------------------------------------------------- ep_wait / ep_signal
-__global__ void ep_wait_kernel(const uint64_t* flags, int kind, int world, int me, uint64_t epoch,
-                               uint64_t timeout_ns, int32_t* status) {
+__global__ void ep_wait_kernel(const uint64_t* flags, int kind, int world, int me, uint64_t timeout_ns,
+                               int32_t* status) {
+  const uint64_t epoch = current_epoch(flags);
   const int g = threadIdx.x;
   if (g < world && g != me) {
     if (!wait_flag(flags + kind * kMaxRanks + g, epoch, timeout_ns)) atomicOr(status, DMOE_DEVERR_EP_TIMEOUT);
   }
 }
 
-__global__ void ep_signal_kernel(EpPeers peers, int kind, uint64_t epoch) {
+__global__ void ep_signal_kernel(EpPeers peers, int kind) {
+  const uint64_t epoch = current_epoch(peers.flags[peers.rank]);
   __threadfence_system();
   const int g = threadIdx.x;
   if (g < peers.world) st_release_sys(peers.flags[g] + kind * kMaxRanks + peers.rank, epoch);
@@ -424,7 +480,8 @@ int fill_peers(EpPeers* p, const dmoe_ep_window* w) {
     if (in) {
       DMOE_REQUIRE(w->recv[g] && w->out[g] && aligned16(w->recv[g]) && aligned16(w->out[g]),
                    "dmoe_ep: rank %d's rows must be 16-byte aligned device pointers", g);
-      if (w->world > 1) DMOE_REQUIRE(w->flags[g] && w->counts[g], "dmoe_ep: rank %d has no flags/counts", g);
+      DMOE_REQUIRE(w->flags[g] != nullptr, "dmoe_ep: rank %d has no flag array", g);
+      if (w->world > 1) DMOE_REQUIRE(w->counts[g] != nullptr, "dmoe_ep: rank %d has no count matrix", g);
     }
   }
   return DMOE_OK;
@@ -435,7 +492,7 @@ int fill_peers(EpPeers* p, const dmoe_ep_window* w) {
 
 using namespace dmoe;
 
-extern "C" size_t dmoe_ep_flags_bytes(void) { return (size_t)kFlagKinds * kMaxRanks * sizeof(uint64_t); }
+extern "C" size_t dmoe_ep_flags_bytes(void) { return (size_t)(kEpochSlot + 1) * sizeof(uint64_t); }
 
 extern "C" size_t dmoe_ep_counts_bytes(int n_inst) {
   return (size_t)2 * kMaxRanks * (size_t)(n_inst > 0 ? n_inst : 0) * sizeof(int32_t);
@@ -443,8 +500,7 @@ extern "C" size_t dmoe_ep_counts_bytes(int n_inst) {
 
 extern "C" int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, int E, int n_inst, int policy,
                             const int32_t* alive_n, const int32_t* alive_inst, const int32_t* inst_rank,
-                            const int32_t* inst_slot, const int32_t* inst_first, int64_t cap, uint64_t epoch,
-                            uint64_t timeout_ns, int32_t* part_n, int32_t* part_inst, int32_t* part_start,
+                            const int32_t* inst_slot, const int32_t* inst_first, int64_t cap, uint64_t timeout_ns, int32_t* part_n, int32_t* part_inst, int32_t* part_start,
                             int32_t* dest_off, int32_t* seg_expert, int32_t* seg_end, int32_t* dev_status,
                             void* stream) {
   clear_error();
@@ -458,7 +514,6 @@ extern "C" int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, 
                policy);
   DMOE_REQUIRE(cap >= 0 && cap < (1ll << kRowShift), "dmoe_ep_plan: capacity %lld rows not in [0, 2^27)",
                (long long)cap);
-  DMOE_REQUIRE(epoch >= 1, "dmoe_ep_plan: epochs start at 1");
   DMOE_REQUIRE(alive_n && alive_inst && inst_rank && inst_slot && inst_first && part_n && part_inst && part_start &&
                    dest_off && seg_expert && seg_end && dev_status,
                "dmoe_ep_plan: null pointer");
@@ -472,7 +527,6 @@ extern "C" int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, 
   a.inst_slot = inst_slot;
   a.inst_first = inst_first;
   a.cap = cap;
-  a.epoch = epoch;
   a.timeout_ns = timeout_ns;
   a.status = dev_status;
   a.part_n = part_n;
@@ -489,7 +543,7 @@ extern "C" int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, 
 extern "C" int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_t row_bytes, int T, int k, int E,
                                 const int32_t* offsets, const int32_t* perm_token, const int32_t* part_n,
                                 const int32_t* part_inst, const int32_t* part_start, const int32_t* inst_rank,
-                                const int32_t* dest_off, int64_t cap, int32_t* ret, uint32_t* done, uint64_t epoch,
+                                const int32_t* dest_off, int64_t cap, int32_t* ret, uint32_t* done,
                                 int32_t* dev_status, void* stream) {
   clear_error();
   EpDispatchArgs a{};
@@ -517,18 +571,20 @@ extern "C" int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_
   a.cap = cap;
   a.ret = ret;
   a.done = done;
-  a.epoch = epoch;
   a.status = dev_status;
   int64_t blocks = (a.n + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;  // an empty batch still raises the data flags
-  ep_dispatch_kernel<<<(int)blocks, 256, 0, as_stream(stream)>>>(a);
+  if (E <= kTableMaxE)
+    ep_dispatch_kernel<true><<<(int)blocks, 256, 0, as_stream(stream)>>>(a);
+  else
+    ep_dispatch_kernel<false><<<(int)blocks, 256, 0, as_stream(stream)>>>(a);
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }
 
-extern "C" int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t epoch, uint64_t timeout_ns,
-                            int32_t* dev_status, void* stream) {
+extern "C" int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t timeout_ns, int32_t* dev_status,
+                            void* stream) {
   clear_error();
   EpPeers p{};
   int r = fill_peers(&p, win);
@@ -536,20 +592,19 @@ extern "C" int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t epoch,
   DMOE_REQUIRE(kind >= 0 && kind < kFlagKinds, "dmoe_ep_wait: bad flag kind %d", kind);
   DMOE_REQUIRE(dev_status, "dmoe_ep_wait: null status");
   if (p.world == 1) return DMOE_OK;
-  ep_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(p.flags[p.rank], kind, p.world, p.rank, epoch, timeout_ns,
-                                                  dev_status);
+  ep_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(p.flags[p.rank], kind, p.world, p.rank, timeout_ns, dev_status);
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }
 
-extern "C" int dmoe_ep_signal(const dmoe_ep_window* win, int kind, uint64_t epoch, void* stream) {
+extern "C" int dmoe_ep_signal(const dmoe_ep_window* win, int kind, void* stream) {
   clear_error();
   EpPeers p{};
   int r = fill_peers(&p, win);
   if (r) return r;
   DMOE_REQUIRE(kind >= 0 && kind < kFlagKinds, "dmoe_ep_signal: bad flag kind %d", kind);
   if (p.world == 1) return DMOE_OK;
-  ep_signal_kernel<<<1, 32, 0, as_stream(stream)>>>(p, kind, epoch);
+  ep_signal_kernel<<<1, 32, 0, as_stream(stream)>>>(p, kind);
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }

@@ -221,13 +221,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
       __syncwarp();
       const int per_group = E / a.n_group;
       if (lane < a.n_group) {
+        // The two best scores of the group in torch.topk's order (NaN above every number),
+        // so a group holding a NaN score ranks first, as the group top-k does.
         float b1 = -INFINITY, b2 = -INFINITY;
         for (int e = lane * per_group; e < (lane + 1) * per_group; ++e) {
           const float v = s_logit[warp][e];
-          if (v > b1) {
+          if (ranks_before(v, 0, b1, 1)) {
             b2 = b1;
             b1 = v;
-          } else if (v > b2) {
+          } else if (ranks_before(v, 0, b2, 1)) {
             b2 = v;
           }
         }
@@ -292,20 +294,60 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
 }
 
 // ------------------------------------------------------------------------- few experts
-// Softmax router for E <= 16 experts and 16-bit inputs (the Mixtral-style router).  One
+// Softmax router for E <= 8 experts and 16-bit inputs (the Mixtral-style router).  One
 // persistent CTA per SM; its warps split the hidden dimension (warp w owns V runs of 512
-// contiguous bytes of every row) and each lane keeps its columns of all E router rows in
-// registers for the whole kernel, so the weights are read once per CTA.  Tiles of
+// contiguous bytes of every row) and each lane keeps its columns of all router rows in
+// registers as fp32 for the whole kernel, so the weights are read once per CTA.  Tiles of
 // consecutive tokens (contiguous in x) stream into a 4-stage shared-memory ring through
 // bulk async copies that complete on mbarriers: several tiles are in flight per SM
-// independent of the register budget.  Per tile, each warp reduces its E partial dot
-// products per token, and one thread per token sums the warps' partials in a fixed order,
-// adds the logit bias and does the softmax and top-k (same order as the warp kernel: NaN
-// first, then larger, then lower index).
+// independent of the register budget.  Per token, a warp's EP partial dot products are
+// reduced with a butterfly reduce-scatter (EP/2 + ... + 1 + 2 shuffles) that leaves each
+// lane one expert's warp sum.  After one CTA barrier per tile, warp 0 alone sums the warps'
+// partials in a fixed order (one lane per token and expert), then each group of EP lanes
+// does its token's softmax and top-k with shuffles (same order as the warp kernel: NaN
+// first, then larger, then lower index) while the other warps go on with the next tile.
 constexpr int kSmallStages = 4;
 constexpr int kSmallStageBytes = 32 * 1024;
 constexpr int kSmallMaxTile = 16;
 constexpr uint64_t kSmallWaitNs = 2000000000ull;
+
+// Butterfly reduce-scatter of EP values per lane over the 32 lanes of a warp: returns the
+// full warp sum of value number `expert_of_lane(lane)`.
+template <int EP>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[EP], int lane) {
+  float cur[EP];
+#pragma unroll
+  for (int e = 0; e < EP; ++e) cur[e] = v[e];
+  int n = EP;
+#pragma unroll
+  for (int o = 16; n > 1; o >>= 1) {
+    const bool hi = lane & o;
+    const int h = n / 2;
+#pragma unroll
+    for (int q = 0; q < EP / 2; ++q) {
+      if (q < h) {
+        const float send = hi ? cur[q] : cur[q + h];
+        const float keep = hi ? cur[q + h] : cur[q];
+        cur[q] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    n = h;
+  }
+  // n == 1: lanes that differ only in the low bits hold partial sums of the same value
+  float r = cur[0];
+  constexpr int used = EP == 8 ? 3 : (EP == 4 ? 2 : (EP == 2 ? 1 : 0));
+#pragma unroll
+  for (int o = 1 << (4 - used); o >= 1; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}
+
+// Which value a lane holds after warp_reduce_scatter: its bits 4, 3, 2 (EP = 8) select the
+// upper halves of the successive splits.
+template <int EP>
+__device__ __forceinline__ int expert_of_lane(int lane) {
+  constexpr int used = EP == 8 ? 3 : (EP == 4 ? 2 : (EP == 2 ? 1 : 0));
+  return (lane >> (5 - used)) & (EP - 1);
+}
 
 template <int DT, int EP, int V>
 __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a, int tile_t, int n_tiles) {
@@ -316,15 +358,18 @@ __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a
   uint8_t* ring = smem_raw;
   float* s_part = reinterpret_cast<float*>(smem_raw + kSmallStages * kSmallStageBytes);  // [2][tile][nw][EP]
   uint64_t* full = reinterpret_cast<uint64_t*>(s_part + 2 * tile_t * nw * EP);
+  constexpr int used = EP == 8 ? 3 : (EP == 4 ? 2 : (EP == 2 ? 1 : 0));
+  constexpr uint32_t low_mask = (1u << (5 - used)) - 1u;  // lanes sharing one reduced value
 
-  uint4 wreg[EP][V];
+  float wf[EP][V * 8];
 #pragma unroll
   for (int e = 0; e < EP; ++e)
 #pragma unroll
     for (int j = 0; j < V; ++j) {
       const int64_t col = ((int64_t)(warp * V + j) * 32 + lane) * 8;
-      wreg[e][j] = e < a.E ? *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.w_r) + ((int64_t)e * a.d + col) * 2)
-                           : make_uint4(0, 0, 0, 0);
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (e < a.E) raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.w_r) + ((int64_t)e * a.d + col) * 2);
+      unpack8<DT>(raw, &wf[e][j * 8]);
     }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSmallStages; ++s) bar_init(&full[s], 1);
@@ -344,6 +389,7 @@ __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a
   if (threadIdx.x == 0)
     for (int i = 0; i < kSmallStages && blockIdx.x + i * gridDim.x < n_tiles; ++i) issue(i);
 
+  const int my_e = expert_of_lane<EP>(lane);
   for (int i = 0; blockIdx.x + i * gridDim.x < n_tiles; ++i) {
     const int tile = blockIdx.x + i * gridDim.x;
     const int t0 = tile * tile_t;
@@ -371,70 +417,68 @@ __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a
         float xf[8];
         unpack8<DT>(*reinterpret_cast<const uint4*>(st + r * row_bytes + col * 2), xf);
 #pragma unroll
-        for (int e = 0; e < EP; ++e) {
-          float wf[8];
-          unpack8<DT>(wreg[e][j], wf);
+        for (int e = 0; e < EP; ++e)
 #pragma unroll
-          for (int q = 0; q < 8; ++q) acc[e] = fmaf(xf[q], wf[q], acc[e]);
-        }
+          for (int q = 0; q < 8; ++q) acc[e] = fmaf(xf[q], wf[e][j * 8 + q], acc[e]);
       }
-#pragma unroll
-      for (int e = 0; e < EP; ++e) acc[e] = warp_sum(acc[e]);
-      if (lane == 0)
-#pragma unroll
-        for (int e = 0; e < EP; ++e) part[(r * nw + warp) * EP + e] = acc[e];
+      const float sum = warp_reduce_scatter<EP>(acc, lane);
+      if ((lane & low_mask) == 0) part[(r * nw + warp) * EP + my_e] = sum;
     }
-    __syncthreads();  // the stage is consumed and the partials are visible
+    __syncthreads();  // the stage is consumed and every warp's partials are written
     if (threadIdx.x == 0 && blockIdx.x + (i + kSmallStages) * gridDim.x < n_tiles) {
       fence_async_shared();
       issue(i + kSmallStages);
     }
-    if (threadIdx.x < nt) {
-      const int t = t0 + threadIdx.x;
-      float l[EP], p[EP];
-      float m = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < EP; ++e) {
-        float v = 0.f;
-        for (int w = 0; w < nw; ++w) v += part[(threadIdx.x * nw + w) * EP + e];
-        if (e < a.E) {
+    if (warp == 0) {
+      // lane = token-in-chunk * EP + expert; groups of EP lanes hold one token's logits
+      for (int r0 = 0; r0 < nt; r0 += 32 / EP) {
+        const int r = r0 + lane / EP, e = lane % EP;
+        const bool live = r < nt && e < a.E;
+        float l = -INFINITY;
+        if (live) {
+          float v = 0.f;
+          for (int w = 0; w < nw; ++w) v += part[(r * nw + w) * EP + e];
           if (a.logit_bias) v += a.logit_bias[e];
-          if (a.logits_out) a.logits_out[(int64_t)t * a.E + e] = v;
-          m = fmaxf(m, v);
+          if (a.logits_out) a.logits_out[(int64_t)(t0 + r) * a.E + e] = v;
+          l = v;
         }
-        l[e] = v;
-      }
-      float sum = 0.f;
+        float m = l;
 #pragma unroll
-      for (int e = 0; e < EP; ++e) {
-        p[e] = e < a.E ? expf(l[e] - m) : 0.f;
-        sum += p[e];
-      }
-      uint32_t used = 0;
-      float wsum = 0.f;
-      float pw[kMaxTopK];
-      int pe[kMaxTopK];
-      for (int r = 0; r < a.k; ++r) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        float bp = 0.f;
+        for (int o = 1; o < EP; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, EP));
+        float p = live ? expf(l - m) : 0.f;
+        float ps = p;
 #pragma unroll
-        for (int e = 0; e < EP; ++e)
-          if (e < a.E && !(used >> e & 1u) && ranks_before(l[e], e, bv, bi)) {
-            bv = l[e];
-            bi = e;
-            bp = p[e] / sum;
+        for (int o = 1; o < EP; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o, EP);
+        p = p / ps;
+        bool avail = live;
+        float wsum = 0.f, mine_w = 0.f;
+        int mine_e = 0;
+        for (int q = 0; q < a.k; ++q) {
+          float bv = avail ? l : -INFINITY;
+          int bi = avail ? e : 0x7fffffff;
+#pragma unroll
+          for (int o = 1; o < EP; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o, EP);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o, EP);
+            if (ranks_before(ov, oi, bv, bi)) {
+              bv = ov;
+              bi = oi;
+            }
           }
-        used |= 1u << bi;
-        pe[r] = bi;
-        pw[r] = bp;
-        wsum += bp;
-      }
-      for (int r = 0; r < a.k; ++r) {
-        float w = a.renormalize ? pw[r] / wsum : pw[r];
-        w *= a.scale;
-        a.idx_out[(int64_t)t * a.k + r] = pe[r];
-        store_from_float(a.w_out, (int64_t)t * a.k + r, w, a.w_dtype);
+          const float pw = __shfl_sync(0xffffffffu, p, (lane & ~(EP - 1)) | (bi & (EP - 1)), 32);
+          if (e == bi) avail = false;
+          wsum += pw;
+          if (e == q) {
+            mine_w = pw;
+            mine_e = bi;
+          }
+        }
+        if (r < nt && e < a.k) {
+          float w = a.renormalize ? mine_w / wsum : mine_w;
+          w *= a.scale;
+          a.idx_out[(int64_t)(t0 + r) * a.k + e] = mine_e;
+          store_from_float(a.w_out, (int64_t)(t0 + r) * a.k + e, w, a.w_dtype);
+        }
       }
     }
   }

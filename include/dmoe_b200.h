@@ -254,16 +254,19 @@ int dmoe_flag_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, in
  * dmoe_ep_plan wrote (seg_expert, seg_end; n_seg = the rank's instance count).
  *
  * Window: per rank, in its own GPU memory and mapped into every rank (CUDA IPC):
- *   flags   dmoe_ep_flags_bytes() of uint64 epochs [kind][sender], zero-initialised
+ *   flags   dmoe_ep_flags_bytes() of uint64, zero-initialised: epochs [kind][sender], then
+ *           the rank's epoch counter (advanced by dmoe_ep_plan, read by the other calls)
  *   counts  dmoe_ep_counts_bytes(n_inst) of int32 [2][DMOE_EP_MAX_RANKS][n_inst]
  *   recv    [cap, d] rows other ranks dispatch to (instance-major, then sender rank)
  *   out     [cap, d] the grouped MLP's output rows of recv
  * The table passed to every call lists all ranks' windows as this process addresses them.
  * Instances (an expert's weights on one rank) are numbered rank-major; rank r's instances
  * are [inst_first[r], inst_first[r+1]) in the order of its weight stack (inst_slot).
- * Epochs: one per forward, equal on all ranks, starting at 1, increasing.  With world == 1
- * no flags are touched.  Every wait is bounded by timeout_ns and reports
- * DMOE_DEVERR_EP_TIMEOUT; the rows of a rank that did not answer are left out.
+ * Epochs: one per forward, counted on the device (every rank calls dmoe_ep_plan once per
+ * forward, so the counters agree), starting at 1; no call takes an epoch from the host, so a
+ * forward can be captured in a CUDA graph and replayed.  With world == 1 no flag of another
+ * rank is touched.  Every wait is bounded by timeout_ns and reports DMOE_DEVERR_EP_TIMEOUT;
+ * the rows of a rank that did not answer are left out.
  * A rank's waits are only ever satisfied by other GPUs: every rank must be its own GPU.
  */
 #define DMOE_EP_MAX_RANKS 16
@@ -293,11 +296,11 @@ size_t dmoe_ep_counts_bytes(int n_inst);
  * alive blocks, MoE/pools/ExpertBlocksPool.py:37-71); an expert with none has its rows
  * dropped.  Writes part_n [E], part_inst [E][R], part_start [E][R+1], dest_off [n_inst]
  * (first receive row of this rank's rows of each instance on the owner) and this rank's
- * grouped-MLP table seg_expert / seg_end [its instance count].
+ * grouped-MLP table seg_expert / seg_end [its instance count].  Advances the epoch counter.
  */
 int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, int E, int n_inst, int policy,
                  const int32_t* alive_n, const int32_t* alive_inst, const int32_t* inst_rank, const int32_t* inst_slot,
-                 const int32_t* inst_first, int64_t cap, uint64_t epoch, uint64_t timeout_ns, int32_t* part_n,
+                 const int32_t* inst_first, int64_t cap, uint64_t timeout_ns, int32_t* part_n,
                  int32_t* part_inst, int32_t* part_start, int32_t* dest_off, int32_t* seg_expert, int32_t* seg_end,
                  int32_t* dev_status, void* stream);
 
@@ -309,14 +312,14 @@ int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, int E, int 
 int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_t row_bytes, int T, int k, int E,
                      const int32_t* offsets, const int32_t* perm_token, const int32_t* part_n, const int32_t* part_inst,
                      const int32_t* part_start, const int32_t* inst_rank, const int32_t* dest_off, int64_t cap,
-                     int32_t* ret, uint32_t* done, uint64_t epoch, int32_t* dev_status, void* stream);
+                     int32_t* ret, uint32_t* done, int32_t* dev_status, void* stream);
 
-/* Wait (bounded) until every other rank raised its flag of `kind` to `epoch` on this rank. */
-int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t epoch, uint64_t timeout_ns, int32_t* dev_status,
-                 void* stream);
+/* Wait (bounded) until every other rank raised its flag of `kind` to this forward's epoch. */
+int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t timeout_ns, int32_t* dev_status, void* stream);
 
-/* Raise this rank's flag of `kind` to `epoch` on every rank after the stream's prior work. */
-int dmoe_ep_signal(const dmoe_ep_window* win, int kind, uint64_t epoch, void* stream);
+/* Raise this rank's flag of `kind` to this forward's epoch on every rank after the stream's
+ * prior work. */
+int dmoe_ep_signal(const dmoe_ep_window* win, int kind, void* stream);
 
 /*
  * out[t] = (out[t] if accumulate) + sum_s w[t,s] * out_rows_of(ret[inverse[t*k+s]]), reading

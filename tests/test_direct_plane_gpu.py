@@ -80,7 +80,8 @@ def test_exchange_bookkeeping_matches_restatement(policy):
     x = torch.randn(T, d, generator=g, device=DEV).to(torch.bfloat16)
     recv = torch.zeros(cap, d, dtype=torch.bfloat16, device=DEV)
     out = torch.zeros_like(recv)
-    win = N.ep_window(1, 0, [0], [0], [recv.data_ptr()], [out.data_ptr()])
+    flags = torch.zeros(N.ep_flags_bytes() // 8, dtype=torch.int64, device=DEV)
+    win = N.ep_window(1, 0, [flags.data_ptr()], [0], [recv.data_ptr()], [out.data_ptr()])
     i32 = dict(dtype=torch.int32, device=DEV)
     R = N.EP_MAX_REPLICAS
     table = (torch.tensor(n, **i32), torch.tensor(alive_inst, **i32), torch.tensor(inst.inst_rank, **i32),
@@ -89,13 +90,14 @@ def test_exchange_bookkeeping_matches_restatement(policy):
     part_start, dest_off = torch.zeros(E * (R + 1), **i32), torch.zeros(inst.n_inst, **i32)
     seg_expert, seg_end = torch.zeros(inst.n_inst, **i32), torch.zeros(inst.n_inst, **i32)
     ret, done = torch.empty(T * k, **i32), torch.zeros(1, **i32)
-    for epoch in (1, 2, 3):
-        N.ep_plan(win, plan["counts"], E, inst.n_inst, policy, table, cap, epoch, 10**9,
+    for epoch in (1, 2, 3):  # the window's counter: one per ep_plan call
+        N.ep_plan(win, plan["counts"], E, inst.n_inst, policy, table, cap, 10**9,
                   (part_n, part_inst, part_start, dest_off, seg_expert, seg_end))
         N.ep_dispatch(win, x, T, k, E, plan["offsets"], plan["perm_token"], (part_n, part_inst, part_start, dest_off),
-                      table[2], cap, ret, done, epoch)
+                      table[2], cap, ret, done)
         torch.cuda.synchronize()
         N.check_device_status(DEV)
+        assert flags[3 * N.EP_MAX_RANKS].item() == epoch
         alive = [[[alive_inst[e * R + q] for q in range(n[e])] for e in range(E)]]
         ref = P.placement([counts], alive, inst.inst_rank, inst.inst_first, policy, epoch, cap)
         assert dest_off.cpu().tolist() == ref["dest_off"][0]
@@ -243,3 +245,40 @@ def test_direct_deepseek_router_and_shared_expert():
                           shared=(sg, su, sd), compute_dtype=torch.float32)
     for y in ys:
         _check(y, ref)
+
+
+@gpu
+def test_direct_layer_cuda_graph_replays_match_eager():
+    """cuda_graphs=True: the first forward of each token count runs eagerly and is captured;
+    later ones replay the graph (new inputs through the static buffer).  Every output matches
+    the oracle, a block lost between replays is routed around (the alive table is uploaded
+    outside the graph), and the replays are counted as library launches."""
+    from distributedmoe_b200 import _native as N
+    E, k, d, I = 8, 2, 256, 512
+    gate, up, down, w_r, g = _weights(E, d, I, 16)
+    blocks = [[b, (b + 1) % E] for b in range(E)]
+    stacked = [(gate[b].contiguous(), up[b].contiguous(), down[b].contiguous()) for b in blocks]
+    from distributedmoe_b200.MoE.local_cluster import LocalCluster
+    from distributedmoe_b200.TensorTransferEngine import TensorTransferEngineBackend as B
+    cl = LocalCluster(E, blocks, k, d, torch.bfloat16, DEV, [DEV] * len(blocks), stacked=stacked, io_buffer_size=256,
+                      number_of_io_buffers=1, backend=B.NVLinkDirect, max_tokens=512, cuda_graphs=True,
+                      activation="silu", renormalize=True, expert_block_policy="least_loaded")
+    outs = []
+    try:
+        with torch.no_grad():
+            cl.moe.gate.weight.copy_(w_r)
+        for i, T in enumerate([64, 64, 64, 300, 64, 300, 300, 64]):
+            if i == 5:
+                cl.moe.disable_experts_block(2)
+            x = torch.randn(T, d, generator=g, device=DEV).to(torch.bfloat16)
+            before = N.launch_count()
+            y = cl.moe(x)
+            outs.append((x, y, N.launch_count() - before))
+        torch.cuda.synchronize()
+        N.check_device_status(DEV)
+        assert sorted(cl.moe._ep["graphs"]) == [64, 300]
+    finally:
+        cl.close()
+    for x, y, launches in outs:
+        _check(y, _oracle(x, w_r, gate, up, down, k))
+        assert launches >= 6

@@ -71,6 +71,8 @@ def _worker(rank, world, port, cfg, results):
         xs = [torch.randn(n, d, generator=g).to(torch.bfloat16) for n in sizes]
         backend = B.NVLinkDirect if cfg.get("backend", "direct") == "direct" else B.NVLinkIPC
         extra = {} if backend == B.NVLinkDirect else dict(io_buffer_size=cfg["io"], number_of_io_buffers=4)
+        if backend == B.NVLinkDirect:
+            extra["cuda_graphs"] = cfg.get("graphs", False)
         cl = ShardedCluster(E, k, d, torch.bfloat16, dev, stacked, activation="silu", renormalize=True,
                             forward_timeout=20000, backend=backend, max_tokens=T, blocks=blocks,
                             expert_block_policy=cfg.get("policy", "fifo"), **extra)
@@ -146,6 +148,12 @@ def _replicas(world):
 @pytest.mark.parametrize("backend", ["direct", "tasks"])
 def test_expert_parallel_two_gpus(backend):
     _run(2, dict(T=1024, d=512, E=8, k=2, I=1024, io=2048, seed=21, backend=backend))
+
+
+@gpu
+def test_expert_parallel_two_gpus_direct_cuda_graphs():
+    """Decode-size batches replayed from CUDA graphs on both ranks (same step sequence)."""
+    _run(2, dict(T=48, d=256, E=16, k=4, I=256, io=1024, seed=26, backend="direct", steps=6, graphs=True))
 
 
 @gpu
