@@ -292,9 +292,12 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
   __shared__ int32_t s_off[TABLE ? kTableMaxE + 1 : 1];
   __shared__ ExpertPlacement s_pl[TABLE ? kTableMaxE : 1];
   if constexpr (TABLE) {
-    for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
-      s_off[e] = a.offsets[e];
-      load_placement(a, e, s_pl[e]);
+    // An empty batch has no plan (offsets may be NULL): nothing to look up, only the flags.
+    if (a.n > 0) {
+      for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+        s_off[e] = a.offsets[e];
+        load_placement(a, e, s_pl[e]);
+      }
     }
     __syncthreads();
   }
