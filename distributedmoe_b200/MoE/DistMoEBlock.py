@@ -648,6 +648,20 @@ class DistMoEBlock(nn.Module):
             out = self._direct_step(xs)
         ep["graphs"][T] = (xs, out, graph, N.launch_count() - before)
 
+    def _direct_tile_policy(self, T: int) -> int:
+        """Tile shape of the grouped MLP from the rows an expert instance can expect (every
+        rank sending about T tokens): the segment table is on the device, so the host cannot
+        see the actual sizes.  Hundreds of rows per expert or more: 256-row pair tiles; a few
+        hundred: pair tiles plus single-SM tiles for remainders of at most 128 rows (a
+        segment of 257-384 rows then costs three SM-tiles, not four); fewer: single-SM tiles."""
+        ep = self._ep
+        expected = ep["world"] * T * self.top_k / max(1, ep["inst"].n_inst)
+        if expected >= 768:
+            return N.TILES_PAIR
+        if expected >= 128:
+            return N.TILES_PAIR_SPLIT
+        return N.TILES_SINGLE
+
     def _direct_step(self, x: torch.Tensor) -> torch.Tensor:
         ep = self._ep
         T, E, k = x.shape[0], self.number_of_experts, self.top_k
@@ -679,7 +693,8 @@ class DistMoEBlock(nn.Module):
             g, u, dn = ep["stack"]
             tte = self.tensor_transfer_engine
             N.grouped_gated_mlp(tte.recv, g, u, dn, ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]],
-                                ACTIVATIONS[self.config.activation], tte.out, m_rows=cap)
+                                ACTIVATIONS[self.config.activation], tte.out, m_rows=cap,
+                                tile_policy=self._direct_tile_policy(T))
         N.ep_signal(win, N.EP_FLAG_RESULTS, dev)
         N.ep_wait(win, N.EP_FLAG_RESULTS, tmo, dev)
         if T > 0:

@@ -19,6 +19,7 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("DMOE_LIB", os.path.join(_PKG, "libdmoe_b200.so"))
 
 F32, F16, BF16 = 0, 1, 2
+TILES_AUTO, TILES_PAIR, TILES_SINGLE, TILES_PAIR_SPLIT = 0, 1, 2, 3
 ACT_RELU, ACT_SILU = 0, 1
 ROUTER_SOFTMAX, ROUTER_SIGMOID_GROUP = 0, 1
 
@@ -71,6 +72,9 @@ SIGNATURES = {
                                                _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dmoe_permute_rows": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, ctypes.c_int, _vp]),
     "dmoe_grouped_mlp_workspace_size": (_sz, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "dmoe_grouped_gated_mlp_ex": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int, _vp, _vp, _sz, _vp, ctypes.c_int, _vp]),
     "dmoe_grouped_mlp_set_sm_reserve": (ctypes.c_int, [ctypes.c_int]),
     "dmoe_router_logits": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
                                           _vp]),
@@ -400,7 +404,7 @@ def permute_rows(src: torch.Tensor, dst: torch.Tensor, seg_src: Sequence[int], s
 
 def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
                       seg_expert, seg_end, act: int, Y: torch.Tensor, m_rows: Optional[int] = None,
-                      op_name: str = "grouped_gated_mlp") -> None:
+                      op_name: str = "grouped_gated_mlp", tile_policy: int = TILES_AUTO) -> None:
     """Grouped expert MLP over row segments.  seg_expert/seg_end: Python int sequences (host
     table) or int32 CUDA tensors (device table)."""
     _require_cuda(X, Y)
@@ -411,12 +415,13 @@ def grouped_gated_mlp(X: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     m = X.shape[0] if m_rows is None else m_rows
     if m > X.shape[0] or m > Y.shape[0]:
         raise DMoEError("m_rows exceeds the rows of X or Y")
-    grouped_gated_mlp_ptrs(X.data_ptr(), Y.data_ptr(), m, w_gate, w_up, w_down, seg_expert, seg_end, act, op_name)
+    grouped_gated_mlp_ptrs(X.data_ptr(), Y.data_ptr(), m, w_gate, w_up, w_down, seg_expert, seg_end, act, op_name,
+                           tile_policy)
 
 
 def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Tensor, w_up: torch.Tensor,
                            w_down: torch.Tensor, seg_expert, seg_end, act: int,
-                           op_name: str = "grouped_gated_mlp") -> None:
+                           op_name: str = "grouped_gated_mlp", tile_policy: int = TILES_AUTO) -> None:
     """Same as :func:`grouped_gated_mlp` on raw device pointers (rows of d elements of the
     weights' dtype), e.g. a transfer-engine buffer of another block on this GPU."""
     dev = _require_cuda(w_gate, w_up, w_down)
@@ -445,9 +450,9 @@ def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Te
                 start = end
             work = 6.0 * rows * d * I
     tm = _Timed(op_name, _stream(dev), dev, work)
-    rc = lib().dmoe_grouped_gated_mlp(x_ptr, w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
-                                      se, sn, n_seg, on_dev, m_rows, act, y_ptr, ws.data_ptr(), ws.numel(),
-                                      scratch.status(dev).data_ptr(), _stream(dev))
+    rc = lib().dmoe_grouped_gated_mlp_ex(x_ptr, w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
+                                         se, sn, n_seg, on_dev, m_rows, act, y_ptr, ws.data_ptr(), ws.numel(),
+                                         scratch.status(dev).data_ptr(), int(tile_policy), _stream(dev))
     del keep
     _check(rc, "dmoe_grouped_gated_mlp")
     tm.done()

@@ -51,6 +51,10 @@ struct GemmSegs {
   int n_seg;
   int m_rows;
   int e_stack;
+  // Which rows of each segment a launch computes: 0 all; 1 the pair kernel's part of a
+  // split (the whole 256-row blocks, plus the remainder when it exceeds 128 rows); 2 the
+  // single-SM kernel's part (a remainder of at most 128 rows, one 128-row tile).
+  int split;
   const int32_t* dev_expert;
   const int32_t* dev_end;
   int32_t expert[kMaxSegParam];
@@ -238,6 +242,20 @@ struct TileInfo {
   int row0, row_end, expert, nt;
 };
 
+// The part of a segment [first, first + len) that a launch with split mode `split` computes
+// (see GemmSegs::split); updates len and returns the first row.
+__device__ __forceinline__ int split_rows(int split, int first, int& len) {
+  if (split == 0) return first;
+  int full = (len / 256) * 256;
+  if (len - full > 128) full = len;
+  if (split == 1) {
+    len = full;
+    return first;
+  }
+  len -= full;
+  return first + full;
+}
+
 template <int TILE_M>
 __device__ __forceinline__ TileInfo decode_tile(int tile, int total_m, int n_tiles_n, int raster_n_fast, int n_seg,
                                                 const int32_t* s_start, const int32_t* s_end,
@@ -328,8 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         len = 0;
         s_expert[i] = 0;
       }
-      s_start[i] = prev;
-      s_end[i] = prev + len;
+      const int first = split_rows(segs.split, prev, len);
+      s_start[i] = first;
+      s_end[i] = first + len;
       s_tile[i] = tiles;
       tiles += (len + BM - 1) / BM;
       prev = en;
@@ -691,8 +710,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         len = 0;
         s_expert[i] = 0;
       }
-      s_start[i] = prev;
-      s_end[i] = prev + len;
+      const int first = split_rows(segs.split, prev, len);
+      s_start[i] = first;
+      s_end[i] = first + len;
       s_tile[i] = tiles;
       tiles += (len + BM2 - 1) / BM2;
       prev = en;
@@ -1110,8 +1130,8 @@ int sm_count() {
 
 template <int DT>
 int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack, int d, int I,
-            const GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
-            cudaStream_t stream) {
+            GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
+            cudaStream_t stream, int policy) {
   CUtensorMap ta, tg, tu, th, td;
   {
     const uint64_t dims[2] = {(uint64_t)d, (uint64_t)m_rows};
@@ -1141,7 +1161,14 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
   }
   const int nt1 = (I + BN / 2 - 1) / (BN / 2);
   const int nt2 = (d + BN - 1) / BN;
-  if (use_2sm(segs.n_seg, m_rows)) {
+  bool pair = policy == DMOE_TILES_PAIR || policy == DMOE_TILES_PAIR_SPLIT;
+  if (policy == DMOE_TILES_AUTO) pair = use_2sm(segs.n_seg, m_rows);
+  const char* hyb = getenv("DMOE_GEMM_HYBRID");
+  const bool split = policy == DMOE_TILES_PAIR_SPLIT || (pair && hyb && strcmp(hyb, "1") == 0);
+  if (pair && split) {
+    // Whole 256-row blocks (and remainders over 128 rows) as pair tiles, remainders of at
+    // most 128 rows as one single-SM tile each: a segment of 257-384 rows costs three
+    // SM-tile units instead of four.  Both launches read the same segment table.
     CUtensorMap td2;
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
     const uint32_t box[3] = {BK, 128, 1};
@@ -1149,72 +1176,39 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
     GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
-    // Pair tiles only, unless DMOE_GEMM_HYBRID=1 moves short remainders to the single-SM kernel.
-    // With the segment-by-segment tile order a remainder's pair tile reads the expert's weights
-    // from L2 next to the expert's other tiles, while a separate single-SM launch re-reads
-    // them from DRAM after the pair launch (measured on the Mixtral layer: 2.22 ms for pair
-    // tiles only against 2.26 ms split).
-    const char* hyb = getenv("DMOE_GEMM_HYBRID");
-    if (total_m_host < 0 || !(hyb && strcmp(hyb, "1") == 0)) {
-      r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
-      if (r) return r;
-      return launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, -1, stream);
-    }
-    if (total_m_host == 0) return DMOE_OK;
-    // Host table: whole 256-row blocks (and remainders over 128 rows) go to the pair kernel; a
-    // remainder of at most 128 rows is one 128-row tile of the single-SM kernel instead of a
-    // mostly empty pair tile.  Rows a launch skips carry expert -1 in its table.
-    static thread_local GemmSegs pair_segs, rest_segs;
-    pair_segs.n_seg = rest_segs.n_seg = 0;
-    pair_segs.m_rows = rest_segs.m_rows = segs.m_rows;
-    pair_segs.e_stack = rest_segs.e_stack = segs.e_stack;
-    pair_segs.dev_expert = rest_segs.dev_expert = nullptr;
-    pair_segs.dev_end = rest_segs.dev_end = nullptr;
-    int pair_m = 0, rest_m = 0, prev = 0;
-    auto push = [](GemmSegs& g, int e, int end) {
-      g.expert[g.n_seg] = e;
-      g.end[g.n_seg] = end;
-      ++g.n_seg;
-    };
-    for (int i = 0; i < segs.n_seg; ++i) {
-      const int len = segs.end[i] - prev;
-      int full = (len / BM2) * BM2;
-      if (len - full > 128) full = len;
-      const int rem = len - full;
-      if (full > 0) {
-        push(pair_segs, segs.expert[i], prev + full);
-        pair_m += (full + BM2 - 1) / BM2;
-      }
-      if (rem > 0) {
-        push(pair_segs, -1, segs.end[i]);
-        if (full > 0) push(rest_segs, -1, prev + full);
-        push(rest_segs, segs.expert[i], segs.end[i]);
-        rest_m += 1;
-      } else {
-        push(rest_segs, -1, segs.end[i]);
-      }
-      prev = segs.end[i];
-    }
-    if (pair_m > 0) {
-      r = launch_gemm_2sm<true, DT>(ta, tg, tu, pair_segs, a1, pair_m * nt1, stream);
-      if (r) return r;
-    }
-    const int sms1 = usable_sms();
-    if (rest_m > 0) {
-      const int64_t t1 = (int64_t)rest_m * nt1;
-      r = launch_gemm<true, DT>(ta, tg, tu, rest_segs, a1, (int)(t1 < sms1 ? t1 : sms1), stream);
-      if (r) return r;
-    }
-    if (pair_m > 0) {
-      r = launch_gemm_2sm<false, DT>(th, td2, td2, pair_segs, a2, pair_m * nt2, stream);
-      if (r) return r;
-    }
-    if (rest_m > 0) {
-      const int64_t t2 = (int64_t)rest_m * nt2;
-      r = launch_gemm<false, DT>(th, td, td, rest_segs, a2, (int)(t2 < sms1 ? t2 : sms1), stream);
-      if (r) return r;
-    }
-    return DMOE_OK;
+    GemmArgs s1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
+    GemmArgs s2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
+    const int sms = usable_sms();
+    segs.split = 1;
+    r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
+    if (r) return r;
+    segs.split = 2;
+    r = launch_gemm<true, DT>(ta, tg, tu, segs, s1, sms, stream);
+    if (r) return r;
+    segs.split = 1;
+    r = launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, -1, stream);
+    if (r) return r;
+    segs.split = 2;
+    r = launch_gemm<false, DT>(th, td, td, segs, s2, sms, stream);
+    segs.split = 0;
+    return r;
+  }
+  if (pair) {
+    CUtensorMap td2;
+    const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
+    const uint32_t box[3] = {BK, 128, 1};
+    int r = make_map(&td2, DT, w_down, 3, dims, box);
+    if (r) return r;
+    GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
+    GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
+    // Pair tiles only.  With the segment-by-segment tile order a remainder's pair tile reads
+    // the expert's weights from L2 next to the expert's other tiles, while a separate
+    // single-SM launch re-reads them from DRAM after the pair launch (measured on the
+    // Mixtral layer, about 1000 rows per expert: 2.22 ms for pair tiles only against 2.26 ms
+    // split); the split pays off for ragged experts of a few hundred rows.
+    r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
+    if (r) return r;
+    return launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, -1, stream);
   }
   const int sms = usable_sms();
   int g1 = sms, g2 = sms;
@@ -1239,6 +1233,7 @@ int run_logits(const void* X, const void* W, int T, int d, int E, float* out, in
   segs.n_seg = 1;
   segs.m_rows = T;
   segs.e_stack = 1;
+  segs.split = 0;
   segs.dev_expert = nullptr;
   segs.dev_end = nullptr;
   segs.expert[0] = 0;
@@ -1303,12 +1298,14 @@ extern "C" size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype) 
   return (size_t)m_rows * (size_t)I * 2 + 256;
 }
 
-extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down,
-                                      int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
-                                      const int32_t* seg_end, int n_seg, int seg_on_device, int m_rows, int act,
-                                      void* Y, void* workspace, size_t workspace_bytes, int32_t* dev_status,
-                                      void* stream) {
+extern "C" int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, const void* w_up, const void* w_down,
+                                         int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
+                                         const int32_t* seg_end, int n_seg, int seg_on_device, int m_rows, int act,
+                                         void* Y, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                         int tile_policy, void* stream) {
   clear_error();
+  DMOE_REQUIRE(tile_policy >= DMOE_TILES_AUTO && tile_policy <= DMOE_TILES_PAIR_SPLIT,
+               "dmoe_grouped_gated_mlp: bad tile policy %d", tile_policy);
   DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_grouped_gated_mlp: dtype must be f16 or bf16");
   DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "dmoe_grouped_gated_mlp: bad activation %d", act);
   DMOE_REQUIRE(d > 0 && I > 0 && d % 8 == 0 && I % 8 == 0, "dmoe_grouped_gated_mlp: d=%d, I=%d must be multiples of 8",
@@ -1328,6 +1325,7 @@ extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const v
   segs.n_seg = n_seg;
   segs.m_rows = m_rows;
   segs.e_stack = E_stack;
+  segs.split = 0;
   int total_m = -1;
   if (seg_on_device) {
     DMOE_REQUIRE(n_seg <= kMaxSegDev, "dmoe_grouped_gated_mlp: n_seg=%d > %d", n_seg, kMaxSegDev);
@@ -1353,6 +1351,18 @@ extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const v
   void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   cudaStream_t s = as_stream(stream);
   if (dtype == DMOE_BF16)
-    return run_mlp<DMOE_BF16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s);
-  return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s);
+    return run_mlp<DMOE_BF16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s,
+                              tile_policy);
+  return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s,
+                           tile_policy);
+}
+
+extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down,
+                                      int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
+                                      const int32_t* seg_end, int n_seg, int seg_on_device, int m_rows, int act,
+                                      void* Y, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                      void* stream) {
+  return dmoe_grouped_gated_mlp_ex(X, w_gate, w_up, w_down, E_stack, d, I, dtype, seg_expert, seg_end, n_seg,
+                                   seg_on_device, m_rows, act, Y, workspace, workspace_bytes, dev_status,
+                                   DMOE_TILES_AUTO, stream);
 }

@@ -172,6 +172,26 @@ int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const void* w_up, 
                            int32_t* dev_status, void* stream);
 
 /*
+ * dmoe_grouped_gated_mlp with a tile policy (no reference counterpart: how the segments are
+ * cut into tensor-core tiles).  DMOE_TILES_AUTO (what dmoe_grouped_gated_mlp uses) takes
+ * 256-row two-SM pair tiles when the segments average at least 128 rows of m_rows, else
+ * 128-row single-SM tiles; DMOE_TILES_PAIR / DMOE_TILES_SINGLE force one; and
+ * DMOE_TILES_PAIR_SPLIT runs every segment's whole 256-row blocks (and remainders over 128
+ * rows) as pair tiles and remainders of at most 128 rows as single-SM tiles (two launches
+ * per GEMM), for ragged experts of a few hundred rows.  With a device segment table the
+ * host cannot see the segment sizes, so a caller that knows the expected rows per expert
+ * picks the policy.
+ */
+#define DMOE_TILES_AUTO 0
+#define DMOE_TILES_PAIR 1
+#define DMOE_TILES_SINGLE 2
+#define DMOE_TILES_PAIR_SPLIT 3
+int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack,
+                              int d, int I, int dtype, const int32_t* seg_expert, const int32_t* seg_end, int n_seg,
+                              int seg_on_device, int m_rows, int act, void* Y, void* workspace,
+                              size_t workspace_bytes, int32_t* dev_status, int tile_policy, void* stream);
+
+/*
  * Number of SMs (0..64, process-wide, default 0) that later dmoe_grouped_gated_mlp launches
  * leave free.  No counterpart in the reference.  The grouped MLP is a persistent kernel that
  * holds each SM it gets until its last tile; where one GPU also serves other streams' short

@@ -303,7 +303,7 @@ def test_grouped_mlp_matches_fp32_reference(dtype, act, E, d, I, sizes):
 
 @gpu
 @pytest.mark.parametrize("env", [{"DMOE_GEMM_HYBRID": "1"}, {"DMOE_GEMM_RASTER": "0"}, {"DMOE_GEMM_RASTER": "1"},
-                                 {"DMOE_GEMM_VARIANT": "1sm"}])
+                                 {"DMOE_GEMM_VARIANT": "1sm"}, {"DMOE_GEMM_HYBRID": "1", "DMOE_GEMM_RASTER": "1"}])
 def test_grouped_mlp_launch_variants(env, monkeypatch):
     """The non-default launch shapes (pair tiles with single-SM remainders, the other tile
     orders, single-SM tiles only) give the same results."""
@@ -318,6 +318,33 @@ def test_grouped_mlp_launch_variants(env, monkeypatch):
     _status_ok()
     ref = _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act)
     _assert_close_bf16(Y[:ends[-1]].cpu(), ref[:ends[-1]])
+
+
+@gpu
+@pytest.mark.parametrize("policy", [1, 2, 3])
+@pytest.mark.parametrize("device_table", [False, True])
+def test_grouped_mlp_tile_policies(policy, device_table):
+    """Every tile policy (pair tiles, single-SM tiles, pairs with single-SM remainders) on a
+    ragged table (empty, 1, 128, 129, 256, 257, 300, 384, 385, 511 rows) gives the same
+    rows, with host and device segment tables; rows outside the segments stay untouched."""
+    N = _nat()
+    dtype, act = torch.bfloat16, O.ACT_SILU
+    sizes = [257, 0, 300, 1, 128, 129, 256, 384, 385, 511]
+    X, wg, wu, wd, experts, ends = _mlp_case(79 + policy, 10, 256, 384, sizes, dtype, act)
+    Y = torch.full((X.shape[0] + 64, 256), 7.0, dtype=dtype, device=DEV)
+    Xd = torch.cat([X, torch.zeros(64, X.shape[1], dtype=dtype)]).to(DEV)
+    if device_table:
+        se = torch.tensor(experts, dtype=torch.int32, device=DEV)
+        sn = torch.tensor(ends, dtype=torch.int32, device=DEV)
+    else:
+        se, sn = experts, ends
+    N.grouped_gated_mlp(Xd, wg.to(DEV), wu.to(DEV), wd.to(DEV), se, sn, act, Y, tile_policy=policy)
+    torch.cuda.synchronize()
+    _status_ok()
+    ref = _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act)
+    n = ends[-1]
+    _assert_close_bf16(Y[:n].cpu(), ref[:n])
+    assert torch.all(Y[n:].cpu() == 7.0), "rows outside the segments must stay untouched"
 
 
 @gpu
