@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import asyncio
 import math
+import os
 import struct
 import threading
 import timeit
@@ -653,7 +654,11 @@ class DistMoEBlock(nn.Module):
         rank sending about T tokens): the segment table is on the device, so the host cannot
         see the actual sizes.  Hundreds of rows per expert or more: 256-row pair tiles; a few
         hundred: pair tiles plus single-SM tiles for remainders of at most 128 rows (a
-        segment of 257-384 rows then costs three SM-tiles, not four); fewer: single-SM tiles."""
+        segment of 257-384 rows then costs three SM-tiles, not four); fewer: single-SM tiles.
+        DMOE_TILE_POLICY (0 auto, 1 pair, 2 single, 3 pair + single remainders) overrides."""
+        forced = os.environ.get("DMOE_TILE_POLICY")
+        if forced:
+            return int(forced)
         ep = self._ep
         expected = ep["world"] * T * self.top_k / max(1, ep["inst"].n_inst)
         if expected >= 768:
