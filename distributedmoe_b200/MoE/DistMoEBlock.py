@@ -678,7 +678,6 @@ class DistMoEBlock(nn.Module):
         out = torch.empty(x.shape, dtype=self.dtype, device=dev)
         self.output_batch = out
         shared = self.shared_expert is not None and T > 0
-        shared_done = self._launch_shared_expert(x) if shared else None
         if not capturing:
             self._direct_alive()
         table = (ep["alive"][:E], ep["alive"][E:], ep["inst_rank"], ep["inst_slot"], ep["inst_first"])
@@ -692,6 +691,12 @@ class DistMoEBlock(nn.Module):
         inst = ep["inst"]
         N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, tmo, placement + (ep["seg_expert"], ep["seg_end"]))
         N.ep_dispatch(win, x, T, k, E, offsets, perm_token, placement, ep["inst_rank"], cap, ep["ret"], ep["done"])
+        if shared:
+            # The shared expert runs here, on this stream: the routing kernels before it did not
+            # wait for its SMs, and it hides the wait for the other ranks' rows.
+            g, u, dn = self.shared_expert
+            N.grouped_gated_mlp(x, g, u, dn, [0], [T], ACTIVATIONS[self.config.activation], out,
+                                op_name="shared_expert_mlp")
         # This GPU's expert instances, once, over every host's rows (the expert blocks' part).
         N.ep_wait(win, N.EP_FLAG_DATA, tmo, dev)
         if ep["n_local"] > 0:
@@ -703,8 +708,6 @@ class DistMoEBlock(nn.Module):
         N.ep_signal(win, N.EP_FLAG_RESULTS, dev)
         N.ep_wait(win, N.EP_FLAG_RESULTS, tmo, dev)
         if T > 0:
-            if shared_done is not None:
-                torch.cuda.current_stream(dev).wait_event(shared_done)
             N.ep_combine(win, inverse, ep["ret"], w, T, k, out, accumulate=shared)
         if self.metrics_collector is not None and not capturing:
             self.metrics_collector.end_forward_pass()
