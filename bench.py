@@ -738,9 +738,10 @@ def run_movers(args):
     score_bias = torch.randn(E, generator=gen, device=dev) * w.score_bias_std if w.score_bias_std else None
     n = T * k
     recv = torch.empty(n, D, dtype=torch.bfloat16, device=dev)
+    back = torch.full((n,), -1, dtype=torch.int32, device=dev)
     rows = _randn_bf16((n, D), 1.0, gen, dev)
     flags = torch.zeros(N.ep_flags_bytes() // 8, dtype=torch.int64, device=dev)
-    win = N.ep_window(1, 0, [flags.data_ptr()], [0], [recv.data_ptr()], [rows.data_ptr()])
+    win = N.ep_window(1, 0, [flags.data_ptr()], [0], [recv.data_ptr()], [back.data_ptr()], [rows.data_ptr()])
     inst = InstanceTable.from_blocks([list(range(E))], [0], 1, E)
     alive_n, alive_inst = inst.alive_arrays([True])
     i32 = dict(dtype=torch.int32, device=dev)
@@ -757,9 +758,10 @@ def run_movers(args):
     def one():
         idx, wts, _ = N.router(x, w_r, k, mode=mode, renormalize=True, scale=w.scale, score_bias=score_bias,
                                n_group=w.n_group, topk_group=w.topk_group, w_dtype=torch.float32)
-        plan = N.route_plan(idx, None, E, want_slot=False, want_weight=False)
+        plan = N.route_plan(idx, None, E, want_slot=True, want_weight=False)
         N.ep_plan(win, plan["counts"], E, E, N.EP_POLICY_ROTATE, table, n, 10**9, place + segs)
-        N.ep_dispatch(win, x, T, k, E, plan["offsets"], plan["perm_token"], place, table[2], n, ret, done)
+        N.ep_dispatch(win, x, T, k, E, plan["offsets"], plan["perm_token"], plan["perm_slot"], place, table[2], n, ret,
+                      done)
         N.ep_combine(win, plan["inverse"], ret, wts, T, k, out)
 
     for _ in range(args.warmup):
@@ -772,7 +774,7 @@ def run_movers(args):
     N.enable_kernel_timing(False)
     N.check_device_status(dev)
     _, _, hbm, src = _peaks()
-    nbytes = {"router": T * D * 2 + E * D * 2 + n * 12, "ep_dispatch": 2 * n * D * 2 + n * 8,
+    nbytes = {"router": T * D * 2 + E * D * 2 + n * 12, "ep_dispatch": 2 * n * D * 2 + n * 12,
               "ep_combine": n * D * 2 + T * D * 2 + n * 12}
     res = {}
     for name, r in recs.items():

@@ -581,7 +581,7 @@ class DistMoEBlock(nn.Module):
             raise NotImplementedError("the device-driven data plane computes in bf16 or fp16")
         dev = self.device
         with torch.cuda.device(dev):
-            tte.open_window(capacity, d, self.dtype, inst.n_inst, dev)
+            tte.open_window(capacity, max(max_tokens * k, 1), d, self.dtype, inst.n_inst, dev)
             descs = exchange(tte.window_descriptor())
             win = tte.attach_windows(descs, rank)
             i32 = dict(dtype=torch.int32, device=dev)
@@ -684,13 +684,15 @@ class DistMoEBlock(nn.Module):
         placement = (ep["part_n"], ep["part_inst"], ep["part_start"], ep["dest_off"])
         if T > 0:
             idx, w = self._route(x, w_dtype=torch.float32)
-            plan = N.route_plan(idx, None, E, want_slot=False, want_weight=False)
+            plan = N.route_plan(idx, None, E, want_slot=True, want_weight=False)
             counts, offsets, perm_token, inverse = plan["counts"], plan["offsets"], plan["perm_token"], plan["inverse"]
+            perm_slot = plan["perm_slot"]
         else:
-            counts = offsets = perm_token = inverse = w = None
+            counts = offsets = perm_token = perm_slot = inverse = w = None
         inst = ep["inst"]
         N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, tmo, placement + (ep["seg_expert"], ep["seg_end"]))
-        N.ep_dispatch(win, x, T, k, E, offsets, perm_token, placement, ep["inst_rank"], cap, ep["ret"], ep["done"])
+        N.ep_dispatch(win, x, T, k, E, offsets, perm_token, perm_slot, placement, ep["inst_rank"], cap, ep["ret"],
+                      ep["done"])
         if shared:
             # The shared expert runs here, on this stream: the routing kernels before it did not
             # wait for its SMs, and it hides the wait for the other ranks' rows.
@@ -700,11 +702,11 @@ class DistMoEBlock(nn.Module):
         # This GPU's expert instances, once, over every host's rows (the expert blocks' part).
         N.ep_wait(win, N.EP_FLAG_DATA, tmo, dev)
         if ep["n_local"] > 0:
+            # The down-projection stores every row straight into its host's return rows.
             g, u, dn = ep["stack"]
-            tte = self.tensor_transfer_engine
-            N.grouped_gated_mlp(tte.recv, g, u, dn, ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]],
-                                ACTIVATIONS[self.config.activation], tte.out, m_rows=cap,
-                                tile_policy=self._direct_tile_policy(T))
+            rows = T * k if ep["world"] == 1 else None
+            N.ep_expert_mlp(win, g, u, dn, ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]], cap,
+                            ACTIVATIONS[self.config.activation], self._direct_tile_policy(T), work_rows=rows)
         N.ep_signal(win, N.EP_FLAG_RESULTS, dev)
         N.ep_wait(win, N.EP_FLAG_RESULTS, tmo, dev)
         if T > 0:

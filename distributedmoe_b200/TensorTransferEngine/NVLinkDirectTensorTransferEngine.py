@@ -7,8 +7,11 @@ events) stays available.  On top, each engine owns one window in its GPU's memor
 * ``recv``   [capacity, d]  the rows every host dispatches to this GPU's expert instances
              (the input buffer of the GPU's expert blocks, written by the senders' gather
              kernel through peer pointers);
-* ``out``    [capacity, d]  the grouped-MLP output of ``recv``, read back by the senders'
-             combine kernel through peer pointers;
+* ``back``   [capacity] int32  each receive row's return address (host rank, token * k +
+             slot), written by the senders' gather beside the row;
+* ``rows``   [max_tokens * k, d]  this host's expert outputs in (token, slot) order, written
+             by the owners' down-projection epilogues through peer pointers (the host's
+             output buffer), read by its own combine;
 * ``flags``  epoch flags [kind][sender] that senders and receivers raise on each other;
 * ``counts`` the per-instance row counts every sender writes before dispatching.
 
@@ -38,7 +41,8 @@ class NVLinkDirectTensorTransferEngine(NVLinkTensorTransferEngine):
     def __init__(self, config) -> None:
         super().__init__(config)
         self.recv: Optional[torch.Tensor] = None
-        self.out: Optional[torch.Tensor] = None
+        self.back: Optional[torch.Tensor] = None
+        self.rows: Optional[torch.Tensor] = None
         self.flags: Optional[torch.Tensor] = None
         self.counts: Optional[torch.Tensor] = None
         self.capacity = 0
@@ -46,25 +50,29 @@ class NVLinkDirectTensorTransferEngine(NVLinkTensorTransferEngine):
         self._peer_regions: List[list] = []
         self.window: Optional[N.EpWindow] = None
 
-    def open_window(self, capacity: int, hidden: int, dtype: torch.dtype, n_inst: int, device: torch.device) -> None:
-        """Allocate and register this GPU's window (flags and counts zeroed)."""
+    def open_window(self, capacity: int, return_rows: int, hidden: int, dtype: torch.dtype, n_inst: int,
+                    device: torch.device) -> None:
+        """Allocate and register this GPU's window (flags and counts zeroed).  capacity:
+        receive rows; return_rows: this host's max_tokens * top_k."""
         if self.recv is not None:
             raise RuntimeError("the window is already open")
-        if capacity < 1:
-            raise ValueError("the receive window needs at least one row")
+        if capacity < 1 or return_rows < 1:
+            raise ValueError("the window needs at least one receive row and one return row")
         device = torch.device(device)
         with torch.cuda.device(device):
             self.recv = torch.empty(capacity, hidden, dtype=dtype, device=device)
-            self.out = torch.empty(capacity, hidden, dtype=dtype, device=device)
+            self.back = torch.full((capacity,), -1, dtype=torch.int32, device=device)
+            self.rows = torch.empty(return_rows, hidden, dtype=dtype, device=device)
             self.flags = torch.zeros(N.ep_flags_bytes() // 8, dtype=torch.int64, device=device)
             self.counts = torch.zeros(max(N.ep_counts_bytes(n_inst) // 4, 1), dtype=torch.int32, device=device)
             torch.cuda.synchronize(device)  # zeros are in place before any peer can see the window
         self.capacity = capacity
-        regions, _ = self.register_batch([self.flags, self.counts, self.recv, self.out], "VRAM", device.index)
+        regions, _ = self.register_batch([self.flags, self.counts, self.recv, self.back, self.rows], "VRAM",
+                                         device.index)
         self._window_regions = regions
 
     def window_descriptor(self) -> bytes:
-        """Serialized descriptors of this window's four regions (flags, counts, recv, out)."""
+        """Serialized descriptors of this window's regions (flags, counts, recv, back, rows)."""
         if self._window_regions is None:
             raise RuntimeError("open_window first")
         _, blob = self.serialize_descs(self._window_regions)
@@ -76,15 +84,15 @@ class NVLinkDirectTensorTransferEngine(NVLinkTensorTransferEngine):
         world = len(descriptors)
         if not 1 <= world <= N.EP_MAX_RANKS:
             raise ValueError(f"{world} ranks; 1..{N.EP_MAX_RANKS} supported")
-        flags, counts, recv, out = [], [], [], []
+        flags, counts, recv, back, rows = [], [], [], [], []
         self._peer_regions = []
         for g, blob in enumerate(descriptors):
             (cap,) = struct.unpack("!Q", blob[:8])
             if cap != self.capacity:
                 raise ValueError(f"rank {g} opened a window of {cap} rows, this rank {self.capacity}")
             regions = self.deserialize_descs((len(blob) - 8, blob[8:]))
-            if len(regions) != 4:
-                raise ValueError("a window descriptor holds four regions")
+            if len(regions) != 5:
+                raise ValueError("a window descriptor holds five regions")
             if g != rank and regions[0].device == self.recv.device.index and regions[0].pid != self.pid:
                 raise ValueError("two ranks share one GPU: the exchange needs a GPU per rank")
             self._peer_regions.append(regions)
@@ -92,8 +100,9 @@ class NVLinkDirectTensorTransferEngine(NVLinkTensorTransferEngine):
             flags.append(ptrs[0])
             counts.append(ptrs[1])
             recv.append(ptrs[2])
-            out.append(ptrs[3])
-        self.window = N.ep_window(world, rank, flags, counts, recv, out)
+            back.append(ptrs[3])
+            rows.append(ptrs[4])
+        self.window = N.ep_window(world, rank, flags, counts, recv, back, rows)
         return self.window
 
     def close(self) -> None:

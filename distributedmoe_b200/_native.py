@@ -51,11 +51,12 @@ _sz = ctypes.c_size_t
 
 
 class EpWindow(ctypes.Structure):
-    """``dmoe_ep_window``: every rank's flags, count matrix, receive and output rows, as
-    this process addresses them (its own memory, or CUDA-IPC mappings of the peers')."""
+    """``dmoe_ep_window``: every rank's flags, count matrix, receive rows, back map and return
+    rows, as this process addresses them (its own memory, or CUDA-IPC mappings of the
+    peers')."""
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
                 ("flags", _vp * EP_MAX_RANKS), ("counts", _vp * EP_MAX_RANKS),
-                ("recv", _vp * EP_MAX_RANKS), ("out", _vp * EP_MAX_RANKS)]
+                ("recv", _vp * EP_MAX_RANKS), ("back", _vp * EP_MAX_RANKS), ("rows", _vp * EP_MAX_RANKS)]
 
 # name -> (restype, argtypes); mirrors include/dmoe_b200.h
 SIGNATURES = {
@@ -95,7 +96,10 @@ SIGNATURES = {
     "dmoe_ep_plan": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _i64,
                                     _u64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dmoe_ep_dispatch": (ctypes.c_int, [_vp, _vp, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp,
-                                        _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+                                        _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "dmoe_ep_expert_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          _vp, _vp, ctypes.c_int, _i64, ctypes.c_int, _vp, _sz, _vp, ctypes.c_int,
+                                          _vp]),
     "dmoe_ep_wait": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _vp, _vp]),
     "dmoe_ep_signal": (ctypes.c_int, [_vp, ctypes.c_int, _vp]),
     "dmoe_ep_combine": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -573,11 +577,11 @@ def ep_counts_bytes(n_inst: int) -> int:
 
 
 def ep_window(world: int, rank: int, flags: Sequence[int], counts: Sequence[int], recv: Sequence[int],
-              out: Sequence[int]) -> EpWindow:
+              back: Sequence[int], rows: Sequence[int]) -> EpWindow:
     w = EpWindow()
     w.world, w.rank = int(world), int(rank)
     for g in range(world):
-        w.flags[g], w.counts[g], w.recv[g], w.out[g] = flags[g], counts[g], recv[g], out[g]
+        w.flags[g], w.counts[g], w.recv[g], w.back[g], w.rows[g] = flags[g], counts[g], recv[g], back[g], rows[g]
     return w
 
 
@@ -601,19 +605,41 @@ def ep_plan(win: EpWindow, counts_e: Optional[torch.Tensor], E: int, n_inst: int
 
 
 def ep_dispatch(win: EpWindow, x: torch.Tensor, T: int, k: int, E: int, offsets: Optional[torch.Tensor],
-                perm_token: Optional[torch.Tensor], placement, inst_rank: torch.Tensor, cap: int,
-                ret: torch.Tensor, done: torch.Tensor, stream: Optional[int] = None) -> None:
-    """Gather rows into their receivers' buffers (peer stores) and raise the data flags.
-    placement: (part_n, part_inst, part_start, dest_off) from :func:`ep_plan`."""
+                perm_token: Optional[torch.Tensor], perm_slot: Optional[torch.Tensor], placement,
+                inst_rank: torch.Tensor, cap: int, ret: torch.Tensor, done: torch.Tensor,
+                stream: Optional[int] = None) -> None:
+    """Gather rows (and their return addresses) into their receivers' windows (peer stores)
+    and raise the data flags.  placement: (part_n, part_inst, part_start, dest_off) from
+    :func:`ep_plan`."""
     part_n, part_inst, part_start, dest_off = placement
     dev = inst_rank.device
     st = stream if stream is not None else _stream(dev)
     tm = _Timed("ep_dispatch", st, dev)
     rc = lib().dmoe_ep_dispatch(ctypes.byref(win), _ptr(x), x.shape[-1] * x.element_size(), T, k, E, _ptr(offsets),
-                                _ptr(perm_token), part_n.data_ptr(), part_inst.data_ptr(), part_start.data_ptr(),
+                                _ptr(perm_token), _ptr(perm_slot), part_n.data_ptr(), part_inst.data_ptr(),
+                                part_start.data_ptr(),
                                 inst_rank.data_ptr(), dest_off.data_ptr(), int(cap), ret.data_ptr(), done.data_ptr(),
                                 scratch.status(dev).data_ptr(), st)
     _check(rc, "dmoe_ep_dispatch")
+    tm.done()
+
+
+def ep_expert_mlp(win: EpWindow, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
+                  seg_expert: torch.Tensor, seg_end: torch.Tensor, cap: int, act: int,
+                  tile_policy: int = TILES_AUTO, work_rows: Optional[float] = None) -> None:
+    """The exchange's expert step: grouped MLP over this rank's receive rows, the
+    down-projection stored straight into the hosts' return rows.  work_rows: the rows
+    computed, if known, for the timing record's FLOPs."""
+    dev = _require_cuda(w_gate, w_up, w_down, seg_expert, seg_end)
+    E, I, d = w_gate.shape
+    dt = dtype_code(w_gate.dtype)
+    ws = scratch.get(dev, "mlp", lib().dmoe_grouped_mlp_workspace_size(cap, I, dt))
+    tm = _Timed("grouped_gated_mlp", _stream(dev), dev, None if work_rows is None else 6.0 * work_rows * d * I)
+    rc = lib().dmoe_ep_expert_mlp(ctypes.byref(win), w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), E, d, I, dt,
+                                  seg_expert.data_ptr(), seg_end.data_ptr(), seg_expert.numel(), int(cap), int(act),
+                                  ws.data_ptr(), ws.numel(), scratch.status(dev).data_ptr(), int(tile_policy),
+                                  _stream(dev))
+    _check(rc, "dmoe_ep_expert_mlp")
     tm.done()
 
 

@@ -7,17 +7,19 @@
 //   READ of the host's input buffer       (MoE/pools/BuffersPool.py:55-71, PipelineTask.py:459)
 //   WRITE of the expert output            (MoE/pools/BuffersPool.py:73-90, PipelineTask.py:555)
 //   HostOutputBufferUnlocked + combine    (MoE/PipelineTask.py:306-370, 558-565)
-// with four kernels around one grouped-MLP launch per GPU:
+// with these kernels around one grouped-MLP launch per GPU:
 //   ep_plan      exchange per-instance row counts with every rank (peer stores + an epoch
 //                flag), then derive where this rank's rows land in each receiver's buffer
 //                and this GPU's grouped-MLP segment table.
 //   ep_dispatch  gather this rank's rows straight into the receivers' registered buffers
-//                (peer stores over NVLink), remember each row's (rank, row) address, and
-//                raise the data flag on every rank once the last CTA is done.
+//                (peer stores over NVLink) with each row's return address (this rank,
+//                token * k + slot) in the receiver's back map, remember each row's (rank,
+//                row), and raise the data flag on every rank once the last CTA is done.
 //   ep_wait      bounded wait until every rank's flag of a kind reached the epoch.
 //   ep_signal    raise this rank's result flag on every rank after the grouped MLP.
-//   ep_combine   per token, read its k expert rows back from the owners' output buffers
-//                (peer loads) and store the weighted fp32 sum once.
+//   ep_combine   per token, sum its k expert rows, which the owners' down-projection
+//                epilogues stored into this rank's return rows (peer stores during the
+//                GEMM, dmoe_ep_expert_mlp), weighted in fp32, and store once.
 //
 // An expert "instance" is one copy of an expert's weights on one rank (replicas give an
 // expert several instances).  Instances are numbered rank-major and, within a rank, in the
@@ -50,7 +52,8 @@ struct EpPeers {
   uint64_t* flags[kMaxRanks];   // [kFlagKinds][kMaxRanks] epochs of each rank
   int32_t* counts[kMaxRanks];   // [2][kMaxRanks][n_inst] count matrix of each rank
   char* recv[kMaxRanks];        // receive rows of each rank
-  const char* out[kMaxRanks];   // expert-output rows of each rank
+  int32_t* back[kMaxRanks];     // back map of each rank's receive rows
+  char* rows[kMaxRanks];        // return rows of each rank, (token, slot) order
 };
 
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
@@ -246,6 +249,8 @@ struct EpDispatchArgs {
   int E;
   const int32_t* offsets;    // [E + 1] permuted-order start of each expert
   const int32_t* perm_token; // [n]
+  const int32_t* perm_slot;  // [n]
+  int k;
   const int32_t* part_n;
   const int32_t* part_inst;
   const int32_t* part_start;
@@ -332,7 +337,11 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
       const int64_t row = (int64_t)pl->base[q] + i;
       if (row < a.cap) {
         code = (int32_t)(((uint32_t)r << kRowShift) | (uint32_t)row);
-        const uint4* src = reinterpret_cast<const uint4*>(a.x) + (int64_t)a.perm_token[p] * a.row_vecs;
+        const int tok = a.perm_token[p];
+        if (lane == 0)
+          a.peers.back[r][row] =
+              (int32_t)(((uint32_t)a.peers.rank << kRowShift) | (uint32_t)(tok * a.k + a.perm_slot[p]));
+        const uint4* src = reinterpret_cast<const uint4*>(a.x) + (int64_t)tok * a.row_vecs;
         uint4* d = reinterpret_cast<uint4*>(a.peers.recv[r]) + row * a.row_vecs;
         int64_t c = lane;
         for (; c + 224 < a.row_vecs; c += 256) {
@@ -385,7 +394,7 @@ __global__ void ep_signal_kernel(EpPeers peers, int kind) {
 
 // ------------------------------------------------------------------------- ep_combine
 template <int DT, int KU, int CU>
-__global__ void __launch_bounds__(256) ep_combine_kernel(EpPeers peers, const int32_t* __restrict__ inverse,
+__global__ void __launch_bounds__(256) ep_combine_kernel(const char* __restrict__ rows, const int32_t* __restrict__ inverse,
                                                          const int32_t* __restrict__ ret, const void* __restrict__ w,
                                                          int w_dtype, int T, int k, int d, int accumulate,
                                                          void* __restrict__ out) {
@@ -402,15 +411,13 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpPeers peers, const in
       src[s] = nullptr;
       wt[s] = 0.f;
       if (s < k) {
+        // The owner's epilogue wrote slot (t, s) at row t*k + s unless the activation was
+        // dropped (no alive instance, or past a receive buffer's capacity).
         const int32_t pos = inverse[(int64_t)t * k + s];
         const int32_t code = pos < 0 ? -1 : ret[pos];
         if (code >= 0) {
-          const int r = (int)((uint32_t)code >> kRowShift);
-          const int64_t row = code & ((1 << kRowShift) - 1);
-          if (r < peers.world) {
-            src[s] = reinterpret_cast<const uint4*>(peers.out[r]) + row * row_vecs;
-            wt[s] = load_as_float(w, (int64_t)t * k + s, w_dtype);
-          }
+          src[s] = reinterpret_cast<const uint4*>(rows) + ((int64_t)t * k + s) * row_vecs;
+          wt[s] = load_as_float(w, (int64_t)t * k + s, w_dtype);
         }
       }
     }
@@ -456,16 +463,16 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpPeers peers, const in
 }
 
 template <int DT>
-void launch_ep_combine(int blocks, cudaStream_t s, const EpPeers& peers, const int32_t* inverse, const int32_t* ret,
+void launch_ep_combine(int blocks, cudaStream_t s, const char* rows, const int32_t* inverse, const int32_t* ret,
                        const void* w, int w_dtype, int T, int k, int d, int accumulate, void* out) {
   if (k <= 2)
-    ep_combine_kernel<DT, 2, 4><<<blocks, 256, 0, s>>>(peers, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+    ep_combine_kernel<DT, 2, 4><<<blocks, 256, 0, s>>>(rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   else if (k <= 4)
-    ep_combine_kernel<DT, 4, 2><<<blocks, 256, 0, s>>>(peers, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+    ep_combine_kernel<DT, 4, 2><<<blocks, 256, 0, s>>>(rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   else if (k <= 8)
-    ep_combine_kernel<DT, 8, 1><<<blocks, 256, 0, s>>>(peers, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+    ep_combine_kernel<DT, 8, 1><<<blocks, 256, 0, s>>>(rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   else
-    ep_combine_kernel<DT, 16, 1><<<blocks, 256, 0, s>>>(peers, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+    ep_combine_kernel<DT, 16, 1><<<blocks, 256, 0, s>>>(rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
 }
 
 int fill_peers(EpPeers* p, const dmoe_ep_window* w) {
@@ -479,10 +486,12 @@ int fill_peers(EpPeers* p, const dmoe_ep_window* w) {
     p->flags[g] = in ? reinterpret_cast<uint64_t*>(w->flags[g]) : nullptr;
     p->counts[g] = in ? reinterpret_cast<int32_t*>(w->counts[g]) : nullptr;
     p->recv[g] = in ? reinterpret_cast<char*>(w->recv[g]) : nullptr;
-    p->out[g] = in ? reinterpret_cast<const char*>(w->out[g]) : nullptr;
+    p->back[g] = in ? reinterpret_cast<int32_t*>(w->back[g]) : nullptr;
+    p->rows[g] = in ? reinterpret_cast<char*>(w->rows[g]) : nullptr;
     if (in) {
-      DMOE_REQUIRE(w->recv[g] && w->out[g] && aligned16(w->recv[g]) && aligned16(w->out[g]),
-                   "dmoe_ep: rank %d's rows must be 16-byte aligned device pointers", g);
+      DMOE_REQUIRE(w->recv[g] && w->rows[g] && w->back[g] && aligned16(w->recv[g]) && aligned16(w->rows[g]),
+                   "dmoe_ep: rank %d's receive rows, back map and return rows must be device pointers (rows "
+                   "16-byte aligned)", g);
       DMOE_REQUIRE(w->flags[g] != nullptr, "dmoe_ep: rank %d has no flag array", g);
       if (w->world > 1) DMOE_REQUIRE(w->counts[g] != nullptr, "dmoe_ep: rank %d has no count matrix", g);
     }
@@ -544,10 +553,10 @@ extern "C" int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, 
 }
 
 extern "C" int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_t row_bytes, int T, int k, int E,
-                                const int32_t* offsets, const int32_t* perm_token, const int32_t* part_n,
-                                const int32_t* part_inst, const int32_t* part_start, const int32_t* inst_rank,
-                                const int32_t* dest_off, int64_t cap, int32_t* ret, uint32_t* done,
-                                int32_t* dev_status, void* stream) {
+                                const int32_t* offsets, const int32_t* perm_token, const int32_t* perm_slot,
+                                const int32_t* part_n, const int32_t* part_inst, const int32_t* part_start,
+                                const int32_t* inst_rank, const int32_t* dest_off, int64_t cap, int32_t* ret,
+                                uint32_t* done, int32_t* dev_status, void* stream) {
   clear_error();
   EpDispatchArgs a{};
   int r = fill_peers(&a.peers, win);
@@ -559,13 +568,19 @@ extern "C" int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_
   DMOE_REQUIRE(cap >= 0 && cap < (1ll << kRowShift), "dmoe_ep_dispatch: capacity %lld rows", (long long)cap);
   DMOE_REQUIRE(done && dev_status && part_n && part_inst && part_start && inst_rank && dest_off,
                "dmoe_ep_dispatch: null pointer");
-  if (T > 0) DMOE_REQUIRE(x && aligned16(x) && offsets && perm_token && ret, "dmoe_ep_dispatch: null or unaligned x");
+  if (T > 0)
+    DMOE_REQUIRE(x && aligned16(x) && offsets && perm_token && perm_slot && ret,
+                 "dmoe_ep_dispatch: null or unaligned x, or a missing plan array");
+  DMOE_REQUIRE((int64_t)T * k < (1ll << kRowShift), "dmoe_ep_dispatch: T*k=%lld exceeds 2^27 return rows",
+               (long long)T * k);
   a.x = reinterpret_cast<const char*>(x);
   a.row_vecs = row_bytes / 16;
   a.n = (int64_t)T * k;
   a.E = E;
   a.offsets = offsets;
   a.perm_token = perm_token;
+  a.perm_slot = perm_slot;
+  a.k = k;
   a.part_n = part_n;
   a.part_inst = part_inst;
   a.part_start = part_start;
@@ -627,10 +642,11 @@ extern "C" int dmoe_ep_combine(const dmoe_ep_window* win, const int32_t* inverse
   int blocks = (T + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   cudaStream_t s = as_stream(stream);
+  const char* rows = p.rows[p.rank];
   if (dtype == DMOE_BF16)
-    launch_ep_combine<DMOE_BF16>(blocks, s, p, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+    launch_ep_combine<DMOE_BF16>(blocks, s, rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   else
-    launch_ep_combine<DMOE_F16>(blocks, s, p, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+    launch_ep_combine<DMOE_F16>(blocks, s, rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }

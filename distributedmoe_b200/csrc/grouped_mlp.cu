@@ -72,7 +72,24 @@ struct GemmArgs {
   int prefetch;     // k-blocks of L2 prefetch ahead of the TMA loads (0: off)
   int32_t* status;
   int out_f32;      // plain GEMM only: store the fp32 accumulators instead of rounding to DT
+  // plain GEMM only: instead of row r of `out`, store row r at scatter_base[code >> 27] +
+  // (code & 0x7ffffff) rows, code = scatter_map[r] (code < 0: the row is not stored).  The
+  // bases may be other GPUs' memory (peer stores over NVLink).
+  int scatter;
+  const int32_t* scatter_map;
+  char* scatter_base[DMOE_EP_MAX_RANKS];
 };
+
+// Destination of output row `row` of a plain GEMM (nullptr: not stored).
+__device__ __forceinline__ char* out_row(const GemmArgs& args, int row, bool valid) {
+  if (!valid) return nullptr;
+  if (!args.scatter) return reinterpret_cast<char*>(args.out) + (int64_t)row * args.ldo * 2;
+  const int32_t code = args.scatter_map[row];
+  if (code < 0) return nullptr;
+  char* base = args.scatter_base[(uint32_t)code >> 27];  // index <= 15: code is non-negative
+  if (base == nullptr) return nullptr;                    // no such rank: never stored
+  return base + (int64_t)(code & 0x7ffffff) * args.ldo * 2;
+}
 
 // ------------------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -518,6 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
+        char* const drow = args.out_f32 ? nullptr : out_row(args, row, valid);
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
           uint32_t y[32];
@@ -530,11 +548,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int v = 0; v < 8; ++v)
               if (col0 + v * 4 < args.n_out)
                 *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-          } else if (valid) {
+          } else if (drow != nullptr) {
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
-            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+            char* dst = drow + (int64_t)col0 * 2;
 #pragma unroll
             for (int v = 0; v < 4; ++v)
               if (col0 + v * 8 < args.n_out)
@@ -550,6 +568,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // Scattered rows may live in other GPUs' memory: make them visible system-wide before the
+  // kernel ends (the caller raises a flag the other GPUs act on after this launch).
+  if (args.scatter) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -891,6 +912,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
+        char* const drow = args.out_f32 ? nullptr : out_row(args, row, valid);
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
           uint32_t y[32];
@@ -903,11 +925,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int v = 0; v < 8; ++v)
               if (col0 + v * 4 < args.n_out)
                 *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-          } else if (valid) {
+          } else if (drow != nullptr) {
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
-            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+            char* dst = drow + (int64_t)col0 * 2;
 #pragma unroll
             for (int v = 0; v < 4; ++v)
               if (col0 + v * 8 < args.n_out)
@@ -923,6 +945,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (args.scatter) __threadfence_system();  // scattered rows may live in other GPUs' memory
   tc_fence_before();
   __syncthreads();
   // Exit handshake: tell the peer this CTA is done with the pair's shared state, then wait
@@ -1128,10 +1151,23 @@ int sm_count() {
   return cached[dev];
 }
 
+// Where GEMM2 stores its rows when they are scattered to their hosts (see GemmArgs::scatter).
+struct ScatterSpec {
+  const int32_t* map;
+  char* base[DMOE_EP_MAX_RANKS];
+};
+
+void apply_scatter(GemmArgs& a, const ScatterSpec* sc) {
+  if (sc == nullptr) return;
+  a.scatter = 1;
+  a.scatter_map = sc->map;
+  for (int g = 0; g < DMOE_EP_MAX_RANKS; ++g) a.scatter_base[g] = sc->base[g];
+}
+
 template <int DT>
 int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack, int d, int I,
             GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
-            cudaStream_t stream, int policy) {
+            cudaStream_t stream, int policy, const ScatterSpec* sc = nullptr) {
   CUtensorMap ta, tg, tu, th, td;
   {
     const uint64_t dims[2] = {(uint64_t)d, (uint64_t)m_rows};
@@ -1178,6 +1214,8 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
     GemmArgs s1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
     GemmArgs s2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
+    apply_scatter(a2, sc);
+    apply_scatter(s2, sc);
     const int sms = usable_sms();
     segs.split = 1;
     r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
@@ -1201,6 +1239,7 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
     GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
+    apply_scatter(a2, sc);
     // Pair tiles only.  With the segment-by-segment tile order a remainder's pair tile reads
     // the expert's weights from L2 next to the expert's other tiles, while a separate
     // single-SM launch re-reads them from DRAM after the pair launch (measured on the
@@ -1222,6 +1261,7 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
   int r = launch_gemm<true, DT>(ta, tg, tu, segs, a1, g1, stream);
   if (r) return r;
   GemmArgs a2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
+  apply_scatter(a2, sc);
   return launch_gemm<false, DT>(th, td, td, segs, a2, g2, stream);
 }
 
@@ -1365,4 +1405,52 @@ extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const v
   return dmoe_grouped_gated_mlp_ex(X, w_gate, w_up, w_down, E_stack, d, I, dtype, seg_expert, seg_end, n_seg,
                                    seg_on_device, m_rows, act, Y, workspace, workspace_bytes, dev_status,
                                    DMOE_TILES_AUTO, stream);
+}
+
+extern "C" int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate, const void* w_up, const void* w_down,
+                                  int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
+                                  const int32_t* seg_end, int n_seg, int64_t cap, int act, void* workspace,
+                                  size_t workspace_bytes, int32_t* dev_status, int tile_policy, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(win != nullptr && win->world >= 1 && win->world <= DMOE_EP_MAX_RANKS && win->rank >= 0 &&
+                   win->rank < win->world,
+               "dmoe_ep_expert_mlp: bad window table");
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_ep_expert_mlp: dtype must be f16 or bf16");
+  DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "dmoe_ep_expert_mlp: bad activation %d", act);
+  DMOE_REQUIRE(d > 0 && I > 0 && d % 8 == 0 && I % 8 == 0, "dmoe_ep_expert_mlp: d=%d, I=%d must be multiples of 8", d,
+               I);
+  DMOE_REQUIRE(E_stack >= 1 && n_seg >= 0 && n_seg <= kMaxSegDev, "dmoe_ep_expert_mlp: bad E_stack/n_seg");
+  DMOE_REQUIRE(cap >= 0 && cap < (1ll << 31), "dmoe_ep_expert_mlp: bad capacity");
+  DMOE_REQUIRE(tile_policy >= DMOE_TILES_AUTO && tile_policy <= DMOE_TILES_PAIR_SPLIT,
+               "dmoe_ep_expert_mlp: bad tile policy %d", tile_policy);
+  if (n_seg == 0 || cap == 0) return DMOE_OK;
+  const void* X = win->recv[win->rank];
+  DMOE_REQUIRE(X && win->back[win->rank] && w_gate && w_up && w_down && workspace && dev_status && seg_expert &&
+                   seg_end,
+               "dmoe_ep_expert_mlp: null pointer");
+  for (int g = 0; g < win->world; ++g)
+    DMOE_REQUIRE(win->rows[g] != nullptr && aligned16(win->rows[g]), "dmoe_ep_expert_mlp: rank %d has no return rows",
+                 g);
+  DMOE_REQUIRE(aligned16(X) && aligned16(w_gate) && aligned16(w_up) && aligned16(w_down) && aligned16(workspace),
+               "dmoe_ep_expert_mlp: tensors must be 16-byte aligned");
+  DMOE_REQUIRE(workspace_bytes >= dmoe_grouped_mlp_workspace_size((int)cap, I, dtype),
+               "dmoe_ep_expert_mlp: workspace %zu < %zu bytes", workspace_bytes,
+               dmoe_grouped_mlp_workspace_size((int)cap, I, dtype));
+  static thread_local GemmSegs segs;
+  segs.n_seg = n_seg;
+  segs.m_rows = (int)cap;
+  segs.e_stack = E_stack;
+  segs.split = 0;
+  segs.dev_expert = seg_expert;
+  segs.dev_end = seg_end;
+  ScatterSpec sc{};
+  sc.map = reinterpret_cast<const int32_t*>(win->back[win->rank]);
+  for (int g = 0; g < DMOE_EP_MAX_RANKS; ++g) sc.base[g] = g < win->world ? reinterpret_cast<char*>(win->rows[g]) : nullptr;
+  void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DMOE_BF16)
+    return run_mlp<DMOE_BF16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H, dev_status,
+                              s, tile_policy, &sc);
+  return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H, dev_status, s,
+                           tile_policy, &sc);
 }

@@ -270,15 +270,19 @@ int dmoe_flag_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, in
  *     MoE/pools/BuffersPool.py:73-90) -> dmoe_ep_signal / dmoe_ep_wait (epoch flags),
  *   HostPipelineTask.combine (MoE/PipelineTask.py:306-370) -> dmoe_ep_combine (peer loads).
  * Between dmoe_ep_wait(DATA) and dmoe_ep_signal(RESULTS) each rank runs ONE
- * dmoe_grouped_gated_mlp over its receive buffer with the device segment table that
- * dmoe_ep_plan wrote (seg_expert, seg_end; n_seg = the rank's instance count).
+ * dmoe_ep_expert_mlp over its receive buffer with the device segment table that
+ * dmoe_ep_plan wrote (seg_expert, seg_end; n_seg = the rank's instance count); its
+ * down-projection epilogue stores every row straight into its host's `rows` (the fused
+ * return path: the transfer overlaps the GEMM, and the combine reads local rows).
  *
  * Window: per rank, in its own GPU memory and mapped into every rank (CUDA IPC):
  *   flags   dmoe_ep_flags_bytes() of uint64, zero-initialised: epochs [kind][sender], then
  *           the rank's epoch counter (advanced by dmoe_ep_plan, read by the other calls)
  *   counts  dmoe_ep_counts_bytes(n_inst) of int32 [2][DMOE_EP_MAX_RANKS][n_inst]
  *   recv    [cap, d] rows other ranks dispatch to (instance-major, then sender rank)
- *   out     [cap, d] the grouped MLP's output rows of recv
+ *   back    [cap] int32: for each receive row, (sender rank << 27) | (token * k + slot)
+ *   rows    [max_tokens * k, d] this rank's expert outputs, written by the owners' grouped
+ *           MLP epilogues (peer stores) in (token, slot) order
  * The table passed to every call lists all ranks' windows as this process addresses them.
  * Instances (an expert's weights on one rank) are numbered rank-major; rank r's instances
  * are [inst_first[r], inst_first[r+1]) in the order of its weight stack (inst_slot).
@@ -303,7 +307,8 @@ typedef struct dmoe_ep_window {
   void* flags[DMOE_EP_MAX_RANKS];
   void* counts[DMOE_EP_MAX_RANKS];
   void* recv[DMOE_EP_MAX_RANKS];
-  void* out[DMOE_EP_MAX_RANKS];
+  void* back[DMOE_EP_MAX_RANKS];
+  void* rows[DMOE_EP_MAX_RANKS];
 } dmoe_ep_window;
 
 size_t dmoe_ep_flags_bytes(void);
@@ -325,14 +330,30 @@ int dmoe_ep_plan(const dmoe_ep_window* win, const int32_t* counts_e, int E, int 
                  int32_t* dev_status, void* stream);
 
 /*
- * Gather x[perm_token[p]] of every permuted activation p into its receiver's recv buffer
- * (peer stores), record ret[p] = (rank << 27) | row (-1: dropped), then raise the DATA flag
- * of this rank on every rank.  done: a zeroed uint32 of this rank's scratch.
+ * Gather x[perm_token[p]] of every permuted activation p into its receiver's recv buffer and
+ * (this rank << 27) | (perm_token[p] * k + perm_slot[p]) into the receiver's back map (peer
+ * stores), record ret[p] = (rank << 27) | row (-1: dropped), then raise the DATA flag of
+ * this rank on every rank.  done: a zeroed uint32 of this rank's scratch.
  */
 int dmoe_ep_dispatch(const dmoe_ep_window* win, const void* x, int64_t row_bytes, int T, int k, int E,
-                     const int32_t* offsets, const int32_t* perm_token, const int32_t* part_n, const int32_t* part_inst,
-                     const int32_t* part_start, const int32_t* inst_rank, const int32_t* dest_off, int64_t cap,
-                     int32_t* ret, uint32_t* done, int32_t* dev_status, void* stream);
+                     const int32_t* offsets, const int32_t* perm_token, const int32_t* perm_slot,
+                     const int32_t* part_n, const int32_t* part_inst, const int32_t* part_start,
+                     const int32_t* inst_rank, const int32_t* dest_off, int64_t cap, int32_t* ret, uint32_t* done,
+                     int32_t* dev_status, void* stream);
+
+/*
+ * The expert step of the exchange: the grouped gated MLP over this rank's receive buffer
+ * (rows [0, cap), device segment table seg_expert / seg_end of n_seg local instances), whose
+ * down-projection stores each row r at rows[back[r] >> 27] + (back[r] & 0x7ffffff) rows --
+ * the host's return buffer, over NVLink for other ranks -- instead of an output buffer.
+ * Replaces ExpertsBlockPipelineTask.run + the WRITE to the host's output buffer
+ * (MoE/PipelineTask.py:478-520,555).  workspace >= dmoe_grouped_mlp_workspace_size(cap, I,
+ * dtype); tile_policy as dmoe_grouped_gated_mlp_ex.
+ */
+int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate, const void* w_up, const void* w_down,
+                       int E_stack, int d, int I, int dtype, const int32_t* seg_expert, const int32_t* seg_end,
+                       int n_seg, int64_t cap, int act, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                       int tile_policy, void* stream);
 
 /* Wait (bounded) until every other rank raised its flag of `kind` to this forward's epoch. */
 int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t timeout_ns, int32_t* dev_status, void* stream);
@@ -342,8 +363,9 @@ int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t timeout_ns, int32
 int dmoe_ep_signal(const dmoe_ep_window* win, int kind, void* stream);
 
 /*
- * out[t] = (out[t] if accumulate) + sum_s w[t,s] * out_rows_of(ret[inverse[t*k+s]]), reading
- * each row from its owner's `out` buffer (peer loads), fp32 accumulation, one store.
+ * out[t] = (out[t] if accumulate) + sum_s w[t,s] * rows[t*k + s], over this rank's own return
+ * rows (written by the owners' epilogues), skipping slots whose activation was dropped
+ * (ret[inverse[t*k+s]] < 0); fp32 accumulation, one store.
  */
 int dmoe_ep_combine(const dmoe_ep_window* win, const int32_t* inverse, const int32_t* ret, const void* w, int w_dtype,
                     int T, int k, int d, int dtype, int accumulate, void* out, void* stream);

@@ -2,7 +2,8 @@
 
 * The exchange kernels' bookkeeping (dmoe_ep_plan / dmoe_ep_dispatch) against the CPU
   restatement in ``oracle/ep_placement.py``, bit for bit: parts, receive offsets, segment
-  table, per-activation destinations, and the rows that land in the receive buffer.
+  table, per-activation destinations, the rows that land in the receive buffer and their
+  return addresses in the back map.
 * The layer through ``DistMoEBlock.forward`` on the direct plane against the oracle:
   one block, several blocks with replicas (even split over alive replicas, one block lost
   mid-run), rotation over replicas, an expert with no alive block (its rows leave the sum),
@@ -74,14 +75,15 @@ def test_exchange_bookkeeping_matches_restatement(policy):
     n[5] = 0  # expert 5 is in no block: its rows are dropped
     g = torch.Generator(device=DEV).manual_seed(5)
     idx = torch.stack([torch.randperm(E, generator=g, device=DEV)[:k] for _ in range(T)])
-    plan = N.route_plan(idx, None, E, want_slot=False, want_weight=False)
+    plan = N.route_plan(idx, None, E, want_slot=True, want_weight=False)
     counts = plan["counts"].cpu().tolist()
     cap = T * k
     x = torch.randn(T, d, generator=g, device=DEV).to(torch.bfloat16)
     recv = torch.zeros(cap, d, dtype=torch.bfloat16, device=DEV)
-    out = torch.zeros_like(recv)
+    back = torch.full((cap,), -1, dtype=torch.int32, device=DEV)
+    rows_ret = torch.zeros(T * k, d, dtype=torch.bfloat16, device=DEV)
     flags = torch.zeros(N.ep_flags_bytes() // 8, dtype=torch.int64, device=DEV)
-    win = N.ep_window(1, 0, [flags.data_ptr()], [0], [recv.data_ptr()], [out.data_ptr()])
+    win = N.ep_window(1, 0, [flags.data_ptr()], [0], [recv.data_ptr()], [back.data_ptr()], [rows_ret.data_ptr()])
     i32 = dict(dtype=torch.int32, device=DEV)
     R = N.EP_MAX_REPLICAS
     table = (torch.tensor(n, **i32), torch.tensor(alive_inst, **i32), torch.tensor(inst.inst_rank, **i32),
@@ -93,8 +95,8 @@ def test_exchange_bookkeeping_matches_restatement(policy):
     for epoch in (1, 2, 3):  # the window's counter: one per ep_plan call
         N.ep_plan(win, plan["counts"], E, inst.n_inst, policy, table, cap, 10**9,
                   (part_n, part_inst, part_start, dest_off, seg_expert, seg_end))
-        N.ep_dispatch(win, x, T, k, E, plan["offsets"], plan["perm_token"], (part_n, part_inst, part_start, dest_off),
-                      table[2], cap, ret, done)
+        N.ep_dispatch(win, x, T, k, E, plan["offsets"], plan["perm_token"], plan["perm_slot"],
+                      (part_n, part_inst, part_start, dest_off), table[2], cap, ret, done)
         torch.cuda.synchronize()
         N.check_device_status(DEV)
         assert flags[3 * N.EP_MAX_RANKS].item() == epoch
@@ -114,6 +116,10 @@ def test_exchange_bookkeeping_matches_restatement(policy):
         src = x[pt[[p for p, _ in rows]].to(DEV)]
         dst = recv[torch.tensor([row for _, row in rows], device=DEV)]
         assert torch.equal(src, dst)
+        # ... and each placed row's return address (rank 0, token * k + slot) in the back map
+        ps = plan["perm_slot"].cpu()
+        bk = back.cpu()
+        assert all(bk[row].item() == pt[p].item() * k + ps[p].item() for p, row in rows)
         assert sum(1 for r, _ in dests if r < 0) == counts[5]
 
 
