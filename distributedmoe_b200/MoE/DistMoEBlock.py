@@ -693,12 +693,10 @@ class DistMoEBlock(nn.Module):
         N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, tmo, placement + (ep["seg_expert"], ep["seg_end"]))
         N.ep_dispatch(win, x, T, k, E, offsets, perm_token, perm_slot, placement, ep["inst_rank"], cap, ep["ret"],
                       ep["done"])
-        if shared:
-            # The shared expert runs here, on this stream: the routing kernels before it did not
-            # wait for its SMs, and it hides the wait for the other ranks' rows.
-            g, u, dn = self.shared_expert
-            N.grouped_gated_mlp(x, g, u, dn, [0], [T], ACTIVATIONS[self.config.activation], out,
-                                op_name="shared_expert_mlp")
+        # The shared expert starts on a side stream once the rows are sent: the routing kernels
+        # before it never wait for its SMs, and it overlaps the wait for the other ranks' rows
+        # and the routed grouped MLP's last, partly empty wave of tiles.
+        shared_done = self._launch_shared_expert(x) if shared else None
         # This GPU's expert instances, once, over every host's rows (the expert blocks' part).
         N.ep_wait(win, N.EP_FLAG_DATA, tmo, dev)
         if ep["n_local"] > 0:
@@ -710,6 +708,8 @@ class DistMoEBlock(nn.Module):
         N.ep_signal(win, N.EP_FLAG_RESULTS, dev)
         N.ep_wait(win, N.EP_FLAG_RESULTS, tmo, dev)
         if T > 0:
+            if shared_done is not None:
+                torch.cuda.current_stream(dev).wait_event(shared_done)
             N.ep_combine(win, inverse, ep["ret"], w, T, k, out, accumulate=shared)
         if self.metrics_collector is not None and not capturing:
             self.metrics_collector.end_forward_pass()
