@@ -76,6 +76,11 @@ int once_per_device(PerDeviceOnce& o, int dev, F&& init) {
 // run beside them size their grids for those SMs.
 int gemm_sm_reserve();
 
+// Router logits for few tokens on the CUDA cores (router.cu); dmoe_router_logits uses it when
+// T is small, where the tensor-core logits GEMM would run on one or two CTAs.
+bool logits_few_tokens_eligible(int T, int d, int E);
+int run_logits_few_tokens(const void* x, const void* w, int dtype, int T, int d, int E, float* out, cudaStream_t s);
+
 inline int dtype_bytes(int dt) { return dt == DMOE_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == DMOE_F32 || dt == DMOE_F16 || dt == DMOE_BF16; }
 

@@ -1329,6 +1329,7 @@ extern "C" int dmoe_router_logits(const void* x, const void* w_r, int dtype, int
   DMOE_REQUIRE(x && w_r && logits_out && dev_status, "dmoe_router_logits: null pointer");
   DMOE_REQUIRE(aligned16(x) && aligned16(w_r) && aligned16(logits_out), "dmoe_router_logits: 16-byte alignment");
   cudaStream_t s = as_stream(stream);
+  if (logits_few_tokens_eligible(T, d, E)) return run_logits_few_tokens(x, w_r, dtype, T, d, E, logits_out, s);
   if (dtype == DMOE_BF16) return run_logits<DMOE_BF16>(x, w_r, T, d, E, logits_out, dev_status, s);
   return run_logits<DMOE_F16>(x, w_r, T, d, E, logits_out, dev_status, s);
 }

@@ -484,6 +484,62 @@ __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a
   }
 }
 
+// Router logits for few tokens (decode): the tensor-core logits GEMM would give the whole
+// reduction to one or two CTAs when T is small, so here eight experts go to each CTA: their
+// weight rows land in shared memory with one bulk copy, each warp takes tokens in turn and
+// streams the token's row (L2-resident: a decode batch is small), and the 9-shuffle
+// reduce-scatter leaves lane groups holding one expert's sum each.
+constexpr int kFewTokensMax = 256;
+constexpr int kFewTokensSmemMax = 200 * 1024;
+
+template <int DT>
+__global__ void __launch_bounds__(256) logits_few_tokens_kernel(const void* x, const void* w, int T, int d, int E,
+                                                                float* out) {
+  extern __shared__ __align__(128) uint8_t s_wrows[];
+  __shared__ uint64_t bar;
+  const int e0 = blockIdx.x * 8;
+  const uint32_t bytes = (uint32_t)(8 * d * 2);
+  if (threadIdx.x == 0) {
+    bar_init(&bar, 1);
+    fence_async_shared();
+    bar_expect_tx(&bar, bytes);
+    const char* src = reinterpret_cast<const char*>(w) + (int64_t)e0 * d * 2;
+    for (uint32_t off = 0; off < bytes; off += 16384u) {  // 16 KB pieces, one completion count
+      const uint32_t n = bytes - off < 16384u ? bytes - off : 16384u;
+      bulk_load(s_wrows + off, src + off, n, &bar);
+    }
+  }
+  __syncthreads();
+  bool ok = bar_try_wait(&bar, 0);
+  if (!ok) {
+    const uint64_t w0 = global_timer_ns();
+    while (!(ok = bar_try_wait(&bar, 0)))
+      if (global_timer_ns() - w0 > kSmallWaitNs) break;
+  }
+  if (__syncthreads_or(!ok)) return;  // never wait forever for a copy from valid memory
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = d / 8;
+  for (int t = warp; t < T; t += blockDim.x >> 5) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(x) + (int64_t)t * d * 2);
+    for (int c = lane; c < nvec; c += 32) {
+      float xf[8];
+      unpack8<DT>(xr[c], xf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float wf[8];
+        unpack8<DT>(reinterpret_cast<const uint4*>(s_wrows + (int64_t)e * d * 2)[c], wf);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[e] = fmaf(xf[q], wf[q], acc[e]);
+      }
+    }
+    const float v = warp_reduce_scatter<8>(acc, lane);
+    if ((lane & 3) == 0) out[(int64_t)t * E + e0 + expert_of_lane<8>(lane)] = v;
+  }
+}
+
 template <int DT, int EP, int V>
 int launch_router_small(int grid, int threads, size_t smem, cudaStream_t s, const RouterArgs& a, int tile_t,
                         int n_tiles) {
@@ -552,7 +608,35 @@ int launch_router(dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Rout
   return DMOE_OK;
 }
 
+template <int DT>
+int launch_logits_few_tokens(const void* x, const void* w, int T, int d, int E, float* out, cudaStream_t s) {
+  static PerDeviceOnce once;
+  int dev = 0;
+  DMOE_CUDA(cudaGetDevice(&dev));
+  const int r = once_per_device(once, dev, [] {
+    DMOE_CUDA(cudaFuncSetAttribute(logits_few_tokens_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kFewTokensSmemMax));
+    return DMOE_OK;
+  });
+  if (r) return r;
+  logits_few_tokens_kernel<DT><<<E / 8, 256, (size_t)8 * d * 2, s>>>(x, w, T, d, E, out);
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}
+
 }  // namespace
+
+bool logits_few_tokens_eligible(int T, int d, int E) {
+  const char* v = getenv("DMOE_LOGITS_FEW_TOKENS");
+  if (v && v[0] == '0') return false;
+  return T <= kFewTokensMax && E % 8 == 0 && (int64_t)8 * d * 2 <= kFewTokensSmemMax;
+}
+
+int run_logits_few_tokens(const void* x, const void* w, int dtype, int T, int d, int E, float* out, cudaStream_t s) {
+  if (dtype == DMOE_BF16) return launch_logits_few_tokens<DMOE_BF16>(x, w, T, d, E, out, s);
+  return launch_logits_few_tokens<DMOE_F16>(x, w, T, d, E, out, s);
+}
+
 }  // namespace dmoe
 
 using namespace dmoe;

@@ -89,7 +89,8 @@ int dmoe_router(const void* x, const void* w_r, int x_dtype, const float* logit_
  * MoE/DistMoEBlock.py:134,556 for large expert counts, where a dot product per (token,
  * expert) on the CUDA cores is the slow part of routing; feed the result to dmoe_router as
  * logits_in.  d % 8 == 0, E % 8 == 0.  Bounded waits report through *dev_status like the
- * grouped MLP.
+ * grouped MLP.  For T <= 256 (decode) the logits are computed on the CUDA cores instead,
+ * eight experts per CTA, so that the reduction is spread over E / 8 CTAs.
  */
 int dmoe_router_logits(const void* x, const void* w_r, int dtype, int T, int d, int E, float* logits_out,
                        int32_t* dev_status, void* stream);

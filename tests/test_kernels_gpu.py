@@ -111,6 +111,29 @@ def test_router_tensor_core_logits(T, d, E):
 
 
 @gpu
+@pytest.mark.parametrize("T,d,E", [(1, 2048, 128), (64, 2048, 128), (256, 7168, 256), (100, 512, 64), (257, 2048, 128)])
+@pytest.mark.parametrize("few", ["1", "0"])
+def test_router_logits_few_tokens_and_tensor_cores(T, d, E, few, monkeypatch):
+    """Router logits for E >= 32: the CUDA-core kernel for T <= 256 (eight experts per CTA)
+    and the tensor-core GEMM (DMOE_LOGITS_FEW_TOKENS=0, or T > 256) both agree with the
+    oracle's fp32 logits within the fp32 summation bound; selection from them is bit-exact."""
+    monkeypatch.setenv("DMOE_LOGITS_FEW_TOKENS", few)
+    N = _nat()
+    g = torch.Generator().manual_seed(T + d + E + 1)
+    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    w_r = (torch.randn(E, d, generator=g) * 0.02).to(torch.bfloat16)
+    idx, w, logits = N.router(x.to(DEV), w_r.to(DEV), 8, want_logits=True, renormalize=True, w_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _status_ok()
+    ref = O.router_logits(x, w_r, fp32_logits=True)
+    mag = x.float().abs() @ w_r.float().abs().t()
+    assert bool(((logits.cpu() - ref).abs() <= 2 * d * 2.0 ** -24 * mag + 1e-6).all())
+    rw, sel = O.route(logits.cpu(), 8, torch.float32, renormalize=True)
+    assert torch.equal(idx.cpu(), sel)
+    assert torch.allclose(w.cpu(), rw, rtol=1e-6, atol=1e-7)
+
+
+@gpu
 def test_router_rejects_bad_args():
     N = _nat()
     x = torch.randn(4, 64, device=DEV)
