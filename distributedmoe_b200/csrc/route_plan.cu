@@ -137,9 +137,9 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter(const int64_t* idx,
   }
 }
 
-// Small plans (T*k <= kSingleMax, E <= kSingleMaxE) in one CTA of 1024 threads, one launch
-// instead of three: the expert of every activation is read once into shared memory (int16)
-// while the histogram builds; one block-wide scan gives counts and offsets; then rounds of
+// Small plans (T*k <= kSingleMax with E <= 64, T*k <= kSingleMax / 4 with E <= kSingleMaxE)
+// in one CTA of 1024 threads, one launch instead of three: the expert of every activation is
+// read once into shared memory (int16) while the histogram builds; one block-wide scan gives counts and offsets; then rounds of
 // 1024 consecutive activations (in the slot-major order f = s*T + t) are ranked stably:
 // within a warp by __match_any_sync, across the round's warps by a per-expert scan of the
 // per-warp counts, and across rounds by a running position per expert.  The order is the
@@ -153,8 +153,9 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
                 int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse, void* perm_weight) {
   extern __shared__ __align__(16) int32_t sm[];
   int32_t* s_run = sm;                          // [E] running position of each expert
-  int32_t* s_wc = sm + kSingleMaxE;             // [32][E] per-warp counts, then their prefixes
-  int16_t* s_e = reinterpret_cast<int16_t*>(s_wc + 32 * E);  // [n] expert of each activation (-1: none)
+  const int ws = E + 1;                         // row stride of s_wc: a column walk hits 32 banks
+  int32_t* s_wc = sm + kSingleMaxE;             // [32][E + 1] per-warp counts, then their prefixes
+  int16_t* s_e = reinterpret_cast<int16_t*>(s_wc + 32 * ws);  // [n] expert of each activation (-1: none)
   __shared__ int32_t s_warp[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = T * k;
@@ -212,17 +213,17 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
   }
   // 3. stable ranks, one round of 1024 consecutive activations at a time
   for (int r0 = 0; r0 < n; r0 += kSingleThreads) {
-    for (int i = tid; i < 32 * E; i += kSingleThreads) s_wc[i] = 0;
+    for (int i = tid; i < 32 * ws; i += kSingleThreads) s_wc[i] = 0;
     __syncthreads();
     const int f = r0 + tid;
     const int e = f < n ? (int)s_e[f] : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
-    if (e >= 0 && lane == __ffs(peers) - 1) s_wc[warp * E + e] = __popc(peers);
+    if (e >= 0 && lane == __ffs(peers) - 1) s_wc[warp * ws + e] = __popc(peers);
     __syncthreads();
     // per expert: exclusive scan of the 32 warps' counts, offset by the running position
     for (int ee = warp; ee < E; ee += 32) {
-      const int32_t wc = s_wc[lane * E + ee];
+      const int32_t wc = s_wc[lane * ws + ee];
       int32_t in = wc;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
         if (lane >= o) in += u;
       }
       const int32_t run = s_run[ee];
-      s_wc[lane * E + ee] = run + in - wc;
+      s_wc[lane * ws + ee] = run + in - wc;
       __syncwarp();
       if (lane == 31) s_run[ee] = run + in;
     }
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
     if (f < n) {
       const int s = f / T, t = f - (f / T) * T;
       if (e >= 0) {
-        const int pos = s_wc[warp * E + e] + rank_in_warp;
+        const int pos = s_wc[warp * ws + e] + rank_in_warp;
         perm_token[pos] = t;
         if (perm_slot) perm_slot[pos] = s;
         if (inverse) inverse[(int64_t)t * k + s] = pos;
@@ -252,13 +253,18 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
 }
 
 size_t plan_single_smem(int T, int k, int E) {
-  return (size_t)(kSingleMaxE + 32 * E) * sizeof(int32_t) + (((size_t)T * k * sizeof(int16_t) + 15) & ~size_t(15));
+  return (size_t)(kSingleMaxE + 32 * (E + 1)) * sizeof(int32_t) +
+         (((size_t)T * k * sizeof(int16_t) + 15) & ~size_t(15));
 }
 
 bool plan_single_eligible(int T, int k, int E) {
   const char* v = getenv("DMOE_PLAN_SINGLE");
   if (v && v[0] == '0') return false;
-  return (int64_t)T * k <= kSingleMax && E <= kSingleMaxE;
+  // One CTA ranks 1024 activations per round and scans E experts per round: many experts
+  // and many rounds (DeepSeek's 256 experts at 32768 activations) cost more than the three
+  // grid-wide launches of the multi-CTA path.
+  const int64_t n = (int64_t)T * k;
+  return E <= kSingleMaxE && n <= (E <= 64 ? kSingleMax : kSingleMax / 4);
 }
 
 // Scratch of dmoe_route_plan_noalloc: the per-chunk histogram matrix lives in this

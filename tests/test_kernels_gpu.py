@@ -147,8 +147,9 @@ def test_router_rejects_bad_args():
                                    (4096, 8, 256), (16384, 2, 8), (3000, 8, 1024), (100, 1, 4), (16, 8, 128)])
 @pytest.mark.parametrize("single", ["1", "0"])
 def test_route_plan_bit_exact(T, k, E, single, monkeypatch):
-    """Both plan paths (one CTA for up to 32768 activations and E <= 256, three launches
-    otherwise; DMOE_PLAN_SINGLE=0 forces the latter) give the oracle's plan bit for bit."""
+    """Both plan paths (one CTA for up to 32768 activations with E <= 64 and 8192 with
+    E <= 256, three launches otherwise; DMOE_PLAN_SINGLE=0 forces the latter) give the
+    oracle's plan bit for bit."""
     monkeypatch.setenv("DMOE_PLAN_SINGLE", single)
     N = _nat()
     g = torch.Generator().manual_seed(T + 31 * k + E)
