@@ -384,7 +384,8 @@ class Layer:
     (LocalCluster on one GPU, ShardedCluster over ranks) and this rank's input tokens."""
 
     def __init__(self, w: Workload, dev: torch.device, world: int = 1, rank: int = 0, parallel: str = "single",
-                 data_plane: str = "direct", x_seed_offset: int = 0, cuda_graphs: bool = False):
+                 data_plane: str = "direct", x_seed_offset: int = 0, cuda_graphs: bool = False,
+                 expert_precision: str = "model"):
         from distributedmoe_b200.MoE.local_cluster import LocalCluster
         from distributedmoe_b200.MoE.sharded_cluster import ShardedCluster
         from distributedmoe_b200.TensorTransferEngine import TensorTransferEngineBackend as B
@@ -414,6 +415,7 @@ class Layer:
             self.stack = expert_weights(w, mine, dev)
             if data_plane == "direct":
                 opts["cuda_graphs"] = cuda_graphs
+                opts["expert_precision"] = expert_precision
             self.cluster = ShardedCluster(w.E, w.k, D, torch.bfloat16, dev, self.stack, backend=backend,
                                           max_tokens=self.T, blocks=blocks, **opts,
                                           **({} if data_plane == "direct" else dict(zip(
@@ -430,6 +432,7 @@ class Layer:
             io_size, io_buffers = w.io(1, "single")
             if data_plane == "direct":
                 opts["cuda_graphs"] = cuda_graphs
+                opts["expert_precision"] = expert_precision
             self.cluster = LocalCluster(w.E, blocks, w.k, D, torch.bfloat16, dev, [dev] * len(blocks),
                                         stacked=stacks, io_buffer_size=io_size, number_of_io_buffers=io_buffers,
                                         backend=backend, max_tokens=self.T, **opts)
@@ -534,7 +537,11 @@ def run_ours(args, dist, rank, world, local_rank):
         raise SystemExit(f"--parallel experts needs a GPU count that divides {w.E}")
     graphs = args.cuda_graphs == "on" or (args.cuda_graphs == "auto" and w.name.endswith("decode-moe-layer"))
     graphs = graphs and args.data_plane == "direct"
-    layer = Layer(w, dev, world, rank, parallel, args.data_plane, cuda_graphs=graphs)
+    fp8 = args.expert_precision == "fp8"
+    if fp8 and args.data_plane != "direct":
+        raise SystemExit("--expert-precision fp8 runs on the direct data plane")
+    layer = Layer(w, dev, world, rank, parallel, args.data_plane, cuda_graphs=graphs,
+                  expert_precision="fp8" if fp8 else "model")
     moe, x, T, D = layer.moe, layer.x, layer.T, w.d
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(T, D, dtype=torch.bfloat16).pin_memory()
@@ -646,7 +653,9 @@ def run_ours(args, dist, rank, world, local_rank):
         n_act = T * w.k
         movers = {
             "router": (T * D * 2 + w.E * D * 2 + n_act * 12, "x read + router weights + indices/weights out"),
-            "ep_dispatch": (2 * n_act * D * 2 + n_act * 8, "routed rows read + written, indices"),
+            "ep_dispatch": (2 * n_act * ((D + 16) if fp8 else D * 2) + n_act * 8,
+                            "routed rows read + written, indices" + (" (8-bit records, d + 16 bytes)" if fp8 else "")),
+            "quantize_rows_e4m3": (T * D * 2 + T * (D + 16), "tokens read (bf16), records written"),
             "ep_combine": (n_act * D * 2 + T * D * 2 + n_act * 12, "routed rows read, tokens written, indices"),
             "permute_rows": (None, "task-plane gathers"),
             "combine": (n_act * D * 2 + T * D * 2 + n_act * 8, "permuted rows read, tokens written"),
@@ -661,6 +670,9 @@ def run_ours(args, dist, rank, world, local_rank):
             hbm_ops[name] = {"us_per_launch": st["ms_per_launch"] * 1e3, "bytes_per_launch": per, "bytes": what,
                              "gbs": gbs, "frac": gbs / hbm}
         roof["hbm"] = {"peak_gbs": hbm, "peak_kind": f"{src} copy", "ops": hbm_ops}
+        if fp8:
+            roof["note"] = ("gate/up GEMM on e4m3 tensor cores (nominally twice the bf16 rate), down GEMM bf16; "
+                            "the peak is the measured bf16 one")
     op_us = {name: _op_stats(krecs, name, steps)["ms_per_launch"] * 1e3 for name in krecs if krecs[name]}
     cpu_tok_s, cores, sample = None, None, None
     if not args.no_cpu:
@@ -671,8 +683,9 @@ def run_ours(args, dist, rank, world, local_rank):
         "metric": METRIC, "value": total_tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong" if (w.strong and parallel == "experts") else "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": dict(w.config(world, parallel, args.data_plane), cuda_graphs=graphs), "impl": "ours",
+        "vs_baseline": None, "dtype": "e4m3 gate/up, bf16 down and combine" if fp8 else "bf16", "data": "synthetic",
+        "config": dict(w.config(world, parallel, args.data_plane), cuda_graphs=graphs,
+                       **({"expert_precision": "fp8"} if fp8 else {})), "impl": "ours",
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": total_tokens * D * 2, "d2h_bytes_per_step": total_tokens * D * 2,
                 "copies": "pinned host in/out every step; H2D of step i+1 and D2H of step i-1 on two copy "
@@ -706,18 +719,30 @@ def run_gemm_only(args):
     wd = _randn_bf16((Eg, D, w.I), w.w_std, gen, dev)
     Y = torch.empty(rows, D, dtype=torch.bfloat16, device=dev)
     ends = [rows * (e + 1) // Eg for e in range(Eg)]
+    fp8 = args.expert_precision == "fp8"
+    if fp8:  # operands quantised once, outside the timed region: the GEMM pair alone is timed
+        xq, xs = N.quantize_rows_e4m3(X)
+        ex = N.Fp8Experts(wg, wu, wd)
+
+    def launch():
+        if fp8:
+            N.grouped_gated_mlp_fp8(xq, xs, ex, list(range(Eg)), ends, N.ACT_SILU, Y)
+        else:
+            N.grouped_gated_mlp(X, wg, wu, wd, list(range(Eg)), ends, N.ACT_SILU, Y)
+
     for _ in range(args.warmup):
-        N.grouped_gated_mlp(X, wg, wu, wd, list(range(Eg)), ends, N.ACT_SILU, Y)
+        launch()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        N.grouped_gated_mlp(X, wg, wu, wd, list(range(Eg)), ends, N.ACT_SILU, Y)
+        launch()
     b.record()
     torch.cuda.synchronize()
     N.check_device_status(dev)
     ms = a.elapsed_time(b) / args.steps
     print(json.dumps({"mode": "gemm", "workload": w.name, "rows": rows, "experts": Eg, "ms_per_launch_pair": ms,
+                      "precision": "e4m3 gate/up, bf16 down" if fp8 else "bf16",
                       "tflops": 6.0 * rows * D * w.I / (ms * 1e-3) / 1e12}), flush=True)
 
 
@@ -806,6 +831,9 @@ def main():
     ap.add_argument("--mode", default="layer", choices=["layer", "gemm", "movers"],
                     help="gemm: time only the grouped expert MLP; movers: only the router, plan, gather and "
                          "combine (for kernel profiling)")
+    ap.add_argument("--expert-precision", default="bf16", choices=["bf16", "fp8"],
+                    help="fp8: routed experts on 8-bit records and e4m3 gate/up GEMMs (not the headline "
+                         "precision: the headline line is bf16)")
     ap.add_argument("--gemm-rows", type=int, default=4096)
     ap.add_argument("--gemm-experts", type=int, default=2)
     args = ap.parse_args()

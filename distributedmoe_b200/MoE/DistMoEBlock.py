@@ -554,7 +554,8 @@ class DistMoEBlock(nn.Module):
     # ------------------------------------------------------------------ device-driven data plane
     def setup_direct_plane(self, world: int, rank: int, block_ranks: List[int], local_stack, capacity: int,
                            exchange: Callable[[bytes], List[bytes]], max_tokens: int,
-                           wait_timeout_ms: Optional[int] = None, cuda_graphs: bool = False) -> None:
+                           wait_timeout_ms: Optional[int] = None, cuda_graphs: bool = False,
+                           expert_precision: str = "model") -> None:
         """Switch forward() to the device-driven exchange (``NVLinkDirect`` backend only).
 
         world, rank: this host's group (one rank per GPU, every rank calls forward once per
@@ -565,7 +566,13 @@ class DistMoEBlock(nn.Module):
         rank's window descriptor in rank order; max_tokens: tokens per forward of this host.
         cuda_graphs: capture the forward once per token count (after one eager forward of
         that count) and replay it; the input is copied into a static buffer and the result
-        copied out, so callers see ordinary tensors."""
+        copied out, so callers see ordinary tensors.  expert_precision: "model" (the layer's
+        dtype) or "fp8": the routed experts' gate/up weights are quantised once to e4m3 with
+        one scale per output channel, each token row is quantised to e4m3 with one scale
+        before the gather (8-bit records cross NVLink: about half the bytes), the gate/up
+        GEMM runs on 8-bit tensor cores and the down projection in bf16 (bf16 layers only;
+        the reference's benchmark offers "fp8" as a whole-layer 8-bit cast,
+        src/python/MoE/benchmarks/bench.py:184-185)."""
         tte = self.tensor_transfer_engine
         if not getattr(tte, "direct", False):
             raise RuntimeError("the device-driven data plane needs the NVLinkDirect backend")
@@ -579,9 +586,15 @@ class DistMoEBlock(nn.Module):
                              f"[{n_local}, I, {d}] and down [{n_local}, {d}, I]")
         if self.dtype not in (torch.bfloat16, torch.float16):
             raise NotImplementedError("the device-driven data plane computes in bf16 or fp16")
+        if expert_precision not in ("model", "fp8"):
+            raise ValueError(f"expert_precision {expert_precision!r}: 'model' or 'fp8'")
+        fp8 = expert_precision == "fp8"
+        if fp8 and (self.dtype != torch.bfloat16 or d % 16):
+            raise ValueError("8-bit experts need a bf16 layer and hidden % 16 == 0")
         dev = self.device
         with torch.cuda.device(dev):
-            tte.open_window(capacity, max(max_tokens * k, 1), d, self.dtype, inst.n_inst, dev)
+            tte.open_window(capacity, max(max_tokens * k, 1), d, self.dtype, inst.n_inst, dev,
+                            record_bytes=N.fp8_record_bytes(d) if fp8 else None)
             descs = exchange(tte.window_descriptor())
             win = tte.attach_windows(descs, rank)
             i32 = dict(dtype=torch.int32, device=dev)
@@ -591,6 +604,9 @@ class DistMoEBlock(nn.Module):
             self._ep = {
                 "world": world, "rank": rank, "inst": inst, "win": win, "cap": capacity, "policy": policy,
                 "n_local": n_local, "stack": (g, u, dn), "max_tokens": max_tokens,
+                "fp8": N.Fp8Experts(g, u, dn) if fp8 and n_local > 0 else None, "is_fp8": fp8,
+                "records": torch.empty(max(max_tokens, 1), N.fp8_record_bytes(d), dtype=torch.uint8, device=dev)
+                if fp8 else None,
                 "timeout_ns": int(timeout_ms) * 1_000_000,
                 "inst_rank": torch.tensor(inst.inst_rank, **i32),
                 "inst_slot": torch.tensor(inst.inst_slot, **i32),
@@ -691,8 +707,10 @@ class DistMoEBlock(nn.Module):
             counts = offsets = perm_token = perm_slot = inverse = w = None
         inst = ep["inst"]
         N.ep_plan(win, counts, E, inst.n_inst, ep["policy"], table, cap, tmo, placement + (ep["seg_expert"], ep["seg_end"]))
-        N.ep_dispatch(win, x, T, k, E, offsets, perm_token, perm_slot, placement, ep["inst_rank"], cap, ep["ret"],
-                      ep["done"])
+        # 8-bit experts: each token row leaves as one record (e4m3 codes + its scale).
+        rows_out = N.quantize_records(x, ep["records"][:T]) if ep["is_fp8"] else x
+        N.ep_dispatch(win, rows_out, T, k, E, offsets, perm_token, perm_slot, placement, ep["inst_rank"], cap,
+                      ep["ret"], ep["done"])
         # The shared expert starts on a side stream once the rows are sent: the routing kernels
         # before it never wait for its SMs, and it overlaps the wait for the other ranks' rows
         # and the routed grouped MLP's last, partly empty wave of tiles.
@@ -703,8 +721,12 @@ class DistMoEBlock(nn.Module):
             # The down-projection stores every row straight into its host's return rows.
             g, u, dn = ep["stack"]
             rows = T * k if ep["world"] == 1 else None
-            N.ep_expert_mlp(win, g, u, dn, ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]], cap,
-                            ACTIVATIONS[self.config.activation], self._direct_tile_policy(T), work_rows=rows)
+            segs = (ep["seg_expert"][:ep["n_local"]], ep["seg_end"][:ep["n_local"]])
+            act = ACTIVATIONS[self.config.activation]
+            if ep["fp8"] is not None:
+                N.ep_expert_mlp_fp8(win, ep["fp8"], *segs, cap, act, self._direct_tile_policy(T), work_rows=rows)
+            else:
+                N.ep_expert_mlp(win, g, u, dn, *segs, cap, act, self._direct_tile_policy(T), work_rows=rows)
         N.ep_signal(win, N.EP_FLAG_RESULTS, dev)
         N.ep_wait(win, N.EP_FLAG_RESULTS, tmo, dev)
         if T > 0:

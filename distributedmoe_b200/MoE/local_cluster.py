@@ -46,12 +46,14 @@ class LocalCluster:
                  expert_layers: Optional[List[list]] = None, stacked: Optional[list] = None,
                  io_buffer_size: int = 8192, number_of_io_buffers: int = 4, forward_timeout: int = 60000,
                  p2p_timeout_ms: int = 3000, backend: TensorTransferEngineBackend = TensorTransferEngineBackend.NVLinkIPC,
-                 max_tokens: Optional[int] = None, cuda_graphs: bool = False, **options):
+                 max_tokens: Optional[int] = None, cuda_graphs: bool = False, expert_precision: str = "model",
+                 **options):
         """backend NVLinkDirect runs forward() as the device-driven exchange with world 1: every
         block must sit on the host's GPU; the blocks' stacks are concatenated (block order)
         into the one weight stack the grouped MLP reads; max_tokens (default io_buffer_size *
         number_of_io_buffers // top_k) sizes the receive window; cuda_graphs replays each
-        token count's forward from a captured CUDA graph."""
+        token count's forward from a captured CUDA graph; expert_precision "fp8" runs the
+        routed experts on 8-bit records (DistMoEBlock.setup_direct_plane)."""
         nb = len(expert_blocks)
         ports = free_ports(1 + 5 * nb)
         host_port, rest = ports[0], ports[1:]
@@ -110,7 +112,7 @@ class LocalCluster:
                                                         for i in range(3))
                 mt = max_tokens if max_tokens is not None else max(1, io_buffer_size * number_of_io_buffers // top_k)
                 self.moe.setup_direct_plane(1, 0, [0] * nb, local, mt * top_k, lambda mine: [mine], mt,
-                                            cuda_graphs=cuda_graphs)
+                                            cuda_graphs=cuda_graphs, expert_precision=expert_precision)
 
     def __enter__(self) -> DistMoEBlock:
         return self.moe

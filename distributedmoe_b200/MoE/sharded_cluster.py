@@ -103,13 +103,15 @@ class ShardedCluster:
                  gemm_sm_reserve: Optional[int] = None,
                  backend: TensorTransferEngineBackend = TensorTransferEngineBackend.NVLinkDirect,
                  max_tokens: int = 8192, blocks: Optional[List[List[int]]] = None, cuda_graphs: bool = False,
-                 **options):
+                 expert_precision: str = "model", **options):
         """stacked: this rank's weight stack for the experts of its block, in block order.
         blocks[g]: the experts of rank g's block (default: the contiguous E/G of rank g); an
         expert listed by two ranks is replicated.  max_tokens: tokens per forward of one host
         (sizes the NVLinkDirect receive windows: G * max_tokens * top_k rows per GPU).
         cuda_graphs: replay each token count's forward from a captured CUDA graph (every rank
-        captures at the same step; capturing runs no kernel, so the ranks stay in step)."""
+        captures at the same step; capturing runs no kernel, so the ranks stay in step).
+        expert_precision: "fp8" sends 8-bit records and runs the gate/up GEMM on e4m3 tensor
+        cores (DistMoEBlock.setup_direct_plane)."""
         direct = backend == TensorTransferEngineBackend.NVLinkDirect
         if direct:
             # The task buffers only serve the metadata hand-shake: keep them small.
@@ -192,7 +194,7 @@ class ShardedCluster:
             if direct:
                 self.moe.setup_direct_plane(G, r, list(range(G)), stacked, G * max_tokens * top_k,
                                             lambda mine: gather_window_descriptors(mine, group), max_tokens,
-                                            cuda_graphs=cuda_graphs)
+                                            cuda_graphs=cuda_graphs, expert_precision=expert_precision)
         self.direct = direct
         self.device = device
         dist.barrier(group=group)  # every host and block of every rank is up before the first forward

@@ -6,7 +6,8 @@ events) stays available.  On top, each engine owns one window in its GPU's memor
 
 * ``recv``   [capacity, d]  the rows every host dispatches to this GPU's expert instances
              (the input buffer of the GPU's expert blocks, written by the senders' gather
-             kernel through peer pointers);
+             kernel through peer pointers); with 8-bit experts, uint8 records of d e4m3
+             codes and the row's fp32 scale (d + 16 bytes);
 * ``back``   [capacity] int32  each receive row's return address (host rank, token * k +
              slot), written by the senders' gather beside the row;
 * ``rows``   [max_tokens * k, d]  this host's expert outputs in (token, slot) order, written
@@ -51,16 +52,20 @@ class NVLinkDirectTensorTransferEngine(NVLinkTensorTransferEngine):
         self.window: Optional[N.EpWindow] = None
 
     def open_window(self, capacity: int, return_rows: int, hidden: int, dtype: torch.dtype, n_inst: int,
-                    device: torch.device) -> None:
+                    device: torch.device, record_bytes: Optional[int] = None) -> None:
         """Allocate and register this GPU's window (flags and counts zeroed).  capacity:
-        receive rows; return_rows: this host's max_tokens * top_k."""
+        receive rows; return_rows: this host's max_tokens * top_k; record_bytes: bytes of one
+        receive row when it is not `hidden` elements of `dtype` (8-bit records)."""
         if self.recv is not None:
             raise RuntimeError("the window is already open")
         if capacity < 1 or return_rows < 1:
             raise ValueError("the window needs at least one receive row and one return row")
         device = torch.device(device)
         with torch.cuda.device(device):
-            self.recv = torch.empty(capacity, hidden, dtype=dtype, device=device)
+            if record_bytes is None:
+                self.recv = torch.empty(capacity, hidden, dtype=dtype, device=device)
+            else:
+                self.recv = torch.empty(capacity, record_bytes, dtype=torch.uint8, device=device)
             self.back = torch.full((capacity,), -1, dtype=torch.int32, device=device)
             self.rows = torch.empty(return_rows, hidden, dtype=dtype, device=device)
             self.flags = torch.zeros(N.ep_flags_bytes() // 8, dtype=torch.int64, device=device)

@@ -18,7 +18,7 @@ import torch
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("DMOE_LIB", os.path.join(_PKG, "libdmoe_b200.so"))
 
-F32, F16, BF16 = 0, 1, 2
+F32, F16, BF16, E4M3 = 0, 1, 2, 3
 TILES_AUTO, TILES_PAIR, TILES_SINGLE, TILES_PAIR_SPLIT = 0, 1, 2, 3
 ACT_RELU, ACT_SILU = 0, 1
 ROUTER_SOFTMAX, ROUTER_SIGMOID_GROUP = 0, 1
@@ -77,6 +77,11 @@ SIGNATURES = {
                                                  ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  ctypes.c_int, _vp, _vp, _sz, _vp, ctypes.c_int, _vp]),
     "dmoe_grouped_mlp_set_sm_reserve": (ctypes.c_int, [ctypes.c_int]),
+    "dmoe_quantize_rows_e4m3": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int, _vp, ctypes.c_int64,
+                                               _vp, ctypes.c_int64, _vp]),
+    "dmoe_grouped_gated_mlp_fp8": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_int, _vp, _vp, _sz, _vp, ctypes.c_int, _vp]),
     "dmoe_router_logits": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
                                           _vp]),
     "dmoe_grouped_gated_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -100,6 +105,9 @@ SIGNATURES = {
     "dmoe_ep_expert_mlp": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           _vp, _vp, ctypes.c_int, _i64, ctypes.c_int, _vp, _sz, _vp, ctypes.c_int,
                                           _vp]),
+    "dmoe_ep_expert_mlp_fp8": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              _vp, _vp, ctypes.c_int, _i64, ctypes.c_int, _vp, _sz, _vp, ctypes.c_int,
+                                              _vp]),
     "dmoe_ep_wait": (ctypes.c_int, [_vp, ctypes.c_int, _u64, _vp, _vp]),
     "dmoe_ep_signal": (ctypes.c_int, [_vp, ctypes.c_int, _vp]),
     "dmoe_ep_combine": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -462,6 +470,109 @@ def grouped_gated_mlp_ptrs(x_ptr: int, y_ptr: int, m_rows: int, w_gate: torch.Te
     tm.done()
 
 
+def quantize_rows_e4m3(x: torch.Tensor, q: Optional[torch.Tensor] = None,
+                       scale: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Row-wise e4m3 quantisation of x [..., cols]: returns q (float8_e4m3fn, x's shape) and
+    scale (fp32, one per row), x ~= q * scale[row]."""
+    dev = _require_cuda(x)
+    if not x.is_contiguous():
+        raise DMoEError("x must be contiguous")
+    cols = x.shape[-1]
+    rows = x.numel() // cols if cols else 0
+    if q is None:
+        q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    if scale is None:
+        scale = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    if q.dtype != torch.float8_e4m3fn or q.shape != x.shape or scale.numel() != rows or scale.dtype != torch.float32:
+        raise DMoEError("q must be float8_e4m3fn of x's shape and scale fp32 with one value per row")
+    tm = _Timed("quantize_rows_e4m3", _stream(dev), dev)
+    rc = lib().dmoe_quantize_rows_e4m3(x.data_ptr(), dtype_code(x.dtype), rows, cols, q.data_ptr(), cols,
+                                       scale.data_ptr(), 1, _stream(dev))
+    _check(rc, "dmoe_quantize_rows_e4m3")
+    tm.done()
+    return q, scale
+
+
+def fp8_record_bytes(d: int) -> int:
+    """Bytes of one 8-bit receive record: d e4m3 codes, the row's fp32 scale, padding to 16."""
+    return d + 16
+
+
+def quantize_records(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x [T, d] -> uint8 records [T, d + 16]: row t's e4m3 codes, then its fp32 scale."""
+    dev = _require_cuda(x)
+    T, d = x.shape
+    if d % 16:
+        raise DMoEError(f"8-bit records need d % 16 == 0 (d={d})")
+    if out is None:
+        out = torch.empty(T, d + 16, dtype=torch.uint8, device=x.device)
+    if out.dtype != torch.uint8 or out.shape[0] < T or out.shape[1] != d + 16 or not out.is_contiguous():
+        raise DMoEError("records must be a contiguous uint8 [T, d + 16] tensor")
+    if T == 0:
+        return out
+    tm = _Timed("quantize_rows_e4m3", _stream(dev), dev)
+    rc = lib().dmoe_quantize_rows_e4m3(x.data_ptr(), dtype_code(x.dtype), T, d, out.data_ptr(), d + 16,
+                                       out.data_ptr() + d, (d + 16) // 4, _stream(dev))
+    _check(rc, "dmoe_quantize_rows_e4m3")
+    tm.done()
+    return out
+
+
+class Fp8Experts:
+    """An expert stack with e4m3 gate/up weights (one fp32 scale per output channel) and a
+    bf16 down projection, quantised once from 16-bit stacks."""
+
+    def __init__(self, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor) -> None:
+        E, I, d = w_gate.shape
+        if d % 16:
+            raise DMoEError(f"8-bit experts need d % 16 == 0 (d={d})")
+        if w_up.shape != (E, I, d) or w_down.shape != (E, d, I):
+            raise DMoEError("expert stacks must be gate/up [E, I, d] and down [E, d, I]")
+        self.wg_q, self.wg_scale = quantize_rows_e4m3(w_gate.contiguous())
+        self.wu_q, self.wu_scale = quantize_rows_e4m3(w_up.contiguous())
+        self.w_down = w_down.to(torch.bfloat16).contiguous()
+
+    @property
+    def shape(self):
+        return self.wg_q.shape
+
+
+def grouped_gated_mlp_fp8(Xq: torch.Tensor, x_scale: torch.Tensor, experts: Fp8Experts, seg_expert, seg_end,
+                          act: int, Y: torch.Tensor, m_rows: Optional[int] = None,
+                          tile_policy: int = TILES_AUTO) -> None:
+    """Grouped expert MLP with an e4m3 gate/up GEMM (row and column scales applied in the
+    activation epilogue) and a bf16 down GEMM.  Xq [rows, d] e4m3 with x_scale [rows];
+    Y [rows, d] bf16.  seg_expert/seg_end as :func:`grouped_gated_mlp`."""
+    dev = _require_cuda(Xq, x_scale, experts.wg_q, experts.w_down, Y)
+    E, I, d = experts.wg_q.shape
+    if Xq.dtype != torch.float8_e4m3fn or x_scale.dtype != torch.float32:
+        raise DMoEError("Xq must be float8_e4m3fn with fp32 row scales")
+    if Y.dtype != torch.bfloat16:
+        raise DMoEError("Y must be bf16")
+    if Xq.shape[1] != d or Y.shape[1] != d:
+        raise DMoEError("Xq and Y must be [rows, d]")
+    m = Xq.shape[0] if m_rows is None else m_rows
+    if m > Xq.shape[0] or m > Y.shape[0] or m > x_scale.numel():
+        raise DMoEError("m_rows exceeds the rows of Xq, x_scale or Y")
+    ws = scratch.get(dev, "mlp", lib().dmoe_grouped_mlp_workspace_size(m, I, BF16))
+    if isinstance(seg_expert, torch.Tensor):
+        n_seg = seg_expert.numel()
+        se, sn, on_dev, keep = seg_expert.data_ptr(), seg_end.data_ptr(), 1, None
+    else:
+        n_seg = len(seg_expert)
+        a1, a2 = _i32_array(seg_expert), _i32_array(seg_end)
+        se, sn, on_dev, keep = ctypes.addressof(a1), ctypes.addressof(a2), 0, (a1, a2)
+    tm = _Timed("grouped_gated_mlp_fp8", _stream(dev), dev)
+    rc = lib().dmoe_grouped_gated_mlp_fp8(Xq.data_ptr(), x_scale.data_ptr(), experts.wg_q.data_ptr(),
+                                          experts.wg_scale.data_ptr(), experts.wu_q.data_ptr(),
+                                          experts.wu_scale.data_ptr(), experts.w_down.data_ptr(), E, d, I, se, sn,
+                                          n_seg, on_dev, m, act, Y.data_ptr(), ws.data_ptr(), ws.numel(),
+                                          scratch.status(dev).data_ptr(), int(tile_policy), _stream(dev))
+    del keep
+    _check(rc, "dmoe_grouped_gated_mlp_fp8")
+    tm.done()
+
+
 def set_gemm_sm_reserve(sms: int) -> None:
     """SMs that later grouped-MLP launches of this process leave free for other streams."""
     _check(lib().dmoe_grouped_mlp_set_sm_reserve(int(sms)), "dmoe_grouped_mlp_set_sm_reserve")
@@ -640,6 +751,23 @@ def ep_expert_mlp(win: EpWindow, w_gate: torch.Tensor, w_up: torch.Tensor, w_dow
                                   ws.data_ptr(), ws.numel(), scratch.status(dev).data_ptr(), int(tile_policy),
                                   _stream(dev))
     _check(rc, "dmoe_ep_expert_mlp")
+    tm.done()
+
+
+def ep_expert_mlp_fp8(win: EpWindow, experts: Fp8Experts, seg_expert: torch.Tensor, seg_end: torch.Tensor,
+                      cap: int, act: int, tile_policy: int = TILES_AUTO, work_rows: Optional[float] = None) -> None:
+    """:func:`ep_expert_mlp` for 8-bit receive records (d e4m3 codes + the row's fp32 scale,
+    d + 16 bytes) and e4m3 gate/up stacks; the return rows are bf16."""
+    dev = _require_cuda(experts.w_down, seg_expert, seg_end)
+    E, I, d = experts.wg_q.shape
+    ws = scratch.get(dev, "mlp", lib().dmoe_grouped_mlp_workspace_size(cap, I, BF16))
+    tm = _Timed("grouped_gated_mlp", _stream(dev), dev, None if work_rows is None else 6.0 * work_rows * d * I)
+    rc = lib().dmoe_ep_expert_mlp_fp8(ctypes.byref(win), experts.wg_q.data_ptr(), experts.wg_scale.data_ptr(),
+                                      experts.wu_q.data_ptr(), experts.wu_scale.data_ptr(), experts.w_down.data_ptr(),
+                                      E, d, I, seg_expert.data_ptr(), seg_end.data_ptr(), seg_expert.numel(), int(cap),
+                                      int(act), ws.data_ptr(), ws.numel(), scratch.status(dev).data_ptr(),
+                                      int(tile_policy), _stream(dev))
+    _check(rc, "dmoe_ep_expert_mlp_fp8")
     tm.done()
 
 

@@ -32,6 +32,21 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;    // one 128-byte swizzle atom of 16-bit elements
+
+// Elements in one 128-byte swizzle row: 64 of a 16-bit type, 128 of e4m3.  Shared-memory
+// tiles, barriers and MMA counts are byte-based and the same for both; only the K extent of
+// a box and the MMA kind change (one kind::f16 MMA takes K=16, one kind::f8f6f4 MMA K=32:
+// 32 bytes of a row either way).
+template <int DT>
+__host__ __device__ constexpr int row_elems() {
+  return DT == DMOE_E4M3 ? 128 : 64;
+}
+
+// Type a GEMM on DT operands stores: e4m3 products are stored as bf16.
+template <int DT>
+__host__ __device__ constexpr int out_dtype() {
+  return DT == DMOE_E4M3 ? DMOE_BF16 : DT;
+}
 constexpr int BN = 256;   // MMA N
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
@@ -78,6 +93,13 @@ struct GemmArgs {
   int scatter;
   const int32_t* scatter_map;
   char* scatter_base[DMOE_EP_MAX_RANKS];
+  // e4m3 gated GEMM only: the fp32 scale of each A row (a_scale_ld floats apart) and of each
+  // B row of the gate / up stacks ([E_stack][n_out]); the epilogue multiplies every
+  // accumulator by its row's and its column's scale.
+  const float* a_scale;
+  int a_scale_ld;
+  const float* b0_scale;
+  const float* b1_scale;
 };
 
 // Destination of output row `row` of a plain GEMM (nullptr: not stored).
@@ -192,14 +214,24 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+template <int DT>
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (DT == DMOE_E4M3) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -244,7 +276,8 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor, kind::f16: D fp32, A/B f16 or bf16, both K-major, M=128, N=256.
+// Instruction descriptor: D fp32 (bit 4), A and B formats at bits 7 and 10 (kind::f16: f16 0,
+// bf16 1; kind::f8f6f4: e4m3 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24; M=128, N=256.
 template <int DT>
 __host__ __device__ constexpr uint32_t make_idesc() {
   return (1u << 4) | ((DT == DMOE_BF16 ? 1u : 0u) << 7) | ((DT == DMOE_BF16 ? 1u : 0u) << 10) |
@@ -395,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int total_m = s_tile[n_seg];
   const int total = total_m * args.n_tiles_n;
-  const int nk = (args.K + BK - 1) / BK;
+  constexpr int RE = row_elems<DT>();
+  const int nk = (args.K + RE - 1) / RE;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -415,21 +449,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(sa, &tm_a, &full[stage], kb * BK, ti.row0);
+          tma_load_2d(sa, &tm_a, &full[stage], kb * RE, ti.row0);
           if constexpr (GATED) {
-            tma_load_3d(sb, &tm_b0, &full[stage], kb * BK, ti.nt * (BN / 2), ti.expert);
-            tma_load_3d(sb + B_BYTES / 2, &tm_b1, &full[stage], kb * BK, ti.nt * (BN / 2), ti.expert);
+            tma_load_3d(sb, &tm_b0, &full[stage], kb * RE, ti.nt * (BN / 2), ti.expert);
+            tma_load_3d(sb + B_BYTES / 2, &tm_b1, &full[stage], kb * RE, ti.nt * (BN / 2), ti.expert);
           } else {
-            tma_load_3d(sb, &tm_b0, &full[stage], kb * BK, ti.nt * BN, ti.expert);
+            tma_load_3d(sb, &tm_b0, &full[stage], kb * RE, ti.nt * BN, ti.expert);
           }
           const int kp = kb + args.prefetch;
           if (args.prefetch > 0 && kp < nk) {
-            tma_prefetch_2d(&tm_a, kp * BK, ti.row0);
+            tma_prefetch_2d(&tm_a, kp * RE, ti.row0);
             if constexpr (GATED) {
-              tma_prefetch_3d(&tm_b0, kp * BK, ti.nt * (BN / 2), ti.expert);
-              tma_prefetch_3d(&tm_b1, kp * BK, ti.nt * (BN / 2), ti.expert);
+              tma_prefetch_3d(&tm_b0, kp * RE, ti.nt * (BN / 2), ti.expert);
+              tma_prefetch_3d(&tm_b1, kp * RE, ti.nt * (BN / 2), ti.expert);
             } else {
-              tma_prefetch_3d(&tm_b0, kp * BK, ti.nt * BN, ti.expert);
+              tma_prefetch_3d(&tm_b0, kp * RE, ti.nt * BN, ti.expert);
             }
           }
           armed |= 1u << stage;
@@ -475,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t ad = sdesc_sw128(smem_u32(smem + stage * STAGE_BYTES));
           const uint64_t bd = sdesc_sw128(smem_u32(smem + stage * STAGE_BYTES + A_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)  // K=16 per MMA: +32 bytes = +2 in the address field
-            umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < 4; ++k)  // 32 bytes of K per MMA: +2 in the address field
+            umma_f16<DT>(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -521,11 +555,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col0 = ti.nt * (BN / 2) + j * 32;
           if (valid) {
             uint32_t pk[16];
+            if constexpr (DT == DMOE_E4M3) {
+              // e4m3 operands: back to scale by the row's and each column's quantisation scale.
+              const float sa = args.a_scale[(int64_t)row * args.a_scale_ld];
+              const float* sg = args.b0_scale + (int64_t)ti.expert * args.n_out;
+              const float* su = args.b1_scale + (int64_t)ti.expert * args.n_out;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
-              const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
-              pk[i] = pack2<DT>(h0, h1);
+              for (int i = 0; i < 16; ++i) {
+                const int c = col0 + 2 * i;
+                const float g0 = c < args.n_out ? __uint_as_float(g[2 * i]) * sa * sg[c] : 0.f;
+                const float u0 = c < args.n_out ? __uint_as_float(u[2 * i]) * sa * su[c] : 0.f;
+                const float g1 = c + 1 < args.n_out ? __uint_as_float(g[2 * i + 1]) * sa * sg[c + 1] : 0.f;
+                const float u1 = c + 1 < args.n_out ? __uint_as_float(u[2 * i + 1]) * sa * su[c + 1] : 0.f;
+                pk[i] = pack2<out_dtype<DT>()>(act_fn(g0, args.act) * u0, act_fn(g1, args.act) * u1);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
+                const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
+                pk[i] = pack2<DT>(h0, h1);
+              }
             }
             char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
 #pragma unroll
@@ -656,14 +706,24 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+template <int DT>
 __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (DT == DMOE_E4M3) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
 // Arrive on the barrier at this offset in both CTAs of the pair once the MMAs issued so far complete.
@@ -765,7 +825,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int total_m = s_tile[n_seg];
   const int total = total_m * args.n_tiles_n;
-  const int nk = (args.K + BK2 - 1) / BK2;
+  constexpr int RE = row_elems<DT>();  // one swizzle row; a stage holds two
+  const int nk = (args.K + 2 * RE - 1) / (2 * RE);
   const uint32_t full_leader0 = map_to_cta(smem_u32(&full[0]), 0);
 
   if (warp == 0) {
@@ -792,14 +853,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const CUtensorMap* tb = (GATED && rank == 1) ? &tm_b1 : &tm_b0;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int k0 = kb * BK2 + h * BK;  // a box past K reads zeros and still counts its bytes
+            const int k0 = kb * 2 * RE + h * RE;  // a box past K reads zeros and still counts its bytes
             tma_load_2d_pair(sa + h * SUB2_BYTES, &tm_a, fbar, k0, arow);
             tma_load_3d_pair(sb + h * SUB2_BYTES, tb, fbar, k0, brow, ti.expert);
           }
           const int kp = kb + args.prefetch;
           if (args.prefetch > 0 && kp < nk) {
-            tma_prefetch_2d(&tm_a, kp * BK2, arow);
-            tma_prefetch_3d(tb, kp * BK2, brow, ti.expert);
+            tma_prefetch_2d(&tm_a, kp * 2 * RE, arow);
+            tma_prefetch_3d(tb, kp * 2 * RE, brow, ti.expert);
           }
           armed |= 1u << stage;
           armed_ph = (armed_ph & ~(1u << stage)) | (ph << stage);
@@ -846,10 +907,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t ad = sdesc_sw128(smem_u32(smem + stage * STAGE2_BYTES));
           const uint64_t bd = sdesc_sw128(smem_u32(smem + stage * STAGE2_BYTES + A2_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK2 / 16; ++k) {
-            // sub-box k/4 (16 KB = 1024 in the descriptor's 16-byte units), then +32 bytes per K=16
+          for (int k = 0; k < 8; ++k) {
+            // sub-box k/4 (16 KB = 1024 in the descriptor's 16-byte units), then +32 bytes of K per MMA
             const uint64_t off = (uint64_t)((k >> 2) * (SUB2_BYTES >> 4) + 2 * (k & 3));
-            umma_f16_pair(d_tmem, ad + off, bd + off, idesc, (kb | k) != 0);
+            umma_f16_pair<DT>(d_tmem, ad + off, bd + off, idesc, (kb | k) != 0);
           }
           umma_commit_both(&empty[stage]);
           if (++stage == STAGES2) {
@@ -898,11 +959,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col0 = ti.nt * (BN / 2) + j * 32;
           if (valid) {
             uint32_t pk[16];
+            if constexpr (DT == DMOE_E4M3) {
+              // e4m3 operands: back to scale by the row's and each column's quantisation scale.
+              const float sa = args.a_scale[(int64_t)row * args.a_scale_ld];
+              const float* sg = args.b0_scale + (int64_t)ti.expert * args.n_out;
+              const float* su = args.b1_scale + (int64_t)ti.expert * args.n_out;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
-              const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
-              pk[i] = pack2<DT>(h0, h1);
+              for (int i = 0; i < 16; ++i) {
+                const int c = col0 + 2 * i;
+                const float g0 = c < args.n_out ? __uint_as_float(g[2 * i]) * sa * sg[c] : 0.f;
+                const float u0 = c < args.n_out ? __uint_as_float(u[2 * i]) * sa * su[c] : 0.f;
+                const float g1 = c + 1 < args.n_out ? __uint_as_float(g[2 * i + 1]) * sa * sg[c + 1] : 0.f;
+                const float u1 = c + 1 < args.n_out ? __uint_as_float(u[2 * i + 1]) * sa * su[c + 1] : 0.f;
+                pk[i] = pack2<out_dtype<DT>()>(act_fn(g0, args.act) * u0, act_fn(g1, args.act) * u1);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
+                const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
+                pk[i] = pack2<DT>(h0, h1);
+              }
             }
             char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
 #pragma unroll
@@ -991,6 +1068,7 @@ PFN_encodeTiled get_encode_fn() {
 struct MapCacheEntry {
   const void* base;
   int dt, rank;
+  uint64_t ld;
   uint64_t dims[3];
   uint32_t box[3];
   int dev;
@@ -998,15 +1076,18 @@ struct MapCacheEntry {
 };
 constexpr int kMapCache = 64;
 
-// rank-2 or rank-3 row-major tensor; dims innermost first; box innermost first.
-int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_t* dims, const uint32_t* box) {
+// rank-2 or rank-3 row-major tensor of f16, bf16 or e4m3; dims innermost first; box innermost
+// first.  ld: bytes between rows (dimension 1) when they are not packed, 0 for packed rows.
+int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_t* dims, const uint32_t* box,
+             uint64_t ld = 0) {
   static thread_local MapCacheEntry cache[kMapCache];
   static thread_local int cache_n = 0, cache_next = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   for (int i = 0; i < cache_n; ++i) {
     const MapCacheEntry& c = cache[i];
-    if (c.base == base && c.dt == dt && c.rank == rank && c.dev == dev && c.dims[0] == dims[0] && c.box[0] == box[0] &&
+    if (c.base == base && c.dt == dt && c.rank == rank && c.dev == dev && c.ld == ld && c.dims[0] == dims[0] &&
+        c.box[0] == box[0] &&
         c.dims[1] == dims[1] && c.box[1] == box[1] && (rank < 3 || (c.dims[2] == dims[2] && c.box[2] == box[2]))) {
       *map = c.map;
       return DMOE_OK;
@@ -1016,15 +1097,18 @@ int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_
   DMOE_REQUIRE(enc != nullptr, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t gdim[3], gstride[2];
   cuuint32_t bdim[3], estr[3] = {1, 1, 1};
-  uint64_t stride = 2;
+  uint64_t stride = dt == DMOE_E4M3 ? 1 : 2;  // bytes of one element
   for (int i = 0; i < rank; ++i) {
     gdim[i] = dims[i];
     bdim[i] = box[i];
     if (i > 0) gstride[i - 1] = stride;
     stride *= dims[i];
+    if (i == 0 && ld != 0) stride = ld;
   }
-  CUresult r = enc(map, dt == DMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                   (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUtensorMapDataType et = dt == DMOE_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dt == DMOE_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, et, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -1035,6 +1119,7 @@ int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_
   c.dt = dt;
   c.rank = rank;
   c.dev = dev;
+  c.ld = ld;
   for (int i = 0; i < 3; ++i) {
     c.dims[i] = i < rank ? dims[i] : 0;
     c.box[i] = i < rank ? box[i] : 0;
@@ -1164,35 +1249,55 @@ void apply_scatter(GemmArgs& a, const ScatterSpec* sc) {
   for (int g = 0; g < DMOE_EP_MAX_RANKS; ++g) a.scatter_base[g] = sc->base[g];
 }
 
-template <int DT>
-int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack, int d, int I,
-            GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
-            cudaStream_t stream, int policy, const ScatterSpec* sc = nullptr) {
+// Quantisation scales of an e4m3 gate/up GEMM (GemmArgs::a_scale) and the A rows' stride.
+struct Fp8Scales {
+  const float* a;
+  int a_ld;       // floats between rows' scales
+  const float* gate;
+  const float* up;
+  uint64_t x_ld;  // bytes between A rows (0: packed)
+};
+
+void apply_scales(GemmArgs& a, const Fp8Scales* f) {
+  if (f == nullptr) return;
+  a.a_scale = f->a;
+  a.a_scale_ld = f->a_ld;
+  a.b0_scale = f->gate;
+  a.b1_scale = f->up;
+}
+
+// GEMM1 (gate/up + activation) on DT1 operands, GEMM2 (down) on DT2 operands; h is DT2.
+template <int DT1, int DT2>
+int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack, int d, int I,
+             GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
+             cudaStream_t stream, int policy, const ScatterSpec* sc = nullptr, const Fp8Scales* f8 = nullptr) {
+  static_assert(out_dtype<DT1>() == DT2, "h is written in the down GEMM's operand type");
+  constexpr int RE1 = row_elems<DT1>();
   CUtensorMap ta, tg, tu, th, td;
   {
     const uint64_t dims[2] = {(uint64_t)d, (uint64_t)m_rows};
-    const uint32_t box[2] = {BK, BM};
-    int r = make_map(&ta, DT, X, 2, dims, box);
+    const uint32_t box[2] = {RE1, BM};
+    int r = make_map(&ta, DT1, X, 2, dims, box, f8 ? f8->x_ld : 0);
     if (r) return r;
   }
   {
     const uint64_t dims[3] = {(uint64_t)d, (uint64_t)I, (uint64_t)E_stack};
-    const uint32_t box[3] = {BK, BN / 2, 1};
-    int r = make_map(&tg, DT, w_gate, 3, dims, box);
+    const uint32_t box[3] = {RE1, BN / 2, 1};
+    int r = make_map(&tg, DT1, w_gate, 3, dims, box);
     if (r) return r;
-    r = make_map(&tu, DT, w_up, 3, dims, box);
+    r = make_map(&tu, DT1, w_up, 3, dims, box);
     if (r) return r;
   }
   {
     const uint64_t dims[2] = {(uint64_t)I, (uint64_t)m_rows};
     const uint32_t box[2] = {BK, BM};
-    int r = make_map(&th, DT, H, 2, dims, box);
+    int r = make_map(&th, DT2, H, 2, dims, box);
     if (r) return r;
   }
   {
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
     const uint32_t box[3] = {BK, BN, 1};
-    int r = make_map(&td, DT, w_down, 3, dims, box);
+    int r = make_map(&td, DT2, w_down, 3, dims, box);
     if (r) return r;
   }
   const int nt1 = (I + BN / 2 - 1) / (BN / 2);
@@ -1208,7 +1313,7 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     CUtensorMap td2;
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
     const uint32_t box[3] = {BK, 128, 1};
-    int r = make_map(&td2, DT, w_down, 3, dims, box);
+    int r = make_map(&td2, DT2, w_down, 3, dims, box);
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
     GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
@@ -1216,18 +1321,20 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     GemmArgs s2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
     apply_scatter(a2, sc);
     apply_scatter(s2, sc);
+    apply_scales(a1, f8);
+    apply_scales(s1, f8);
     const int sms = usable_sms();
     segs.split = 1;
-    r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
+    r = launch_gemm_2sm<true, DT1>(ta, tg, tu, segs, a1, -1, stream);
     if (r) return r;
     segs.split = 2;
-    r = launch_gemm<true, DT>(ta, tg, tu, segs, s1, sms, stream);
+    r = launch_gemm<true, DT1>(ta, tg, tu, segs, s1, sms, stream);
     if (r) return r;
     segs.split = 1;
-    r = launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, -1, stream);
+    r = launch_gemm_2sm<false, DT2>(th, td2, td2, segs, a2, -1, stream);
     if (r) return r;
     segs.split = 2;
-    r = launch_gemm<false, DT>(th, td, td, segs, s2, sms, stream);
+    r = launch_gemm<false, DT2>(th, td, td, segs, s2, sms, stream);
     segs.split = 0;
     return r;
   }
@@ -1235,19 +1342,20 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     CUtensorMap td2;
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
     const uint32_t box[3] = {BK, 128, 1};
-    int r = make_map(&td2, DT, w_down, 3, dims, box);
+    int r = make_map(&td2, DT2, w_down, 3, dims, box);
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
     GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
     apply_scatter(a2, sc);
+    apply_scales(a1, f8);
     // Pair tiles only.  With the segment-by-segment tile order a remainder's pair tile reads
     // the expert's weights from L2 next to the expert's other tiles, while a separate
     // single-SM launch re-reads them from DRAM after the pair launch (measured on the
     // Mixtral layer, about 1000 rows per expert: 2.22 ms for pair tiles only against 2.26 ms
     // split); the split pays off for ragged experts of a few hundred rows.
-    r = launch_gemm_2sm<true, DT>(ta, tg, tu, segs, a1, -1, stream);
+    r = launch_gemm_2sm<true, DT1>(ta, tg, tu, segs, a1, -1, stream);
     if (r) return r;
-    return launch_gemm_2sm<false, DT>(th, td2, td2, segs, a2, -1, stream);
+    return launch_gemm_2sm<false, DT2>(th, td2, td2, segs, a2, -1, stream);
   }
   const int sms = usable_sms();
   int g1 = sms, g2 = sms;
@@ -1258,11 +1366,20 @@ int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_d
     g2 = (int)(t2 < sms ? t2 : sms);
   }
   GemmArgs a1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
-  int r = launch_gemm<true, DT>(ta, tg, tu, segs, a1, g1, stream);
+  apply_scales(a1, f8);
+  int r = launch_gemm<true, DT1>(ta, tg, tu, segs, a1, g1, stream);
   if (r) return r;
   GemmArgs a2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
   apply_scatter(a2, sc);
-  return launch_gemm<false, DT>(th, td, td, segs, a2, g2, stream);
+  return launch_gemm<false, DT2>(th, td, td, segs, a2, g2, stream);
+}
+
+template <int DT>
+int run_mlp(const void* X, const void* w_gate, const void* w_up, const void* w_down, int E_stack, int d, int I,
+            GemmSegs& segs, int total_m_host, int m_rows, int act, void* Y, void* H, int32_t* status,
+            cudaStream_t stream, int policy, const ScatterSpec* sc = nullptr) {
+  return run_mlp2<DT, DT>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m_host, m_rows, act, Y, H, status,
+                          stream, policy, sc, nullptr);
 }
 
 // Router logits on the tensor cores: L[T, E] = X[T, d] · W_r[E, d]^T in fp32 (the plain GEMM
@@ -1310,6 +1427,41 @@ using namespace dmoe;
 
 namespace dmoe {
 int gemm_sm_reserve() { return g_sm_reserve.load(std::memory_order_relaxed); }
+
+// Segment tables of a grouped MLP call: device tables are read by the kernels, host tables
+// are checked and copied into the launch parameters.  total_m: M tiles of a host table, -1
+// for a device table.
+int fill_segs(GemmSegs& segs, const int32_t* seg_expert, const int32_t* seg_end, int n_seg, int seg_on_device,
+              int m_rows, int E_stack, int* total_m) {
+  segs.n_seg = n_seg;
+  segs.m_rows = m_rows;
+  segs.e_stack = E_stack;
+  segs.split = 0;
+  *total_m = -1;
+  if (seg_on_device) {
+    DMOE_REQUIRE(n_seg <= kMaxSegDev, "dmoe_grouped_gated_mlp: n_seg=%d > %d", n_seg, kMaxSegDev);
+    segs.dev_expert = seg_expert;
+    segs.dev_end = seg_end;
+    return DMOE_OK;
+  }
+  DMOE_REQUIRE(n_seg <= 256, "dmoe_grouped_gated_mlp: n_seg=%d > 256 for host segment tables", n_seg);
+  segs.dev_expert = nullptr;
+  segs.dev_end = nullptr;
+  int prev = 0, tiles = 0;
+  for (int i = 0; i < n_seg; ++i) {
+    DMOE_REQUIRE(seg_end[i] >= prev && seg_end[i] <= m_rows, "dmoe_grouped_gated_mlp: segment %d end %d invalid", i,
+                 seg_end[i]);
+    DMOE_REQUIRE(seg_expert[i] >= 0 && seg_expert[i] < E_stack, "dmoe_grouped_gated_mlp: segment %d expert %d", i,
+                 seg_expert[i]);
+    segs.expert[i] = seg_expert[i];
+    segs.end[i] = seg_end[i];
+    tiles += (seg_end[i] - prev + BM - 1) / BM;
+    prev = seg_end[i];
+  }
+  *total_m = tiles;
+  return DMOE_OK;
+}
+
 }  // namespace dmoe
 
 extern "C" int dmoe_grouped_mlp_set_sm_reserve(int sms) {
@@ -1363,32 +1515,8 @@ extern "C" int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, cons
                "dmoe_grouped_gated_mlp: workspace %zu < %zu bytes", workspace_bytes,
                dmoe_grouped_mlp_workspace_size(m_rows, I, dtype));
   static thread_local GemmSegs segs;
-  segs.n_seg = n_seg;
-  segs.m_rows = m_rows;
-  segs.e_stack = E_stack;
-  segs.split = 0;
   int total_m = -1;
-  if (seg_on_device) {
-    DMOE_REQUIRE(n_seg <= kMaxSegDev, "dmoe_grouped_gated_mlp: n_seg=%d > %d", n_seg, kMaxSegDev);
-    segs.dev_expert = seg_expert;
-    segs.dev_end = seg_end;
-  } else {
-    DMOE_REQUIRE(n_seg <= 256, "dmoe_grouped_gated_mlp: n_seg=%d > 256 for host segment tables", n_seg);
-    segs.dev_expert = nullptr;
-    segs.dev_end = nullptr;
-    int prev = 0;
-    total_m = 0;
-    for (int i = 0; i < n_seg; ++i) {
-      DMOE_REQUIRE(seg_end[i] >= prev && seg_end[i] <= m_rows, "dmoe_grouped_gated_mlp: segment %d end %d invalid", i,
-                   seg_end[i]);
-      DMOE_REQUIRE(seg_expert[i] >= 0 && seg_expert[i] < E_stack, "dmoe_grouped_gated_mlp: segment %d expert %d", i,
-                   seg_expert[i]);
-      segs.expert[i] = seg_expert[i];
-      segs.end[i] = seg_end[i];
-      total_m += (seg_end[i] - prev + BM - 1) / BM;
-      prev = seg_end[i];
-    }
-  }
+  if (int r = fill_segs(segs, seg_expert, seg_end, n_seg, seg_on_device, m_rows, E_stack, &total_m)) return r;
   void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   cudaStream_t s = as_stream(stream);
   if (dtype == DMOE_BF16)
@@ -1408,45 +1536,92 @@ extern "C" int dmoe_grouped_gated_mlp(const void* X, const void* w_gate, const v
                                    DMOE_TILES_AUTO, stream);
 }
 
-extern "C" int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate, const void* w_up, const void* w_down,
-                                  int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
-                                  const int32_t* seg_end, int n_seg, int64_t cap, int act, void* workspace,
-                                  size_t workspace_bytes, int32_t* dev_status, int tile_policy, void* stream) {
+extern "C" int dmoe_grouped_gated_mlp_fp8(const void* Xq, const float* x_scale, const void* wg_q,
+                                          const float* wg_scale, const void* wu_q, const float* wu_scale,
+                                          const void* w_down, int E_stack, int d, int I, const int32_t* seg_expert,
+                                          const int32_t* seg_end, int n_seg, int seg_on_device, int m_rows, int act,
+                                          void* Y, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                          int tile_policy, void* stream) {
   clear_error();
+  DMOE_REQUIRE(tile_policy >= DMOE_TILES_AUTO && tile_policy <= DMOE_TILES_PAIR_SPLIT,
+               "dmoe_grouped_gated_mlp_fp8: bad tile policy %d", tile_policy);
+  DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "dmoe_grouped_gated_mlp_fp8: bad activation %d", act);
+  DMOE_REQUIRE(d > 0 && I > 0 && d % 16 == 0 && I % 8 == 0,
+               "dmoe_grouped_gated_mlp_fp8: d=%d must be a multiple of 16, I=%d of 8", d, I);
+  DMOE_REQUIRE(E_stack >= 1 && m_rows >= 0 && n_seg >= 0, "dmoe_grouped_gated_mlp_fp8: bad E_stack/m_rows/n_seg");
+  if (n_seg == 0 || m_rows == 0) return DMOE_OK;
+  DMOE_REQUIRE(Xq && x_scale && wg_q && wg_scale && wu_q && wu_scale && w_down && Y && workspace && dev_status &&
+                   seg_expert && seg_end,
+               "dmoe_grouped_gated_mlp_fp8: null pointer");
+  DMOE_REQUIRE(aligned16(Xq) && aligned16(wg_q) && aligned16(wu_q) && aligned16(w_down) && aligned16(Y) &&
+                   aligned16(workspace),
+               "dmoe_grouped_gated_mlp_fp8: tensors must be 16-byte aligned");
+  DMOE_REQUIRE(workspace_bytes >= dmoe_grouped_mlp_workspace_size(m_rows, I, DMOE_BF16),
+               "dmoe_grouped_gated_mlp_fp8: workspace %zu < %zu bytes", workspace_bytes,
+               dmoe_grouped_mlp_workspace_size(m_rows, I, DMOE_BF16));
+  static thread_local GemmSegs segs;
+  int total_m = -1;
+  if (int r = fill_segs(segs, seg_expert, seg_end, n_seg, seg_on_device, m_rows, E_stack, &total_m)) return r;
+  void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  const Fp8Scales f8{x_scale, 1, wg_scale, wu_scale, 0};
+  return run_mlp2<DMOE_E4M3, DMOE_BF16>(Xq, wg_q, wu_q, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H,
+                                        dev_status, as_stream(stream), tile_policy, nullptr, &f8);
+}
+
+namespace dmoe {
+namespace {
+// Checks shared by the 16-bit and the 8-bit exchange expert steps; fills the segment table
+// and the scatter targets (each host's return rows).
+int ep_mlp_setup(const char* name, const dmoe_ep_window* win, const void* w_gate, const void* w_up,
+                 const void* w_down, int E_stack, int d, int I, int h_dtype, const int32_t* seg_expert,
+                 const int32_t* seg_end, int n_seg, int64_t cap, int act, const void* workspace,
+                 size_t workspace_bytes, int32_t* dev_status, int tile_policy, GemmSegs& segs, ScatterSpec& sc) {
   DMOE_REQUIRE(win != nullptr && win->world >= 1 && win->world <= DMOE_EP_MAX_RANKS && win->rank >= 0 &&
                    win->rank < win->world,
-               "dmoe_ep_expert_mlp: bad window table");
-  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_ep_expert_mlp: dtype must be f16 or bf16");
-  DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "dmoe_ep_expert_mlp: bad activation %d", act);
-  DMOE_REQUIRE(d > 0 && I > 0 && d % 8 == 0 && I % 8 == 0, "dmoe_ep_expert_mlp: d=%d, I=%d must be multiples of 8", d,
-               I);
-  DMOE_REQUIRE(E_stack >= 1 && n_seg >= 0 && n_seg <= kMaxSegDev, "dmoe_ep_expert_mlp: bad E_stack/n_seg");
-  DMOE_REQUIRE(cap >= 0 && cap < (1ll << 31), "dmoe_ep_expert_mlp: bad capacity");
-  DMOE_REQUIRE(tile_policy >= DMOE_TILES_AUTO && tile_policy <= DMOE_TILES_PAIR_SPLIT,
-               "dmoe_ep_expert_mlp: bad tile policy %d", tile_policy);
+               "%s: bad window table", name);
+  DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "%s: bad activation %d", name, act);
+  DMOE_REQUIRE(d > 0 && I > 0 && d % 8 == 0 && I % 8 == 0, "%s: d=%d, I=%d must be multiples of 8", name, d, I);
+  DMOE_REQUIRE(E_stack >= 1 && n_seg >= 0 && n_seg <= kMaxSegDev, "%s: bad E_stack/n_seg", name);
+  DMOE_REQUIRE(cap >= 0 && cap < (1ll << 31), "%s: bad capacity", name);
+  DMOE_REQUIRE(tile_policy >= DMOE_TILES_AUTO && tile_policy <= DMOE_TILES_PAIR_SPLIT, "%s: bad tile policy %d", name,
+               tile_policy);
   if (n_seg == 0 || cap == 0) return DMOE_OK;
   const void* X = win->recv[win->rank];
   DMOE_REQUIRE(X && win->back[win->rank] && w_gate && w_up && w_down && workspace && dev_status && seg_expert &&
                    seg_end,
-               "dmoe_ep_expert_mlp: null pointer");
+               "%s: null pointer", name);
   for (int g = 0; g < win->world; ++g)
-    DMOE_REQUIRE(win->rows[g] != nullptr && aligned16(win->rows[g]), "dmoe_ep_expert_mlp: rank %d has no return rows",
-                 g);
+    DMOE_REQUIRE(win->rows[g] != nullptr && aligned16(win->rows[g]), "%s: rank %d has no return rows", name, g);
   DMOE_REQUIRE(aligned16(X) && aligned16(w_gate) && aligned16(w_up) && aligned16(w_down) && aligned16(workspace),
-               "dmoe_ep_expert_mlp: tensors must be 16-byte aligned");
-  DMOE_REQUIRE(workspace_bytes >= dmoe_grouped_mlp_workspace_size((int)cap, I, dtype),
-               "dmoe_ep_expert_mlp: workspace %zu < %zu bytes", workspace_bytes,
-               dmoe_grouped_mlp_workspace_size((int)cap, I, dtype));
-  static thread_local GemmSegs segs;
+               "%s: tensors must be 16-byte aligned", name);
+  DMOE_REQUIRE(workspace_bytes >= dmoe_grouped_mlp_workspace_size((int)cap, I, h_dtype), "%s: workspace %zu < %zu bytes",
+               name, workspace_bytes, dmoe_grouped_mlp_workspace_size((int)cap, I, h_dtype));
   segs.n_seg = n_seg;
   segs.m_rows = (int)cap;
   segs.e_stack = E_stack;
   segs.split = 0;
   segs.dev_expert = seg_expert;
   segs.dev_end = seg_end;
-  ScatterSpec sc{};
   sc.map = reinterpret_cast<const int32_t*>(win->back[win->rank]);
   for (int g = 0; g < DMOE_EP_MAX_RANKS; ++g) sc.base[g] = g < win->world ? reinterpret_cast<char*>(win->rows[g]) : nullptr;
+  return DMOE_OK;
+}
+}  // namespace
+}  // namespace dmoe
+
+extern "C" int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate, const void* w_up, const void* w_down,
+                                  int E_stack, int d, int I, int dtype, const int32_t* seg_expert,
+                                  const int32_t* seg_end, int n_seg, int64_t cap, int act, void* workspace,
+                                  size_t workspace_bytes, int32_t* dev_status, int tile_policy, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_ep_expert_mlp: dtype must be f16 or bf16");
+  static thread_local GemmSegs segs;
+  ScatterSpec sc{};
+  if (int r = ep_mlp_setup("dmoe_ep_expert_mlp", win, w_gate, w_up, w_down, E_stack, d, I, dtype, seg_expert, seg_end,
+                           n_seg, cap, act, workspace, workspace_bytes, dev_status, tile_policy, segs, sc))
+    return r;
+  if (n_seg == 0 || cap == 0) return DMOE_OK;
+  const void* X = win->recv[win->rank];
   void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   cudaStream_t s = as_stream(stream);
   if (dtype == DMOE_BF16)
@@ -1454,4 +1629,26 @@ extern "C" int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate,
                               s, tile_policy, &sc);
   return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H, dev_status, s,
                            tile_policy, &sc);
+}
+
+extern "C" int dmoe_ep_expert_mlp_fp8(const dmoe_ep_window* win, const void* wg_q, const float* wg_scale,
+                                      const void* wu_q, const float* wu_scale, const void* w_down, int E_stack, int d,
+                                      int I, const int32_t* seg_expert, const int32_t* seg_end, int n_seg, int64_t cap,
+                                      int act, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+                                      int tile_policy, void* stream) {
+  clear_error();
+  DMOE_REQUIRE(d % 16 == 0, "dmoe_ep_expert_mlp_fp8: d=%d must be a multiple of 16", d);
+  static thread_local GemmSegs segs;
+  ScatterSpec sc{};
+  if (int r = ep_mlp_setup("dmoe_ep_expert_mlp_fp8", win, wg_q, wu_q, w_down, E_stack, d, I, DMOE_BF16, seg_expert,
+                           seg_end, n_seg, cap, act, workspace, workspace_bytes, dev_status, tile_policy, segs, sc))
+    return r;
+  if (n_seg == 0 || cap == 0) return DMOE_OK;
+  DMOE_REQUIRE(wg_scale && wu_scale, "dmoe_ep_expert_mlp_fp8: null scale pointer");
+  // Receive records: d e4m3 codes, the row's fp32 scale, padding to d + 16 bytes.
+  const char* X = reinterpret_cast<const char*>(win->recv[win->rank]);
+  const Fp8Scales f8{reinterpret_cast<const float*>(X + d), (d + 16) / 4, wg_scale, wu_scale, (uint64_t)d + 16};
+  void* H = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  return run_mlp2<DMOE_E4M3, DMOE_BF16>(X, wg_q, wu_q, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H,
+                                        dev_status, as_stream(stream), tile_policy, &sc, &f8);
 }

@@ -37,6 +37,7 @@ extern "C" {
 #define DMOE_F32 0
 #define DMOE_F16 1
 #define DMOE_BF16 2
+#define DMOE_E4M3 3 /* 8-bit float (1-4-3): only where an entry point says so, always with fp32 scales */
 
 #define DMOE_ACT_RELU 0 /* reference: relu(gate) * up  (MoE/PipelineTask.py:518, MoE/MoE.py:25) */
 #define DMOE_ACT_SILU 1 /* SwiGLU: silu(gate) * up */
@@ -191,6 +192,31 @@ int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, const void* w_u
                               int d, int I, int dtype, const int32_t* seg_expert, const int32_t* seg_end, int n_seg,
                               int seg_on_device, int m_rows, int act, void* Y, void* workspace,
                               size_t workspace_bytes, int32_t* dev_status, int tile_policy, void* stream);
+
+/* 8-bit experts.  The reference's benchmark runs the layer on 8-bit float tensors (precision
+ * "fp8", src/python/MoE/benchmarks/bench.py:184-185); here the gate/up GEMM takes e4m3
+ * operands with fp32 row scales and the down GEMM stays bf16.
+ *
+ * dmoe_quantize_rows_e4m3: x [rows, cols] (f32/f16/bf16) -> q [rows, cols] e4m3 (rows q_ld
+ *   bytes apart) and scale (rows scale_ld floats apart), s = amax(|row|) / 448 (1 for an
+ *   all-zero row), q = e4m3_rn_satfinite(x / s).  cols % 16 == 0, q_ld >= cols and % 16 == 0;
+ *   x and q 16-byte aligned.  Activations give per-token scales; an expert weight [E, I, d]
+ *   viewed as [E * I, d] gives per-output-channel scales.
+ *
+ * dmoe_grouped_gated_mlp_fp8: as dmoe_grouped_gated_mlp_ex with
+ *   Xq [m_rows, d] e4m3, x_scale [m_rows];  wg_q, wu_q [E_stack, I, d] e4m3, wg_scale,
+ *   wu_scale [E_stack, I];  w_down [E_stack, d, I] bf16;  Y [m_rows, d] bf16.
+ *   gate = (Xq . wg_q^T) * x_scale[row] * wg_scale[e, col] (likewise up), accumulated in fp32
+ *   by tcgen05 kind::f8f6f4 MMAs; h = act(gate) * up rounded to bf16.  d % 16 == 0, I % 8 == 0;
+ *   workspace >= dmoe_grouped_mlp_workspace_size(m_rows, I, DMOE_BF16).
+ */
+int dmoe_quantize_rows_e4m3(const void* x, int dtype, int64_t rows, int cols, void* q, int64_t q_ld, float* scale,
+                            int64_t scale_ld, void* stream);
+int dmoe_grouped_gated_mlp_fp8(const void* Xq, const float* x_scale, const void* wg_q, const float* wg_scale,
+                               const void* wu_q, const float* wu_scale, const void* w_down, int E_stack, int d, int I,
+                               const int32_t* seg_expert, const int32_t* seg_end, int n_seg, int seg_on_device,
+                               int m_rows, int act, void* Y, void* workspace, size_t workspace_bytes,
+                               int32_t* dev_status, int tile_policy, void* stream);
 
 /*
  * Number of SMs (0..64, process-wide, default 0) that later dmoe_grouped_gated_mlp launches
@@ -355,6 +381,19 @@ int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate, const void
                        int E_stack, int d, int I, int dtype, const int32_t* seg_expert, const int32_t* seg_end,
                        int n_seg, int64_t cap, int act, void* workspace, size_t workspace_bytes, int32_t* dev_status,
                        int tile_policy, void* stream);
+
+/* The exchange's expert step with 8-bit receive rows: each receive record is d e4m3 codes,
+ * the row's fp32 scale at byte d, padding to d + 16 bytes (dmoe_quantize_rows_e4m3 with
+ * q_ld = d + 16, the scale pointer at q + d and scale_ld = (d + 16) / 4 makes them on the
+ * sending side; the gather then moves d + 16 bytes a row, about half the bytes of a bf16
+ * row).  Gate/up e4m3 [E_stack, I, d] with fp32 scales [E_stack, I]; down bf16
+ * [E_stack, d, I]; the return rows are bf16.  d % 16 == 0; workspace as dmoe_ep_expert_mlp
+ * with dtype DMOE_BF16. */
+int dmoe_ep_expert_mlp_fp8(const dmoe_ep_window* win, const void* wg_q, const float* wg_scale, const void* wu_q,
+                           const float* wu_scale, const void* w_down, int E_stack, int d, int I,
+                           const int32_t* seg_expert, const int32_t* seg_end, int n_seg, int64_t cap, int act,
+                           void* workspace, size_t workspace_bytes, int32_t* dev_status, int tile_policy,
+                           void* stream);
 
 /* Wait (bounded) until every other rank raised its flag of `kind` to this forward's epoch. */
 int dmoe_ep_wait(const dmoe_ep_window* win, int kind, uint64_t timeout_ns, int32_t* dev_status, void* stream);

@@ -329,6 +329,24 @@ def expert_grouped_mlp(X: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor
     return torch.nn.functional.grouped_mm(h, down_w[pos].transpose(1, 2), offs=offs)
 
 
+def quantize_rows_e4m3(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Row-wise e4m3 quantisation of the 8-bit expert path: s = amax(|row|) / 448 (1 for a
+    zero row), q = round-to-nearest-even(x / s) saturated to +-448, in fp32 on the CPU.  The
+    reference's benchmark only casts tensors to an 8-bit float (precision "fp8",
+    ``MoE/benchmarks/bench.py:184-185``); the scales are this implementation's, so the pin is
+    torch's own e4m3 rounding."""
+    xf = x.float().cpu()
+    s = xf.abs().amax(-1) / 448.0
+    s = torch.where(s > 0, s, torch.ones_like(s))
+    q = (xf / s[..., None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q, s
+
+
+def dequantize_rows_e4m3(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """q * s[row] in fp32."""
+    return q.float() * s[..., None]
+
+
 def expert_mlp_fp32(X: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, act: int) -> torch.Tensor:
     """One expert ``down(act(gate(x)) * up(x))`` (``MoE/MoE.py:27-28``) in fp32."""
     X = X.float()

@@ -81,6 +81,38 @@ def test_more_argument_checks_without_gpu():
                            ctypes.c_void_p(16), ctypes.c_void_p(16), 2, None) == 1
 
 
+def test_fp8_argument_checks_without_gpu():
+    """The 8-bit entry points reject rows that TMA cannot tile and bad arguments before any
+    CUDA call."""
+    from distributedmoe_b200 import _native as N
+    lib = N.lib()
+    p16 = ctypes.c_void_p(16)
+    # quantisation: cols a multiple of 16 (16-byte e4m3 rows), dtype f32/f16/bf16, strides
+    assert lib.dmoe_quantize_rows_e4m3(p16, 2, 4, 24, p16, 32, p16, 1, None) == 1
+    assert b"multiple of 16" in lib.dmoe_last_error()
+    assert lib.dmoe_quantize_rows_e4m3(p16, 3, 4, 32, p16, 32, p16, 1, None) == 1
+    assert lib.dmoe_quantize_rows_e4m3(p16, 2, 4, 32, p16, 40, p16, 1, None) == 1  # q_ld not a multiple of 16
+    assert lib.dmoe_quantize_rows_e4m3(p16, 2, 4, 32, p16, 32, p16, 0, None) == 1  # scale_ld < 1
+    assert lib.dmoe_quantize_rows_e4m3(None, 2, 0, 32, None, 32, None, 1, None) == 0  # nothing to do
+    # grouped MLP: d a multiple of 16, activation, tile policy, then the pointers
+    args = [None] * 7 + [4, 200, 128, None, None, 1, 0, 64, 1, None, None, 0, None, 0, None]
+    assert lib.dmoe_grouped_gated_mlp_fp8(*args) == 1 and b"multiple of 16" in lib.dmoe_last_error()
+    args[8] = 256
+    args[15] = 9
+    assert lib.dmoe_grouped_gated_mlp_fp8(*args) == 1 and b"activation" in lib.dmoe_last_error()
+    args[15] = 1
+    args[20] = 7
+    assert lib.dmoe_grouped_gated_mlp_fp8(*args) == 1 and b"tile policy" in lib.dmoe_last_error()
+    args[20] = 0
+    assert lib.dmoe_grouped_gated_mlp_fp8(*args) == 1 and b"null pointer" in lib.dmoe_last_error()
+    # exchange expert step: d a multiple of 16, then the window table
+    assert lib.dmoe_ep_expert_mlp_fp8(None, None, None, None, None, None, 4, 200, 128, None, None, 1, 64, 1, None, 0,
+                                      None, 0, None) == 1
+    assert b"multiple of 16" in lib.dmoe_last_error()
+    assert lib.dmoe_ep_expert_mlp_fp8(None, None, None, None, None, None, 4, 256, 128, None, None, 1, 64, 1, None, 0,
+                                      None, 0, None) == 1
+    assert b"window" in lib.dmoe_last_error()
+
 def test_no_cpu_fallback_in_product():
     """The product never imports the oracle."""
     pkg = os.path.join(ROOT, "distributedmoe_b200")

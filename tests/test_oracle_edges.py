@@ -103,3 +103,20 @@ def test_nan_logit_row_routes_to_valid_experts():
     assert torch.isfinite(w[0]).all() and torch.isfinite(w[3]).all()
     plan = O.route_plan(sel, w, E)
     assert sorted(plan.inverse.flatten().tolist()) == list(range(4 * k))
+
+
+def test_e4m3_row_quantisation_known_values():
+    """The 8-bit restatement: a row whose amax is 448 keeps scale 1 and e4m3's own codes
+    (448 -> 0x7e, 1.0 -> 0x38, -1.0 -> 0xb8, 2^-4 -> 0x18, the halfway 1.0625 rounds to even
+    1.0); a zero row gets scale 1; another row scales its amax to 448."""
+    x = torch.tensor([[448.0, 1.0, -1.0, 0.0625, 1.0625, 0.0, 0.0, 0.0],
+                      [0.0] * 8,
+                      [2.0, -1.0, 0.5, 0.0, 0.0, 0.0, 0.0, 0.0]])
+    q, s = O.quantize_rows_e4m3(x)
+    assert s.tolist() == [1.0, 1.0, torch.tensor(2.0 / 448.0, dtype=torch.float32).item()]
+    codes = q.view(torch.uint8)
+    assert codes[0, :5].tolist() == [0x7E, 0x38, 0xB8, 0x18, 0x38]
+    assert codes[1].tolist() == [0] * 8
+    assert codes[2, 0].item() == 0x7E and codes[2, 1].item() == 0xF6  # 448, -224
+    back = O.dequantize_rows_e4m3(q, s)
+    assert torch.allclose(back[2, :3], torch.tensor([2.0, -1.0, 0.5]), rtol=1e-6, atol=0)
