@@ -267,6 +267,134 @@ bool plan_single_eligible(int T, int k, int E) {
   return E <= kSingleMaxE && n <= (E <= 64 ? kSingleMax : kSingleMax / 4);
 }
 
+// Few experts (E <= 16, T*k <= 32768: Mixtral-style routing) in one CTA with one ranking
+// pass instead of rounds: thread j owns the contiguous activations [j*c, (j+1)*c) of the
+// slot-major order (c = ceil(T*k / 1024)).  Each thread counts its activations per expert
+// in 16-bit fields packed four to a 64-bit word (no field can exceed T*k <= 32768), one
+// block-wide exclusive scan of the four words gives every thread the number of earlier
+// activations of each expert, and the thread walks its activations again assigning
+// positions offset[e] + earlier[e] + running count.  Same order as the other paths.
+constexpr int kFewMaxE = 16;
+constexpr int kFewMax = 32768;
+constexpr int kFewThreads = 1024;
+
+__device__ __forceinline__ uint64_t pick4(const uint64_t (&v)[4], int q) {
+  return q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
+}
+
+__device__ __forceinline__ void add4(uint64_t (&v)[4], int e, uint64_t amount) {
+  const int q = e >> 2;
+  const uint64_t inc = amount << ((e & 3) * 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] += (q == i) ? inc : 0ull;
+}
+
+__device__ __forceinline__ int field4(const uint64_t (&v)[4], int e) {
+  return (int)((pick4(v, e >> 2) >> ((e & 3) * 16)) & 0xffffu);
+}
+
+__global__ void __launch_bounds__(kFewThreads, 1)
+    plan_few_experts(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E, int32_t* counts,
+                     int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse,
+                     void* perm_weight) {
+  extern __shared__ int8_t s_ex[];  // [n] expert of each activation (-1: none)
+  __shared__ uint64_t s_warp[32][4];
+  __shared__ uint64_t s_total[4];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = T * k;
+  // 1. experts of all activations, coalesced over tokens (eight loads in flight per thread)
+  for (int f0 = tid; f0 < n; f0 += 8 * kFewThreads) {
+    int64_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = f0 + u * kFewThreads;
+      v[u] = -1;
+      if (f < n) {
+        const int s = f / T, t = f - s * T;
+        v[u] = idx[(int64_t)t * k + s];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = f0 + u * kFewThreads;
+      if (f < n) s_ex[f] = (int8_t)((v[u] >= 0 && v[u] < E) ? (int)v[u] : -1);
+    }
+  }
+  __syncthreads();
+  // 2. counts of this thread's chunk, then a block-wide exclusive scan of the packed words
+  const int c = (n + kFewThreads - 1) / kFewThreads;
+  const int lo = min(n, tid * c), hi = min(n, lo + c);
+  uint64_t cnt[4] = {0, 0, 0, 0};
+  for (int f = lo; f < hi; ++f) {
+    const int e = s_ex[f];
+    if (e >= 0) add4(cnt, e, 1);
+  }
+  uint64_t incl[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    incl[q] = cnt[q];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t u = __shfl_up_sync(0xffffffffu, incl[q], o);
+      if (lane >= o) incl[q] += u;
+    }
+  }
+  if (lane == 31)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s_warp[warp][q] = incl[q];
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint64_t wv = s_warp[lane][q];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t u = __shfl_up_sync(0xffffffffu, wv, o);
+        if (lane >= o) wv += u;
+      }
+      s_warp[lane][q] = wv;  // inclusive over warps
+      if (lane == 31) s_total[q] = wv;
+    }
+  }
+  __syncthreads();
+  uint64_t base[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) base[q] = incl[q] - cnt[q] + (warp > 0 ? s_warp[warp - 1][q] : 0ull);
+  const uint64_t tot[4] = {s_total[0], s_total[1], s_total[2], s_total[3]};
+  int run = 0;
+  for (int e = 0; e < E; ++e) {
+    const int ce = field4(tot, e);
+    add4(base, e, (uint64_t)run);  // base[e] = offsets[e] + earlier activations of e
+    if (tid == e) {
+      counts[e] = ce;
+      offsets[e] = run;
+    }
+    run += ce;
+  }
+  if (tid == 0) offsets[E] = run;
+  // 3. positions, in order within the chunk
+  for (int f = lo; f < hi; ++f) {
+    const int e = s_ex[f];
+    const int s = f / T, t = f - s * T;
+    if (e >= 0) {
+      const int pos = field4(base, e);
+      add4(base, e, 1);
+      perm_token[pos] = t;
+      if (perm_slot) perm_slot[pos] = s;
+      if (inverse) inverse[(int64_t)t * k + s] = pos;
+      if (perm_weight) store_from_float(perm_weight, pos, load_as_float(w, (int64_t)t * k + s, w_dtype), w_dtype);
+    } else if (inverse) {
+      inverse[(int64_t)t * k + s] = -1;
+    }
+  }
+}
+
+bool plan_few_eligible(int T, int k, int E) {
+  const char* v = getenv("DMOE_PLAN_FEW");
+  if (v && v[0] == '0') return false;
+  return E <= kFewMaxE && (int64_t)T * k <= kFewMax;
+}
+
 // Scratch of dmoe_route_plan_noalloc: the per-chunk histogram matrix lives in this
 // library-owned device array instead of caller memory.  Every GPU that loads the library
 // holds it until the process exits.
@@ -328,6 +456,12 @@ extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, i
   DMOE_REQUIRE(workspace_bytes >= dmoe_route_plan_workspace_size(T, k, E), "dmoe_route_plan: workspace too small");
   cudaStream_t s = as_stream(stream);
   const int64_t n = (int64_t)T * k;
+  if (n > 0 && plan_few_eligible(T, k, E)) {
+    plan_few_experts<<<1, kFewThreads, (size_t)((n + 15) & ~int64_t(15)), s>>>(
+        idx, w, w_dtype, T, k, E, counts, offsets, perm_token, perm_slot, inverse, perm_weight);
+    DMOE_LAUNCH_CHECK();
+    return DMOE_OK;
+  }
   if (plan_single_eligible(T, k, E)) {
     static PerDeviceOnce once;
     int dev = 0;

@@ -295,21 +295,44 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
 
 // ------------------------------------------------------------------------- few experts
 // Softmax router for E <= 8 experts and 16-bit inputs (the Mixtral-style router).  One
-// persistent CTA per SM; its warps split the hidden dimension (warp w owns V runs of 512
-// contiguous bytes of every row) and each lane keeps its columns of all router rows in
-// registers as fp32 for the whole kernel, so the weights are read once per CTA.  Tiles of
-// consecutive tokens (contiguous in x) stream into a 4-stage shared-memory ring through
-// bulk async copies that complete on mbarriers: several tiles are in flight per SM
-// independent of the register budget.  Per token, a warp's EP partial dot products are
-// reduced with a butterfly reduce-scatter (EP/2 + ... + 1 + 2 shuffles) that leaves each
-// lane one expert's warp sum.  After one CTA barrier per tile, warp 0 alone sums the warps'
-// partials in a fixed order (one lane per token and expert), then each group of EP lanes
-// does its token's softmax and top-k with shuffles (same order as the warp kernel: NaN
-// first, then larger, then lower index) while the other warps go on with the next tile.
+// persistent CTA per SM with nw compute warps and one selection warp.  The compute warps
+// split the hidden dimension (warp w owns V runs of 512 contiguous bytes of every row) and
+// each lane keeps its columns of all router rows in registers as fp32 for the whole kernel,
+// so the weights are read once per CTA.  Tiles of consecutive tokens (contiguous in x)
+// stream into a 4-stage shared-memory ring through bulk async copies that complete on
+// mbarriers.  Per token, a warp's EP partial dot products are reduced with a butterfly
+// reduce-scatter (EP/2 + ... + 1 + 2 shuffles) that leaves each lane one expert's warp sum,
+// written to a double-buffered partials array.  No CTA-wide barrier: each compute warp
+// arrives on the tile's "partials written" mbarrier; the selection warp waits for it, refills
+// the consumed stage with the tile STAGES ahead, sums the warps' partials in a fixed order
+// (one lane per token and expert), does each token's softmax and top-k with shuffles (same
+// order as the warp kernel: NaN first, then larger, then lower index) and arrives on the
+// buffer's "partials read" mbarrier, which the compute warps wait for two tiles later.
+// Every wait is bounded; on expiry the warp raises a shared abort flag that ends every
+// other warp's waits, and the refilling thread drains its copies still in flight.
 constexpr int kSmallStages = 4;
 constexpr int kSmallStageBytes = 32 * 1024;
 constexpr int kSmallMaxTile = 16;
 constexpr uint64_t kSmallWaitNs = 2000000000ull;
+
+__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Bounded wait on an mbarrier phase; false (and the abort flag raised) on expiry or when
+// another warp has raised it.
+__device__ __forceinline__ bool bar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (bar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!bar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kSmallWaitNs) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
 
 // Butterfly reduce-scatter of EP values per lane over the 32 lanes of a warp: returns the
 // full warp sum of value number `expert_of_lane(lane)`.
@@ -349,18 +372,130 @@ __device__ __forceinline__ int expert_of_lane(int lane) {
   return (lane >> (5 - used)) & (EP - 1);
 }
 
+// Softmax + top-k of the tokens of one tile from the compute warps' partials (selection warp).
+template <int EP>
+__device__ __forceinline__ void select_tile(const RouterArgs& a, const float* part, int nw, int t0, int nt,
+                                            int lane) {
+  // lane = token-in-chunk * EP + expert; groups of EP lanes hold one token's logits
+  for (int r0 = 0; r0 < nt; r0 += 32 / EP) {
+    const int r = r0 + lane / EP, e = lane % EP;
+    const bool live = r < nt && e < a.E;
+    float l = -INFINITY;
+    if (live) {
+      float v = 0.f;
+      for (int w = 0; w < nw; ++w) v += part[(r * nw + w) * EP + e];
+      if (a.logit_bias) v += a.logit_bias[e];
+      if (a.logits_out) a.logits_out[(int64_t)(t0 + r) * a.E + e] = v;
+      l = v;
+    }
+    float m = l;
+#pragma unroll
+    for (int o = 1; o < EP; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, EP));
+    float p = live ? expf(l - m) : 0.f;
+    float ps = p;
+#pragma unroll
+    for (int o = 1; o < EP; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o, EP);
+    p = p / ps;
+    bool avail = live;
+    float wsum = 0.f, mine_w = 0.f;
+    int mine_e = 0;
+    for (int q = 0; q < a.k; ++q) {
+      float bv = avail ? l : -INFINITY;
+      int bi = avail ? e : 0x7fffffff;
+#pragma unroll
+      for (int o = 1; o < EP; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o, EP);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o, EP);
+        if (ranks_before(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      const float pw = __shfl_sync(0xffffffffu, p, (lane & ~(EP - 1)) | (bi & (EP - 1)), 32);
+      if (e == bi) avail = false;
+      wsum += pw;
+      if (e == q) {
+        mine_w = pw;
+        mine_e = bi;
+      }
+    }
+    if (r < nt && e < a.k) {
+      float w = a.renormalize ? mine_w / wsum : mine_w;
+      w *= a.scale;
+      a.idx_out[(int64_t)(t0 + r) * a.k + e] = mine_e;
+      store_from_float(a.w_out, (int64_t)(t0 + r) * a.k + e, w, a.w_dtype);
+    }
+  }
+}
+
 template <int DT, int EP, int V>
-__global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a, int tile_t, int n_tiles) {
+__global__ void __launch_bounds__(544, 1) router_small_kernel(const RouterArgs a, int tile_t, int n_tiles) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  const int nw = blockDim.x >> 5;
+  const int nw = (blockDim.x >> 5) - 1;  // compute warps; warp nw selects
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row_bytes = (int64_t)a.d * 2;
   uint8_t* ring = smem_raw;
   float* s_part = reinterpret_cast<float*>(smem_raw + kSmallStages * kSmallStageBytes);  // [2][tile][nw][EP]
   uint64_t* full = reinterpret_cast<uint64_t*>(s_part + 2 * tile_t * nw * EP);
-  constexpr int used = EP == 8 ? 3 : (EP == 4 ? 2 : (EP == 2 ? 1 : 0));
-  constexpr uint32_t low_mask = (1u << (5 - used)) - 1u;  // lanes sharing one reduced value
+  uint64_t* pfull = full + kSmallStages;  // [2]: every compute warp wrote its partials
+  uint64_t* pempty = pfull + 2;           // [2]: the selection warp read them
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(pempty + 2);
+  const int my_tiles = blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSmallStages; ++s) bar_init(&full[s], 1);
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&pfull[b], (uint32_t)nw);
+      bar_init(&pempty[b], 1);
+    }
+    *abort_flag = 0;
+    fence_async_shared();
+  }
+  __syncthreads();
+
+  auto issue = [&](int i) {
+    const int t0 = ((int)blockIdx.x + i * (int)gridDim.x) * tile_t;
+    const int nt = min(tile_t, a.T - t0);
+    const int s = i % kSmallStages;
+    const uint32_t bytes = (uint32_t)(nt * row_bytes);
+    bar_expect_tx(&full[s], bytes);
+    bulk_load(ring + s * kSmallStageBytes, reinterpret_cast<const char*>(a.x) + t0 * row_bytes, bytes, &full[s]);
+  };
+
+  if (warp == nw) {
+    // ---------------------------------------------------------------- selection + refills
+    int issued = 0;
+    if (lane == 0)
+      for (; issued < kSmallStages && issued < my_tiles; ++issued) issue(issued);
+    int done = 0;
+    for (int i = 0; i < my_tiles; ++i) {
+      const bool ok = bar_wait_bounded(&pfull[i & 1], (uint32_t)(i >> 1) & 1u, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      // every compute warp has consumed stage i % STAGES: refill it
+      if (lane == 0 && i + kSmallStages < my_tiles) {
+        fence_async_shared();
+        issue(i + kSmallStages);
+        issued = i + kSmallStages + 1;
+      }
+      const int t0 = ((int)blockIdx.x + i * (int)gridDim.x) * tile_t;
+      select_tile<EP>(a, s_part + (i & 1) * tile_t * nw * EP, nw, t0, min(tile_t, a.T - t0), lane);
+      __syncwarp();
+      if (lane == 0) bar_arrive(&pempty[i & 1]);
+      done = i + 1;
+    }
+    // After an abort, wait (bounded) for this thread's copies still in flight.
+    if (lane == 0) {
+      for (int j = done; j < issued; ++j) {
+        const uint32_t ph = (uint32_t)(j / kSmallStages) & 1u;
+        const uint64_t t0 = global_timer_ns();
+        while (!bar_try_wait(&full[j % kSmallStages], ph))
+          if (global_timer_ns() - t0 > kSmallWaitNs) break;
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute warps
   float wf[EP][V * 8];
 #pragma unroll
   for (int e = 0; e < EP; ++e)
@@ -371,41 +506,16 @@ __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a
       if (e < a.E) raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.w_r) + ((int64_t)e * a.d + col) * 2);
       unpack8<DT>(raw, &wf[e][j * 8]);
     }
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kSmallStages; ++s) bar_init(&full[s], 1);
-    fence_async_shared();
-  }
-  __syncthreads();
-
-  auto issue = [&](int i) {
-    const int tile = blockIdx.x + i * gridDim.x;
-    const int t0 = tile * tile_t;
-    const int nt = min(tile_t, a.T - t0);
-    const int s = i % kSmallStages;
-    const uint32_t bytes = (uint32_t)(nt * row_bytes);
-    bar_expect_tx(&full[s], bytes);
-    bulk_load(ring + s * kSmallStageBytes, reinterpret_cast<const char*>(a.x) + t0 * row_bytes, bytes, &full[s]);
-  };
-  if (threadIdx.x == 0)
-    for (int i = 0; i < kSmallStages && blockIdx.x + i * gridDim.x < n_tiles; ++i) issue(i);
-
+  constexpr int used = EP == 8 ? 3 : (EP == 4 ? 2 : (EP == 2 ? 1 : 0));
+  constexpr uint32_t low_mask = (1u << (5 - used)) - 1u;  // lanes sharing one reduced value
   const int my_e = expert_of_lane<EP>(lane);
-  for (int i = 0; blockIdx.x + i * gridDim.x < n_tiles; ++i) {
-    const int tile = blockIdx.x + i * gridDim.x;
-    const int t0 = tile * tile_t;
+  for (int i = 0; i < my_tiles; ++i) {
+    const int t0 = ((int)blockIdx.x + i * (int)gridDim.x) * tile_t;
     const int nt = min(tile_t, a.T - t0);
-    const int s = i % kSmallStages;
-    const uint32_t ph = (uint32_t)(i / kSmallStages) & 1u;
-    bool ok = bar_try_wait(&full[s], ph);
-    if (!ok) {
-      const uint64_t w0 = global_timer_ns();
-      while (!(ok = bar_try_wait(&full[s], ph)))
-        if (global_timer_ns() - w0 > kSmallWaitNs) break;
-    }
-    // A copy from valid memory does not fail; should one never land, every thread leaves
-    // together instead of waiting forever.
-    if (__syncthreads_or(!ok)) return;
-    const uint8_t* st = ring + s * kSmallStageBytes;
+    bool ok = bar_wait_bounded(&full[i % kSmallStages], (uint32_t)(i / kSmallStages) & 1u, abort_flag);
+    if (ok && i >= 2) ok = bar_wait_bounded(&pempty[i & 1], ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const uint8_t* st = ring + (i % kSmallStages) * kSmallStageBytes;
     float* part = s_part + (i & 1) * tile_t * nw * EP;
     for (int r = 0; r < nt; ++r) {
       float acc[EP];
@@ -424,63 +534,8 @@ __global__ void __launch_bounds__(512, 1) router_small_kernel(const RouterArgs a
       const float sum = warp_reduce_scatter<EP>(acc, lane);
       if ((lane & low_mask) == 0) part[(r * nw + warp) * EP + my_e] = sum;
     }
-    __syncthreads();  // the stage is consumed and every warp's partials are written
-    if (threadIdx.x == 0 && blockIdx.x + (i + kSmallStages) * gridDim.x < n_tiles) {
-      fence_async_shared();
-      issue(i + kSmallStages);
-    }
-    if (warp == 0) {
-      // lane = token-in-chunk * EP + expert; groups of EP lanes hold one token's logits
-      for (int r0 = 0; r0 < nt; r0 += 32 / EP) {
-        const int r = r0 + lane / EP, e = lane % EP;
-        const bool live = r < nt && e < a.E;
-        float l = -INFINITY;
-        if (live) {
-          float v = 0.f;
-          for (int w = 0; w < nw; ++w) v += part[(r * nw + w) * EP + e];
-          if (a.logit_bias) v += a.logit_bias[e];
-          if (a.logits_out) a.logits_out[(int64_t)(t0 + r) * a.E + e] = v;
-          l = v;
-        }
-        float m = l;
-#pragma unroll
-        for (int o = 1; o < EP; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, EP));
-        float p = live ? expf(l - m) : 0.f;
-        float ps = p;
-#pragma unroll
-        for (int o = 1; o < EP; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o, EP);
-        p = p / ps;
-        bool avail = live;
-        float wsum = 0.f, mine_w = 0.f;
-        int mine_e = 0;
-        for (int q = 0; q < a.k; ++q) {
-          float bv = avail ? l : -INFINITY;
-          int bi = avail ? e : 0x7fffffff;
-#pragma unroll
-          for (int o = 1; o < EP; o <<= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o, EP);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o, EP);
-            if (ranks_before(ov, oi, bv, bi)) {
-              bv = ov;
-              bi = oi;
-            }
-          }
-          const float pw = __shfl_sync(0xffffffffu, p, (lane & ~(EP - 1)) | (bi & (EP - 1)), 32);
-          if (e == bi) avail = false;
-          wsum += pw;
-          if (e == q) {
-            mine_w = pw;
-            mine_e = bi;
-          }
-        }
-        if (r < nt && e < a.k) {
-          float w = a.renormalize ? mine_w / wsum : mine_w;
-          w *= a.scale;
-          a.idx_out[(int64_t)(t0 + r) * a.k + e] = mine_e;
-          store_from_float(a.w_out, (int64_t)(t0 + r) * a.k + e, w, a.w_dtype);
-        }
-      }
-    }
+    __syncwarp();
+    if (lane == 0) bar_arrive(&pfull[i & 1]);
   }
 }
 
@@ -579,8 +634,8 @@ int run_router_small_dt(const RouterArgs& a, cudaStream_t s) {
   const int EP = a.E <= 4 ? 4 : 8;
   const int grid = n_tiles < 148 ? n_tiles : 148;
   const size_t smem = (size_t)kSmallStages * kSmallStageBytes + (size_t)2 * tile_t * nw * EP * sizeof(float) +
-                      kSmallStages * sizeof(uint64_t);
-  const int threads = nw * 32;
+                      (kSmallStages + 4) * sizeof(uint64_t) + 16;
+  const int threads = (nw + 1) * 32;
   if (EP == 8) return launch_router_small<DT, 8, 1>(grid, threads, smem, s, a, tile_t, n_tiles);
   if (V == 1) return launch_router_small<DT, 4, 1>(grid, threads, smem, s, a, tile_t, n_tiles);
   return launch_router_small<DT, 4, 2>(grid, threads, smem, s, a, tile_t, n_tiles);

@@ -142,15 +142,21 @@ def test_router_rejects_bad_args():
 
 
 # ----------------------------------------------------------------------------- plan
+# Plan paths: one CTA, one ranking pass (E <= 16, T*k <= 32768); one CTA in rounds of 1024
+# (E <= 64 up to 32768 activations, E <= 256 up to 8192); three launches otherwise.
+_PLAN_PATHS = {"few": {}, "single": {"DMOE_PLAN_FEW": "0"}, "multi": {"DMOE_PLAN_FEW": "0", "DMOE_PLAN_SINGLE": "0"}}
+
+
 @gpu
 @pytest.mark.parametrize("T,k,E", [(1, 1, 1), (1, 2, 8), (37, 2, 8), (5, 4, 16), (4096, 2, 8), (8192, 8, 256),
-                                   (4096, 8, 256), (16384, 2, 8), (3000, 8, 1024), (100, 1, 4), (16, 8, 128)])
-@pytest.mark.parametrize("single", ["1", "0"])
-def test_route_plan_bit_exact(T, k, E, single, monkeypatch):
-    """Both plan paths (one CTA for up to 32768 activations with E <= 64 and 8192 with
-    E <= 256, three launches otherwise; DMOE_PLAN_SINGLE=0 forces the latter) give the
-    oracle's plan bit for bit."""
-    monkeypatch.setenv("DMOE_PLAN_SINGLE", single)
+                                   (4096, 8, 256), (16384, 2, 8), (3000, 8, 1024), (100, 1, 4), (16, 8, 128),
+                                   (1000, 3, 13), (8192, 4, 16)])
+@pytest.mark.parametrize("path", sorted(_PLAN_PATHS))
+def test_route_plan_bit_exact(T, k, E, path, monkeypatch):
+    """Every plan path (DMOE_PLAN_FEW=0 and DMOE_PLAN_SINGLE=0 switch the one-CTA paths off)
+    gives the oracle's plan bit for bit wherever it applies."""
+    for key, v in _PLAN_PATHS[path].items():
+        monkeypatch.setenv(key, v)
     N = _nat()
     g = torch.Generator().manual_seed(T + 31 * k + E)
     # distinct experts per token, like top-k
@@ -170,10 +176,11 @@ def test_route_plan_bit_exact(T, k, E, single, monkeypatch):
 
 
 @gpu
-@pytest.mark.parametrize("single", ["1", "0"])
-def test_route_plan_invalid_experts_are_left_out(single, monkeypatch):
+@pytest.mark.parametrize("path", sorted(_PLAN_PATHS))
+def test_route_plan_invalid_experts_are_left_out(path, monkeypatch):
     """Indices outside [0, E) get no position: counts cover only valid ones, inverse is -1."""
-    monkeypatch.setenv("DMOE_PLAN_SINGLE", single)
+    for key, v in _PLAN_PATHS[path].items():
+        monkeypatch.setenv(key, v)
     N = _nat()
     T, k, E = 3000, 2, 8
     g = torch.Generator().manual_seed(9)
