@@ -53,8 +53,8 @@ class DistExpertsBlock(nn.Module):
         self._loop_stopped = threading.Event()
         self.hidden_features = config.hidden_features
         self.dtype = config.dtype
-        if self.dtype not in (torch.bfloat16, torch.float16):
-            raise NotImplementedError("the tcgen05 grouped expert MLP computes in bf16 or fp16")
+        if self.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise NotImplementedError("the tcgen05 grouped expert MLP computes in bf16, fp16 or fp32 (tf32 MMAs)")
         self.activation = ACTIVATIONS[config.activation]
 
         block_experts = config.expert_blocks[experts_block_index]

@@ -584,8 +584,8 @@ class DistMoEBlock(nn.Module):
                 or dn.shape != (n_local, d, g.shape[1]):
             raise ValueError(f"rank {rank} holds {n_local} expert instances: its stack must be gate/up "
                              f"[{n_local}, I, {d}] and down [{n_local}, {d}, I]")
-        if self.dtype not in (torch.bfloat16, torch.float16):
-            raise NotImplementedError("the device-driven data plane computes in bf16 or fp16")
+        if self.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise NotImplementedError("the device-driven data plane computes in bf16, fp16 or fp32")
         if expert_precision not in ("model", "fp8"):
             raise ValueError(f"expert_precision {expert_precision!r}: 'model' or 'fp8'")
         fp8 = expert_precision == "fp8"

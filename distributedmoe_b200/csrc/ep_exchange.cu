@@ -393,6 +393,28 @@ __global__ void ep_signal_kernel(EpPeers peers, int kind) {
 }
 
 // ------------------------------------------------------------------------- ep_combine
+// One 16-byte vector <-> its elements as floats: 8 of a 16-bit type, 4 of fp32.
+template <int DT>
+__device__ __forceinline__ void unpack_vec(const uint4& v, float* f) {
+  if constexpr (DT == DMOE_F32) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  } else {
+    unpack8<DT>(v, f);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ uint4 pack_vec(const float* f) {
+  if constexpr (DT == DMOE_F32) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  } else {
+    return make_uint4(pack2<DT>(f[0], f[1]), pack2<DT>(f[2], f[3]), pack2<DT>(f[4], f[5]), pack2<DT>(f[6], f[7]));
+  }
+}
+
 template <int DT, int KU, int CU>
 __global__ void __launch_bounds__(256) ep_combine_kernel(const char* __restrict__ rows, const int32_t* __restrict__ inverse,
                                                          const int32_t* __restrict__ ret, const void* __restrict__ w,
@@ -401,8 +423,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const char* __restrict_
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
-  const int nchunk = d / 8;
-  const int64_t row_vecs = d / 8;  // 16-byte vectors per row (16-bit types)
+  constexpr int EV = DT == DMOE_F32 ? 4 : 8;  // elements per 16-byte vector
+  const int nchunk = d / EV;
+  const int64_t row_vecs = d / EV;  // 16-byte vectors per row
   for (int t = warp; t < T; t += nwarps) {
     const uint4* src[KU];
     float wt[KU];
@@ -434,29 +457,24 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const char* __restrict_
       for (int u = 0; u < CU; ++u) {
         const int c = c0 + u * 32;
         if (c >= nchunk) break;
-        float acc[8];
+        float acc[EV];
         uint4* o = reinterpret_cast<uint4*>(out) + (int64_t)t * row_vecs + c;
         if (accumulate) {
-          unpack8<DT>(*o, acc);
+          unpack_vec<DT>(*o, acc);
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+          for (int j = 0; j < EV; ++j) acc[j] = 0.f;
         }
 #pragma unroll
         for (int s = 0; s < KU; ++s) {
           if (s < k && src[s] != nullptr) {
-            float v[8];
-            unpack8<DT>(raw[u][s], v);
+            float v[EV];
+            unpack_vec<DT>(raw[u][s], v);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = fmaf(wt[s], v[j], acc[j]);
+            for (int j = 0; j < EV; ++j) acc[j] = fmaf(wt[s], v[j], acc[j]);
           }
         }
-        uint4 pk;
-        pk.x = pack2<DT>(acc[0], acc[1]);
-        pk.y = pack2<DT>(acc[2], acc[3]);
-        pk.z = pack2<DT>(acc[4], acc[5]);
-        pk.w = pack2<DT>(acc[6], acc[7]);
-        *o = pk;
+        *o = pack_vec<DT>(acc);
       }
     }
   }
@@ -635,7 +653,8 @@ extern "C" int dmoe_ep_combine(const dmoe_ep_window* win, const int32_t* inverse
   if (r) return r;
   DMOE_REQUIRE(T >= 0 && k >= 1 && k <= 16, "dmoe_ep_combine: bad T=%d k=%d", T, k);
   DMOE_REQUIRE(d > 0 && d % 8 == 0, "dmoe_ep_combine: d=%d must be a multiple of 8", d);
-  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_ep_combine: rows must be f16 or bf16");
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16 || dtype == DMOE_F32,
+               "dmoe_ep_combine: rows must be f16, bf16 or f32");
   DMOE_REQUIRE(dtype_ok(w_dtype), "dmoe_ep_combine: bad weight dtype");
   if (T == 0) return DMOE_OK;
   DMOE_REQUIRE(inverse && ret && w && out && aligned16(out), "dmoe_ep_combine: null or unaligned pointer");
@@ -645,6 +664,8 @@ extern "C" int dmoe_ep_combine(const dmoe_ep_window* win, const int32_t* inverse
   const char* rows = p.rows[p.rank];
   if (dtype == DMOE_BF16)
     launch_ep_combine<DMOE_BF16>(blocks, s, rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
+  else if (dtype == DMOE_F32)
+    launch_ep_combine<DMOE_F32>(blocks, s, rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   else
     launch_ep_combine<DMOE_F16>(blocks, s, rows, inverse, ret, w, w_dtype, T, k, d, accumulate, out);
   DMOE_LAUNCH_CHECK();

@@ -33,13 +33,13 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;    // one 128-byte swizzle atom of 16-bit elements
 
-// Elements in one 128-byte swizzle row: 64 of a 16-bit type, 128 of e4m3.  Shared-memory
-// tiles, barriers and MMA counts are byte-based and the same for both; only the K extent of
-// a box and the MMA kind change (one kind::f16 MMA takes K=16, one kind::f8f6f4 MMA K=32:
-// 32 bytes of a row either way).
+// Elements in one 128-byte swizzle row: 64 of a 16-bit type, 128 of e4m3, 32 of fp32.
+// Shared-memory tiles, barriers and MMA counts are byte-based and the same for all; only the
+// K extent of a box and the MMA kind change (one kind::f16 MMA takes K=16, one kind::f8f6f4
+// MMA K=32, one kind::tf32 MMA K=8: 32 bytes of a row each).
 template <int DT>
 __host__ __device__ constexpr int row_elems() {
-  return DT == DMOE_E4M3 ? 128 : 64;
+  return DT == DMOE_E4M3 ? 128 : (DT == DMOE_F32 ? 32 : 64);
 }
 
 // Type a GEMM on DT operands stores: e4m3 products are stored as bf16.
@@ -102,15 +102,16 @@ struct GemmArgs {
   const float* b1_scale;
 };
 
-// Destination of output row `row` of a plain GEMM (nullptr: not stored).
+// Destination of output row `row` of a plain GEMM with ESZ-byte elements (nullptr: not stored).
+template <int ESZ>
 __device__ __forceinline__ char* out_row(const GemmArgs& args, int row, bool valid) {
   if (!valid) return nullptr;
-  if (!args.scatter) return reinterpret_cast<char*>(args.out) + (int64_t)row * args.ldo * 2;
+  if (!args.scatter) return reinterpret_cast<char*>(args.out) + (int64_t)row * args.ldo * ESZ;
   const int32_t code = args.scatter_map[row];
   if (code < 0) return nullptr;
   char* base = args.scatter_base[(uint32_t)code >> 27];  // index <= 15: code is non-negative
   if (base == nullptr) return nullptr;                    // no such rank: never stored
-  return base + (int64_t)(code & 0x7ffffff) * args.ldo * 2;
+  return base + (int64_t)(code & 0x7ffffff) * args.ldo * ESZ;
 }
 
 // ------------------------------------------------------------------------- PTX wrappers
@@ -224,6 +225,13 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+  } else if constexpr (DT == DMOE_F32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -277,11 +285,17 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
 }
 
 // Instruction descriptor: D fp32 (bit 4), A and B formats at bits 7 and 10 (kind::f16: f16 0,
-// bf16 1; kind::f8f6f4: e4m3 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24; M=128, N=256.
+// bf16 1; kind::tf32: tf32 2; kind::f8f6f4: e4m3 0), both K-major, N >> 3 at bit 17, M >> 4
+// at bit 24; M=128, N=256.
+template <int DT>
+__host__ __device__ constexpr uint32_t operand_format() {
+  return DT == DMOE_BF16 ? 1u : (DT == DMOE_F32 ? 2u : 0u);
+}
+
 template <int DT>
 __host__ __device__ constexpr uint32_t make_idesc() {
-  return (1u << 4) | ((DT == DMOE_BF16 ? 1u : 0u) << 7) | ((DT == DMOE_BF16 ? 1u : 0u) << 10) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  return (1u << 4) | (operand_format<DT>() << 7) | (operand_format<DT>() << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ float act_fn(float g, int act) {
@@ -553,7 +567,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
           const int col0 = ti.nt * (BN / 2) + j * 32;
-          if (valid) {
+          if (valid && DT == DMOE_F32) {
+            // fp32 operands (tf32 MMAs): h is stored in fp32, eight 16-byte vectors per 32 columns
+            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float h[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                h[i] = act_fn(__uint_as_float(g[4 * v + i]), args.act) * __uint_as_float(u[4 * v + i]);
+              if (col0 + v * 4 < args.n_out) *reinterpret_cast<float4*>(dst + v * 4) = make_float4(h[0], h[1], h[2], h[3]);
+            }
+          } else if (valid) {
             uint32_t pk[16];
             if constexpr (DT == DMOE_E4M3) {
               // e4m3 operands: back to scale by the row's and each column's quantisation scale.
@@ -585,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        char* const drow = args.out_f32 ? nullptr : out_row(args, row, valid);
+        char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
           uint32_t y[32];
@@ -594,6 +619,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col0 = ti.nt * BN + j * 32;
           if (valid && args.out_f32) {
             float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col0 + v * 4 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else if (drow != nullptr && DT == DMOE_F32) {
+            float* dst = reinterpret_cast<float*>(drow) + col0;
 #pragma unroll
             for (int v = 0; v < 8; ++v)
               if (col0 + v * 4 < args.n_out)
@@ -648,9 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   bye       (both) count 1: exit handshake, so no CTA leaves while the peer may still
 //             touch its shared memory.
 constexpr int BM2 = 256;
-constexpr int BK2 = 128;                      // two 64-wide swizzle atoms per stage: 8 MMAs per barrier round
-constexpr int STAGES2 = 3;
-constexpr int SUB2_BYTES = 128 * BK * 2;      // one [128 x 64] box
+constexpr int STAGES2 = 3;                    // a stage: two 128-byte swizzle rows of K, 8 MMAs per barrier round
+constexpr int SUB2_BYTES = 128 * BK * 2;      // one box: 128 rows x 128 bytes
 constexpr int A2_BYTES = 2 * SUB2_BYTES;
 constexpr int B2_BYTES = 2 * SUB2_BYTES;
 constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
@@ -716,6 +746,13 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, 
         "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+  } else if constexpr (DT == DMOE_F32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -737,8 +774,8 @@ __device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
 
 template <int DT>
 __host__ __device__ constexpr uint32_t make_idesc_pair() {
-  return (1u << 4) | ((DT == DMOE_BF16 ? 1u : 0u) << 7) | ((DT == DMOE_BF16 ? 1u : 0u) << 10) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+  return (1u << 4) | (operand_format<DT>() << 7) | (operand_format<DT>() << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM2 >> 4) << 24);
 }
 
 template <bool GATED, int DT>
@@ -957,7 +994,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
           const int col0 = ti.nt * (BN / 2) + j * 32;
-          if (valid) {
+          if (valid && DT == DMOE_F32) {
+            // fp32 operands (tf32 MMAs): h is stored in fp32, eight 16-byte vectors per 32 columns
+            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float h[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                h[i] = act_fn(__uint_as_float(g[4 * v + i]), args.act) * __uint_as_float(u[4 * v + i]);
+              if (col0 + v * 4 < args.n_out) *reinterpret_cast<float4*>(dst + v * 4) = make_float4(h[0], h[1], h[2], h[3]);
+            }
+          } else if (valid) {
             uint32_t pk[16];
             if constexpr (DT == DMOE_E4M3) {
               // e4m3 operands: back to scale by the row's and each column's quantisation scale.
@@ -989,7 +1037,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        char* const drow = args.out_f32 ? nullptr : out_row(args, row, valid);
+        char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
           uint32_t y[32];
@@ -998,6 +1046,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col0 = ti.nt * BN + j * 32;
           if (valid && args.out_f32) {
             float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col0 + v * 4 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else if (drow != nullptr && DT == DMOE_F32) {
+            float* dst = reinterpret_cast<float*>(drow) + col0;
 #pragma unroll
             for (int v = 0; v < 8; ++v)
               if (col0 + v * 4 < args.n_out)
@@ -1097,7 +1151,7 @@ int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_
   DMOE_REQUIRE(enc != nullptr, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t gdim[3], gstride[2];
   cuuint32_t bdim[3], estr[3] = {1, 1, 1};
-  uint64_t stride = dt == DMOE_E4M3 ? 1 : 2;  // bytes of one element
+  uint64_t stride = dt == DMOE_E4M3 ? 1 : (dt == DMOE_F32 ? 4 : 2);  // bytes of one element
   for (int i = 0; i < rank; ++i) {
     gdim[i] = dims[i];
     bdim[i] = box[i];
@@ -1107,6 +1161,7 @@ int make_map(CUtensorMap* map, int dt, const void* base, int rank, const uint64_
   }
   const CUtensorMapDataType et = dt == DMOE_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : dt == DMOE_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : dt == DMOE_F32  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = enc(map, et, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1273,6 +1328,7 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
              cudaStream_t stream, int policy, const ScatterSpec* sc = nullptr, const Fp8Scales* f8 = nullptr) {
   static_assert(out_dtype<DT1>() == DT2, "h is written in the down GEMM's operand type");
   constexpr int RE1 = row_elems<DT1>();
+  constexpr int RE2 = row_elems<DT2>();
   CUtensorMap ta, tg, tu, th, td;
   {
     const uint64_t dims[2] = {(uint64_t)d, (uint64_t)m_rows};
@@ -1290,13 +1346,13 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
   }
   {
     const uint64_t dims[2] = {(uint64_t)I, (uint64_t)m_rows};
-    const uint32_t box[2] = {BK, BM};
+    const uint32_t box[2] = {RE2, BM};
     int r = make_map(&th, DT2, H, 2, dims, box);
     if (r) return r;
   }
   {
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
-    const uint32_t box[3] = {BK, BN, 1};
+    const uint32_t box[3] = {RE2, BN, 1};
     int r = make_map(&td, DT2, w_down, 3, dims, box);
     if (r) return r;
   }
@@ -1312,7 +1368,7 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
     // SM-tile units instead of four.  Both launches read the same segment table.
     CUtensorMap td2;
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
-    const uint32_t box[3] = {BK, 128, 1};
+    const uint32_t box[3] = {RE2, 128, 1};
     int r = make_map(&td2, DT2, w_down, 3, dims, box);
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
@@ -1341,7 +1397,7 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
   if (pair) {
     CUtensorMap td2;
     const uint64_t dims[3] = {(uint64_t)I, (uint64_t)d, (uint64_t)E_stack};
-    const uint32_t box[3] = {BK, 128, 1};
+    const uint32_t box[3] = {RE2, 128, 1};
     int r = make_map(&td2, DT2, w_down, 3, dims, box);
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
@@ -1487,8 +1543,7 @@ extern "C" int dmoe_router_logits(const void* x, const void* w_r, int dtype, int
 }
 
 extern "C" size_t dmoe_grouped_mlp_workspace_size(int m_rows, int I, int dtype) {
-  (void)dtype;
-  return (size_t)m_rows * (size_t)I * 2 + 256;
+  return (size_t)m_rows * (size_t)I * (dtype == DMOE_F32 ? 4 : 2) + 256;
 }
 
 extern "C" int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, const void* w_up, const void* w_down,
@@ -1499,7 +1554,8 @@ extern "C" int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, cons
   clear_error();
   DMOE_REQUIRE(tile_policy >= DMOE_TILES_AUTO && tile_policy <= DMOE_TILES_PAIR_SPLIT,
                "dmoe_grouped_gated_mlp: bad tile policy %d", tile_policy);
-  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_grouped_gated_mlp: dtype must be f16 or bf16");
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16 || dtype == DMOE_F32,
+               "dmoe_grouped_gated_mlp: dtype must be f16, bf16 or f32");
   DMOE_REQUIRE(act == DMOE_ACT_RELU || act == DMOE_ACT_SILU, "dmoe_grouped_gated_mlp: bad activation %d", act);
   DMOE_REQUIRE(d > 0 && I > 0 && d % 8 == 0 && I % 8 == 0, "dmoe_grouped_gated_mlp: d=%d, I=%d must be multiples of 8",
                d, I);
@@ -1522,6 +1578,9 @@ extern "C" int dmoe_grouped_gated_mlp_ex(const void* X, const void* w_gate, cons
   if (dtype == DMOE_BF16)
     return run_mlp<DMOE_BF16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s,
                               tile_policy);
+  if (dtype == DMOE_F32)
+    return run_mlp<DMOE_F32>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s,
+                             tile_policy);
   return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, total_m, m_rows, act, Y, H, dev_status, s,
                            tile_policy);
 }
@@ -1614,7 +1673,8 @@ extern "C" int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate,
                                   const int32_t* seg_end, int n_seg, int64_t cap, int act, void* workspace,
                                   size_t workspace_bytes, int32_t* dev_status, int tile_policy, void* stream) {
   clear_error();
-  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16, "dmoe_ep_expert_mlp: dtype must be f16 or bf16");
+  DMOE_REQUIRE(dtype == DMOE_BF16 || dtype == DMOE_F16 || dtype == DMOE_F32,
+               "dmoe_ep_expert_mlp: dtype must be f16, bf16 or f32");
   static thread_local GemmSegs segs;
   ScatterSpec sc{};
   if (int r = ep_mlp_setup("dmoe_ep_expert_mlp", win, w_gate, w_up, w_down, E_stack, d, I, dtype, seg_expert, seg_end,
@@ -1627,6 +1687,9 @@ extern "C" int dmoe_ep_expert_mlp(const dmoe_ep_window* win, const void* w_gate,
   if (dtype == DMOE_BF16)
     return run_mlp<DMOE_BF16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H, dev_status,
                               s, tile_policy, &sc);
+  if (dtype == DMOE_F32)
+    return run_mlp<DMOE_F32>(X, w_gate, w_up, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H, dev_status,
+                             s, tile_policy, &sc);
   return run_mlp<DMOE_F16>(X, w_gate, w_up, w_down, E_stack, d, I, segs, -1, (int)cap, act, nullptr, H, dev_status, s,
                            tile_policy, &sc);
 }

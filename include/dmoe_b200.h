@@ -159,7 +159,9 @@ int dmoe_permute_rows(const void* src, void* dst, int64_t row_bytes, const int32
  *   h = act(gate_out) * up_out; Y = grouped_mm(h, Wd^T); copy into the output buffer.
  * Weights are the stacks of DistExpertsBlock.initialize_expert_layers
  * (MoE/DistExpertsBlock.py:163-177) in nn.Linear layout:
- *   w_gate, w_up [E_stack, I, d]; w_down [E_stack, d, I]   (dtype DMOE_F16 or DMOE_BF16)
+ *   w_gate, w_up [E_stack, I, d]; w_down [E_stack, d, I]   (dtype DMOE_F16, DMOE_BF16, or DMOE_F32:
+ *   fp32 operands run as tf32 MMAs (10-bit mantissa operands, fp32 accumulation) with h in fp32,
+ *   the reference's fp32 precision)
  * Segment i covers rows [seg_end[i-1], seg_end[i]) (seg_end[-1] = 0) and uses stack entry
  * seg_expert[i]; rows outside every segment are not written.  seg_* are host arrays when
  * seg_on_device == 0 (n_seg <= 256), device arrays otherwise (n_seg <= 1024).
@@ -295,7 +297,7 @@ int dmoe_flag_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, in
  *     MoE/pools/BuffersPool.py:55-71) -> dmoe_ep_dispatch (peer stores into the receiver),
  *   WRITE of the expert output + HostOutputBufferUnlocked (MoE/PipelineTask.py:555-565;
  *     MoE/pools/BuffersPool.py:73-90) -> dmoe_ep_signal / dmoe_ep_wait (epoch flags),
- *   HostPipelineTask.combine (MoE/PipelineTask.py:306-370) -> dmoe_ep_combine (peer loads).
+ *   HostPipelineTask.combine (MoE/PipelineTask.py:306-370) -> dmoe_ep_combine (local rows).
  * Between dmoe_ep_wait(DATA) and dmoe_ep_signal(RESULTS) each rank runs ONE
  * dmoe_ep_expert_mlp over its receive buffer with the device segment table that
  * dmoe_ep_plan wrote (seg_expert, seg_end; n_seg = the rank's instance count); its
@@ -405,7 +407,8 @@ int dmoe_ep_signal(const dmoe_ep_window* win, int kind, void* stream);
 /*
  * out[t] = (out[t] if accumulate) + sum_s w[t,s] * rows[t*k + s], over this rank's own return
  * rows (written by the owners' epilogues), skipping slots whose activation was dropped
- * (ret[inverse[t*k+s]] < 0); fp32 accumulation, one store.
+ * (ret[inverse[t*k+s]] < 0); fp32 accumulation, one store.  dtype: DMOE_BF16, DMOE_F16 or
+ * DMOE_F32 (rows and out).
  */
 int dmoe_ep_combine(const dmoe_ep_window* win, const int32_t* inverse, const int32_t* ret, const void* w, int w_dtype,
                     int T, int k, int d, int dtype, int accumulate, void* out, void* stream);

@@ -331,3 +331,34 @@ def test_direct_layer_fp8_experts(graphs):
         ref16 = _oracle(x, w_r, gate, up, down, k)
         rel = ((y.double() - ref16.double()).norm() / ref16.double().norm()).item()
         assert rel < 0.08, rel
+
+
+@gpu
+def test_direct_layer_fp32():
+    """An fp32 layer on the direct plane: fp32 rows cross the window, the expert GEMMs run on
+    tf32 tensor cores, the combine accumulates fp32 rows; against fp32 math."""
+    from distributedmoe_b200 import _native as N
+    from distributedmoe_b200.MoE.local_cluster import LocalCluster
+    from distributedmoe_b200.TensorTransferEngine import TensorTransferEngineBackend as B
+    E, k, d, I = 8, 2, 256, 384
+    gate, up, down, w_r, g = _weights(E, d, I, 31)
+    gate, up, down, w_r = gate.float(), up.float(), down.float(), w_r.float()
+    blocks = [[0, 1, 2, 3], [4, 5, 6, 7], [2, 5]]
+    stacked = [(gate[b].contiguous(), up[b].contiguous(), down[b].contiguous()) for b in blocks]
+    cl = LocalCluster(E, blocks, k, d, torch.float32, DEV, [DEV] * len(blocks), stacked=stacked, io_buffer_size=256,
+                      number_of_io_buffers=1, backend=B.NVLinkDirect, max_tokens=1024, activation="silu",
+                      renormalize=True, expert_block_policy="least_loaded")
+    outs = []
+    try:
+        with torch.no_grad():
+            cl.moe.gate.weight.copy_(w_r)
+        for T in [1, 300, 1024]:
+            x = torch.randn(T, d, generator=g, device=DEV)
+            outs.append((x, cl.moe(x)))
+        torch.cuda.synchronize()
+        N.check_device_status(DEV)
+    finally:
+        cl.close()
+    for x, y in outs:
+        assert y.shape == x.shape and y.dtype == torch.float32
+        _check(y, _oracle(x, w_r, gate, up, down, k))

@@ -77,6 +77,14 @@ def test_forward_reference_test_shape_fp16():
 
 
 @gpu
+def test_forward_reference_test_shape_fp32():
+    """The reference test's "--precision fp32" (MoE/tests/conftest.py:17-21): fp32 layer, the
+    expert GEMMs on tf32 tensor cores (operands rounded to a 10-bit mantissa, fp32
+    accumulation), within the same bars against fp32 math."""
+    _run(512, 2048, 128, 8, 6144, [list(range(128))], 8192, dtype=torch.float32, x_mean=10.0, forwards=1)
+
+
+@gpu
 def test_forward_split_tasks_two_blocks_silu_renorm_3d():
     _run(700, 128, 8, 2, 256, [[0, 2, 4, 6], [1, 3, 5, 7]], 1024, act="silu", renorm=True, shape3d=True)
 

@@ -309,7 +309,7 @@ def _mlp_ref_fp32(X, wg, wu, wd, experts, ends, act):
 
 
 @gpu
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("act", [O.ACT_RELU, O.ACT_SILU])
 @pytest.mark.parametrize("E,d,I,sizes", [
     (1, 64, 128, [128]),
