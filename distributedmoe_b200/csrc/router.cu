@@ -539,6 +539,198 @@ __global__ void __launch_bounds__(544, 1) router_small_kernel(const RouterArgs a
   }
 }
 
+// ------------------------------------------------------------------------- few experts, MMA
+// The same router with the dot products on the tensor cores (16x8x16 bf16/f16 MMAs with fp32
+// accumulation), for E <= 8 and d a multiple of 1024 up to 5120: a 16-token group is one MMA
+// row block and the (up to) 8 experts one column block, so a warp's 16 x 16 slice of x costs
+// one MMA instead of 64 FMAs per lane.  Per CTA: a producer warp streams each group's rows in
+// K-chunks of 1024 elements (16 bulk copies of 2 KB, one per token, into rows padded by 16
+// bytes so that 8x8 matrix loads hit 32 banks) through a 4-stage ring; 4 compute warps each
+// take 256 columns of every chunk and keep a 16 x 8 fp32 accumulator over the group's chunks;
+// the selection warp sums the 4 partials in a fixed order and selects as router_small_kernel.
+// The router rows sit in shared memory (padded the same way) for the whole kernel.
+constexpr int kMmaChunk = 1024;        // K elements per stage
+constexpr int kMmaWarps = 4;           // compute warps: 256 columns of a chunk each
+constexpr int kMmaStages = 4;
+constexpr int kMmaRowPad = 16;         // bytes after each 2 KB row (bank spread for ldmatrix)
+constexpr int kMmaRowStride = kMmaChunk * 2 + kMmaRowPad;
+constexpr int kMmaStageBytes = 16 * kMmaRowStride;
+constexpr int kMmaMaxD = 5120;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+template <int DT>
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  if constexpr (DT == DMOE_BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__((kMmaWarps + 2) * 32, 1) router_mma_kernel(const RouterArgs a, int n_groups) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = a.d / kMmaChunk;
+  const int w_stride = a.d * 2 + kMmaRowPad;  // bytes between router rows in shared memory
+  uint8_t* ring = smem_raw;
+  uint8_t* s_w = ring + kMmaStages * kMmaStageBytes;                       // [8][d] padded
+  float* s_part = reinterpret_cast<float*>(s_w + 8 * w_stride);            // [2][16][4][8]
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_part + 2 * 16 * kMmaWarps * 8);
+  uint64_t* empty = full + kMmaStages;
+  uint64_t* pfull = empty + kMmaStages;  // [2]: the compute warps wrote a group's partials
+  uint64_t* pempty = pfull + 2;          // [2]: the selection warp read them
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(pempty + 2);
+  const int my_groups = (int)blockIdx.x < n_groups ? (n_groups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int64_t row_bytes = (int64_t)a.d * 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMmaStages; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], kMmaWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&pfull[b], kMmaWarps);
+      bar_init(&pempty[b], 1);
+    }
+    *abort_flag = 0;
+    fence_async_shared();
+  }
+  // Router rows (zero rows past E) into shared memory by every thread.
+  for (int i = threadIdx.x; i < 8 * (a.d / 8); i += blockDim.x) {
+    const int e = i / (a.d / 8), c = i - e * (a.d / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (e < a.E) v = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.w_r) + (int64_t)e * row_bytes + c * 16);
+    *reinterpret_cast<uint4*>(s_w + e * w_stride + c * 16) = v;
+  }
+  __syncthreads();
+
+  const int total = my_groups * nch;  // stages this CTA streams
+  if (warp == kMmaWarps + 1) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int j = 0;
+      for (; j < total; ++j) {
+        const int s = j % kMmaStages;
+        if (j >= kMmaStages && !bar_wait_bounded(&empty[s], ((uint32_t)(j / kMmaStages) & 1u) ^ 1u, abort_flag)) break;
+        const int g = (int)blockIdx.x + (j / nch) * (int)gridDim.x, c = j % nch;
+        const int t0 = g * 16, nt = min(16, a.T - t0);
+        bar_expect_tx(&full[s], (uint32_t)(nt * kMmaChunk * 2));
+        uint8_t* dst = ring + s * kMmaStageBytes;
+        const char* src = reinterpret_cast<const char*>(a.x) + (int64_t)t0 * row_bytes + (int64_t)c * kMmaChunk * 2;
+        for (int r = 0; r < nt; ++r) bulk_load(dst + r * kMmaRowStride, src + r * row_bytes, kMmaChunk * 2, &full[s]);
+      }
+      // After an abort, wait (bounded) for the copies still in flight.
+      if (j < total) {
+        for (int q = j - kMmaStages > 0 ? j - kMmaStages : 0; q < j; ++q) {
+          const uint64_t t0 = global_timer_ns();
+          while (!bar_try_wait(&full[q % kMmaStages], (uint32_t)(q / kMmaStages) & 1u))
+            if (global_timer_ns() - t0 > kSmallWaitNs) break;
+        }
+      }
+    }
+    return;
+  }
+  if (warp == kMmaWarps) {
+    // ---------------------------------------------------------------- selection
+    for (int i = 0; i < my_groups; ++i) {
+      const bool ok = bar_wait_bounded(&pfull[i & 1], (uint32_t)(i >> 1) & 1u, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int t0 = ((int)blockIdx.x + i * (int)gridDim.x) * 16;
+      select_tile<8>(a, s_part + (i & 1) * 16 * kMmaWarps * 8, kMmaWarps, t0, min(16, a.T - t0), lane);
+      __syncwarp();
+      if (lane == 0) bar_arrive(&pempty[i & 1]);
+    }
+    return;
+  }
+  // ------------------------------------------------------------------ compute warps
+  // ldmatrix addresses: A rows lane % 16, 8-column block lane / 16; B (router rows) lane % 8,
+  // 8-column block (lane / 8) % 2.
+  const uint32_t a_off = (uint32_t)((lane & 15) * kMmaRowStride + (lane >> 4) * 16 + warp * 512);
+  const uint32_t b_base = smem_addr(s_w) + (uint32_t)((lane & 7) * w_stride + ((lane >> 3) & 1) * 16);
+  int j = 0;
+  for (int i = 0; i < my_groups; ++i) {
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    bool ok = true;
+    for (int c = 0; c < nch && ok; ++c, ++j) {
+      const int s = j % kMmaStages;
+      ok = bar_wait_bounded(&full[s], (uint32_t)(j / kMmaStages) & 1u, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      const uint32_t a_base = smem_addr(ring + s * kMmaStageBytes) + a_off;
+      const uint32_t kb = (uint32_t)(c * kMmaChunk + warp * 256) * 2;  // byte column of this warp's slice
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {  // 16 steps of 16 columns
+        uint32_t a0, a1, a2, a3, b0, b1;
+        ldsm_x4(a_base + q * 32, a0, a1, a2, a3);
+        ldsm_x2(b_base + kb + q * 32, b0, b1);
+        mma_16816<DT>(acc[q & 1], a0, a1, a2, a3, b0, b1);
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(&empty[s]);
+    }
+    if (!ok) break;
+    if (i >= 2 && !__all_sync(0xffffffffu, bar_wait_bounded(&pempty[i & 1], ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag)))
+      break;
+    // D fragment: rows lane / 4 and lane / 4 + 8, experts 2 * (lane % 4) and + 1
+    float* part = s_part + (i & 1) * 16 * kMmaWarps * 8;
+    const int r = lane >> 2, e = 2 * (lane & 3);
+    part[(r * kMmaWarps + warp) * 8 + e] = acc[0][0] + acc[1][0];
+    part[(r * kMmaWarps + warp) * 8 + e + 1] = acc[0][1] + acc[1][1];
+    part[((r + 8) * kMmaWarps + warp) * 8 + e] = acc[0][2] + acc[1][2];
+    part[((r + 8) * kMmaWarps + warp) * 8 + e + 1] = acc[0][3] + acc[1][3];
+    __syncwarp();
+    if (lane == 0) bar_arrive(&pfull[i & 1]);
+  }
+}
+
+bool router_mma_eligible(int x_dtype, int mode, const float* logits_in, int E, int d) {
+  if (logits_in != nullptr || mode != DMOE_ROUTER_SOFTMAX || E > 8) return false;
+  if (x_dtype != DMOE_BF16 && x_dtype != DMOE_F16) return false;
+  if (d % kMmaChunk != 0 || d > kMmaMaxD) return false;
+  const char* v = getenv("DMOE_ROUTER_MMA");
+  return !(v && v[0] == '0');
+}
+
+template <int DT>
+int run_router_mma(const RouterArgs& a, cudaStream_t s) {
+  const int n_groups = (a.T + 15) / 16;
+  const int grid = n_groups < 148 ? n_groups : 148;
+  const size_t smem = (size_t)kMmaStages * kMmaStageBytes + (size_t)8 * (a.d * 2 + kMmaRowPad) +
+                      (size_t)2 * 16 * kMmaWarps * 8 * sizeof(float) + (2 * kMmaStages + 4) * sizeof(uint64_t) + 16;
+  static PerDeviceOnce once;
+  int dev = 0;
+  DMOE_CUDA(cudaGetDevice(&dev));
+  const int r = once_per_device(once, dev, [] {
+    DMOE_CUDA(cudaFuncSetAttribute(router_mma_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    return DMOE_OK;
+  });
+  if (r) return r;
+  router_mma_kernel<DT><<<grid, (kMmaWarps + 2) * 32, smem, s>>>(a, n_groups);
+  DMOE_LAUNCH_CHECK();
+  return DMOE_OK;
+}
+
 // Router logits for few tokens (decode): the tensor-core logits GEMM would give the whole
 // reduction to one or two CTAs when T is small, so here eight experts go to each CTA: their
 // weight rows land in shared memory with one bulk copy, each warp takes tokens in turn and
@@ -719,6 +911,9 @@ extern "C" int dmoe_router(const void* x, const void* w_r, int x_dtype, const fl
   if (T == 0) return DMOE_OK;
   RouterArgs a{x, w_r, logit_bias, score_bias, logits_in, logits_out, idx_out, w_out, T, d, E, k, mode,
                renormalize, mode == DMOE_ROUTER_SIGMOID_GROUP ? n_group : 1, topk_group, w_dtype, scale};
+  if (router_mma_eligible(x_dtype, mode, logits_in, E, d))
+    return x_dtype == DMOE_BF16 ? run_router_mma<DMOE_BF16>(a, as_stream(stream))
+                                : run_router_mma<DMOE_F16>(a, as_stream(stream));
   if (router_small_eligible(x_dtype, mode, logits_in, E, d)) return run_router_small(x_dtype, a, as_stream(stream));
   int blocks = (T + kRouterWarps - 1) / kRouterWarps;
   cudaStream_t s = as_stream(stream);

@@ -202,16 +202,23 @@ def test_route_plan_invalid_experts_are_left_out(path, monkeypatch):
 
 
 @gpu
-@pytest.mark.parametrize("T,d,E,k", [(4096, 4096, 8, 2), (4097, 4096, 8, 2), (33, 2048, 6, 3), (500, 8192, 4, 2),
-                                     (17, 256, 2, 1)])
-def test_router_few_experts_ring_kernel(T, d, E, k):
-    """The few-expert router (weights in registers, token tiles through a bulk-copy ring):
-    logits within fp32 summation error of the oracle's, selection bit-exact from them, with
-    a logit bias, renormalisation and a scale; also the Mixtral shape."""
+@pytest.mark.parametrize("T,d,E,k,dtype", [(4096, 4096, 8, 2, torch.bfloat16), (4097, 4096, 8, 2, torch.bfloat16),
+                                           (33, 2048, 6, 3, torch.bfloat16), (500, 8192, 4, 2, torch.bfloat16),
+                                           (17, 256, 2, 1, torch.bfloat16), (1, 1024, 8, 2, torch.bfloat16),
+                                           (300, 5120, 8, 2, torch.bfloat16), (1000, 3072, 8, 2, torch.float16)])
+@pytest.mark.parametrize("kernel", ["mma", "ring"])
+def test_router_few_experts_kernels(T, d, E, k, dtype, kernel, monkeypatch):
+    """The few-expert routers -- 16x8x16 tensor-core MMAs over 16-token groups (d a multiple
+    of 1024 up to 5120), or weights in registers with token tiles through a bulk-copy ring
+    (DMOE_ROUTER_MMA=0, and every other shape): logits within fp32 summation error of the
+    oracle's, selection bit-exact from them, with a logit bias, renormalisation and a scale;
+    also the Mixtral shape and a ragged last group."""
+    if kernel == "ring":
+        monkeypatch.setenv("DMOE_ROUTER_MMA", "0")
     N = _nat()
     g = torch.Generator().manual_seed(T + d + E)
-    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
-    w_r = (torch.randn(E, d, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, d, generator=g).to(dtype)
+    w_r = (torch.randn(E, d, generator=g) * 0.02).to(dtype)
     bias = torch.randn(E, generator=g)
     idx, w, logits = N.router(x.to(DEV), w_r.to(DEV), k, want_logits=True, logit_bias=bias.to(DEV),
                               renormalize=True, scale=1.5, w_dtype=torch.float32)
