@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter(const int64_t* idx,
   }
 }
 
-// Small plans (T*k <= kSingleMax with E <= 64, T*k <= kSingleMax / 4 with E <= kSingleMaxE)
+// Small plans (T*k <= kSingleMax / 2 with E <= 64, T*k <= kSingleMax / 4 with E <= kSingleMaxE)
 // in one CTA of 1024 threads, one launch instead of three: the expert of every activation is
 // read once into shared memory (int16) while the histogram builds; one block-wide scan gives counts and offsets; then rounds of
 // 1024 consecutive activations (in the slot-major order f = s*T + t) are ranked stably:
@@ -155,10 +155,14 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
   int32_t* s_run = sm;                          // [E] running position of each expert
   const int ws = E + 1;                         // row stride of s_wc: a column walk hits 32 banks
   int32_t* s_wc = sm + kSingleMaxE;             // [32][E + 1] per-warp counts, then their prefixes
+  const int n = T * k;
+  const int na = (n + 15) & ~15;
   int16_t* s_e = reinterpret_cast<int16_t*>(s_wc + 32 * ws);  // [n] expert of each activation (-1: none)
+  int16_t* s_pos = s_e + na;                                  // [n] position of activation f (-1: none)
+  int16_t* s_tok = s_pos + na;                                // [n] token of position p
+  int8_t* s_slot = reinterpret_cast<int8_t*>(s_tok + na);     // [n] slot of position p
   __shared__ int32_t s_warp[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = T * k;
   for (int e = tid; e < E; e += kSingleThreads) s_run[e] = 0;
   __syncthreads();
   // 1. experts of all activations (eight loads in flight per thread) and the histogram
@@ -238,23 +242,35 @@ __global__ void __launch_bounds__(kSingleThreads, 1)
     __syncthreads();
     if (f < n) {
       const int s = f / T, t = f - (f / T) * T;
+      int pos = -1;
       if (e >= 0) {
-        const int pos = s_wc[warp * ws + e] + rank_in_warp;
-        perm_token[pos] = t;
-        if (perm_slot) perm_slot[pos] = s;
-        if (inverse) inverse[(int64_t)t * k + s] = pos;
-        if (perm_weight) store_from_float(perm_weight, pos, load_as_float(w, (int64_t)t * k + s, w_dtype), w_dtype);
-      } else if (inverse) {
-        inverse[(int64_t)t * k + s] = -1;
+        pos = s_wc[warp * ws + e] + rank_in_warp;
+        s_tok[pos] = (int16_t)t;
+        s_slot[pos] = (int8_t)s;
       }
+      s_pos[f] = (int16_t)pos;
     }
     __syncthreads();
+  }
+  // 4. in-order (coalesced) stores from shared memory: by position, then by (token, slot)
+  const int n_valid = s_run[E - 1];  // the last expert's running position is the end
+  for (int p = tid; p < n_valid; p += kSingleThreads) {
+    const int t = s_tok[p], s = s_slot[p];
+    perm_token[p] = t;
+    if (perm_slot) perm_slot[p] = s;
+    if (perm_weight) store_from_float(perm_weight, p, load_as_float(w, (int64_t)t * k + s, w_dtype), w_dtype);
+  }
+  if (inverse) {
+    for (int i = tid; i < n; i += kSingleThreads) {
+      const int t = i / k, s = i - t * k;
+      inverse[i] = s_pos[s * T + t];
+    }
   }
 }
 
 size_t plan_single_smem(int T, int k, int E) {
-  return (size_t)(kSingleMaxE + 32 * (E + 1)) * sizeof(int32_t) +
-         (((size_t)T * k * sizeof(int16_t) + 15) & ~size_t(15));
+  const size_t na = (size_t)(((int64_t)T * k + 15) & ~int64_t(15));
+  return (size_t)(kSingleMaxE + 32 * (E + 1)) * sizeof(int32_t) + 7 * na;  // expert, position, token, slot
 }
 
 bool plan_single_eligible(int T, int k, int E) {
@@ -264,7 +280,7 @@ bool plan_single_eligible(int T, int k, int E) {
   // and many rounds (DeepSeek's 256 experts at 32768 activations) cost more than the three
   // grid-wide launches of the multi-CTA path.
   const int64_t n = (int64_t)T * k;
-  return E <= kSingleMaxE && n <= (E <= 64 ? kSingleMax : kSingleMax / 4);
+  return E <= kSingleMaxE && n <= (E <= 64 ? kSingleMax / 2 : kSingleMax / 4);
 }
 
 // Few experts (E <= 16, T*k <= 32768: Mixtral-style routing) in one CTA with one ranking
@@ -273,7 +289,10 @@ bool plan_single_eligible(int T, int k, int E) {
 // in 16-bit fields packed four to a 64-bit word (no field can exceed T*k <= 32768), one
 // block-wide exclusive scan of the four words gives every thread the number of earlier
 // activations of each expert, and the thread walks its activations again assigning
-// positions offset[e] + earlier[e] + running count.  Same order as the other paths.
+// positions offset[e] + earlier[e] + running count.  Same order as the other paths.  The
+// results are assembled in shared memory (token and slot by position, position by
+// activation) and written out in order at the end: one SM's scattered 4-byte stores to
+// global memory, not its arithmetic, bound the one-CTA plans.
 constexpr int kFewMaxE = 16;
 constexpr int kFewMax = 32768;
 constexpr int kFewThreads = 1024;
@@ -293,15 +312,25 @@ __device__ __forceinline__ int field4(const uint64_t (&v)[4], int e) {
   return (int)((pick4(v, e >> 2) >> ((e & 3) * 16)) & 0xffffu);
 }
 
+size_t plan_few_smem(int64_t n) {
+  const size_t na = (size_t)((n + 15) & ~int64_t(15));
+  return 6 * na;  // expert and slot (int8), position and token (int16) per activation
+}
+
 __global__ void __launch_bounds__(kFewThreads, 1)
-    plan_few_experts(const int64_t* idx, const void* w, int w_dtype, int T, int k, int E, int32_t* counts,
-                     int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse,
-                     void* perm_weight) {
-  extern __shared__ int8_t s_ex[];  // [n] expert of each activation (-1: none)
+    plan_few_experts(const int64_t* __restrict__ idx, const void* __restrict__ w, int w_dtype, int T, int k, int E,
+                     int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_token,
+                     int32_t* __restrict__ perm_slot, int32_t* __restrict__ inverse, void* __restrict__ perm_weight) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
   __shared__ uint64_t s_warp[32][4];
   __shared__ uint64_t s_total[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = T * k;
+  const int na = (n + 15) & ~15;
+  int8_t* s_ex = reinterpret_cast<int8_t*>(sm_raw);             // [n] expert of activation f (-1: none)
+  int8_t* s_slot = s_ex + na;                                    // [n] slot of position p
+  int16_t* s_pos = reinterpret_cast<int16_t*>(s_slot + na);      // [n] position of activation f (-1: none)
+  int16_t* s_tok = s_pos + na;                                   // [n] token of position p
   // 1. experts of all activations, coalesced over tokens (eight loads in flight per thread)
   for (int f0 = tid; f0 < n; f0 += 8 * kFewThreads) {
     int64_t v[8];
@@ -372,19 +401,31 @@ __global__ void __launch_bounds__(kFewThreads, 1)
     run += ce;
   }
   if (tid == 0) offsets[E] = run;
-  // 3. positions, in order within the chunk
+  // 3. positions, in order within the chunk, into shared memory
   for (int f = lo; f < hi; ++f) {
     const int e = s_ex[f];
-    const int s = f / T, t = f - s * T;
+    int pos = -1;
     if (e >= 0) {
-      const int pos = field4(base, e);
+      pos = field4(base, e);
       add4(base, e, 1);
-      perm_token[pos] = t;
-      if (perm_slot) perm_slot[pos] = s;
-      if (inverse) inverse[(int64_t)t * k + s] = pos;
-      if (perm_weight) store_from_float(perm_weight, pos, load_as_float(w, (int64_t)t * k + s, w_dtype), w_dtype);
-    } else if (inverse) {
-      inverse[(int64_t)t * k + s] = -1;
+      const int s = f / T;
+      s_tok[pos] = (int16_t)(f - s * T);
+      s_slot[pos] = (int8_t)s;
+    }
+    s_pos[f] = (int16_t)pos;
+  }
+  __syncthreads();
+  // 4. in-order (coalesced) stores: by position, then by (token, slot)
+  for (int p = tid; p < run; p += kFewThreads) {
+    const int t = s_tok[p], s = s_slot[p];
+    perm_token[p] = t;
+    if (perm_slot) perm_slot[p] = s;
+    if (perm_weight) store_from_float(perm_weight, p, load_as_float(w, (int64_t)t * k + s, w_dtype), w_dtype);
+  }
+  if (inverse) {
+    for (int i = tid; i < n; i += kFewThreads) {
+      const int t = i / k, s = i - t * k;
+      inverse[i] = s_pos[s * T + t];
     }
   }
 }
@@ -457,8 +498,17 @@ extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, i
   cudaStream_t s = as_stream(stream);
   const int64_t n = (int64_t)T * k;
   if (n > 0 && plan_few_eligible(T, k, E)) {
-    plan_few_experts<<<1, kFewThreads, (size_t)((n + 15) & ~int64_t(15)), s>>>(
-        idx, w, w_dtype, T, k, E, counts, offsets, perm_token, perm_slot, inverse, perm_weight);
+    static PerDeviceOnce once_few;
+    int dev = 0;
+    DMOE_CUDA(cudaGetDevice(&dev));
+    const int r = once_per_device(once_few, dev, [] {
+      DMOE_CUDA(cudaFuncSetAttribute(plan_few_experts, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)plan_few_smem(kFewMax)));
+      return DMOE_OK;
+    });
+    if (r) return r;
+    plan_few_experts<<<1, kFewThreads, plan_few_smem(n), s>>>(idx, w, w_dtype, T, k, E, counts, offsets, perm_token,
+                                                              perm_slot, inverse, perm_weight);
     DMOE_LAUNCH_CHECK();
     return DMOE_OK;
   }
@@ -468,7 +518,7 @@ extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, i
     DMOE_CUDA(cudaGetDevice(&dev));
     const int r = once_per_device(once, dev, [] {
       DMOE_CUDA(cudaFuncSetAttribute(plan_single, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)plan_single_smem(kSingleMax, 1, kSingleMaxE)));
+                                     (int)plan_single_smem(kSingleMax / 2, 1, 64)));
       return DMOE_OK;
     });
     if (r) return r;

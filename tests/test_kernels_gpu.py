@@ -143,7 +143,7 @@ def test_router_rejects_bad_args():
 
 # ----------------------------------------------------------------------------- plan
 # Plan paths: one CTA, one ranking pass (E <= 16, T*k <= 32768); one CTA in rounds of 1024
-# (E <= 64 up to 32768 activations, E <= 256 up to 8192); three launches otherwise.
+# (E <= 64 up to 16384 activations, E <= 256 up to 8192); three launches otherwise.
 _PLAN_PATHS = {"few": {}, "single": {"DMOE_PLAN_FEW": "0"}, "multi": {"DMOE_PLAN_FEW": "0", "DMOE_PLAN_SINGLE": "0"}}
 
 
