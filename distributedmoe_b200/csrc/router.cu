@@ -598,7 +598,8 @@ __global__ void __launch_bounds__((kMmaWarps + 2) * 32, 1) router_mma_kernel(con
   uint64_t* empty = full + kMmaStages;
   uint64_t* pfull = empty + kMmaStages;  // [2]: the compute warps wrote a group's partials
   uint64_t* pempty = pfull + 2;          // [2]: the selection warp read them
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(pempty + 2);
+  uint64_t* wbar = pempty + 2;           // the router rows landed
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(wbar + 1);
   const int my_groups = (int)blockIdx.x < n_groups ? (n_groups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int64_t row_bytes = (int64_t)a.d * 2;
 
@@ -611,15 +612,18 @@ __global__ void __launch_bounds__((kMmaWarps + 2) * 32, 1) router_mma_kernel(con
       bar_init(&pfull[b], kMmaWarps);
       bar_init(&pempty[b], 1);
     }
+    bar_init(wbar, 1);
     *abort_flag = 0;
     fence_async_shared();
+    // The router rows arrive by bulk copies, like the tokens; rows past E are zeroed below.
+    bar_expect_tx(wbar, (uint32_t)(a.E * row_bytes));
+    for (int e = 0; e < a.E; ++e)
+      bulk_load(s_w + e * w_stride, reinterpret_cast<const char*>(a.w_r) + (int64_t)e * row_bytes, (uint32_t)row_bytes,
+                wbar);
   }
-  // Router rows (zero rows past E) into shared memory by every thread.
-  for (int i = threadIdx.x; i < 8 * (a.d / 8); i += blockDim.x) {
-    const int e = i / (a.d / 8), c = i - e * (a.d / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (e < a.E) v = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.w_r) + (int64_t)e * row_bytes + c * 16);
-    *reinterpret_cast<uint4*>(s_w + e * w_stride + c * 16) = v;
+  for (int i = threadIdx.x; i < (8 - a.E) * (a.d / 8); i += blockDim.x) {
+    const int e = a.E + i / (a.d / 8), c = i - (e - a.E) * (a.d / 8);
+    *reinterpret_cast<uint4*>(s_w + e * w_stride + c * 16) = make_uint4(0, 0, 0, 0);
   }
   __syncthreads();
 
@@ -640,6 +644,9 @@ __global__ void __launch_bounds__((kMmaWarps + 2) * 32, 1) router_mma_kernel(con
       }
       // After an abort, wait (bounded) for the copies still in flight.
       if (j < total) {
+        const uint64_t tw = global_timer_ns();
+        while (!bar_try_wait(wbar, 0))
+          if (global_timer_ns() - tw > kSmallWaitNs) break;
         for (int q = j - kMmaStages > 0 ? j - kMmaStages : 0; q < j; ++q) {
           const uint64_t t0 = global_timer_ns();
           while (!bar_try_wait(&full[q % kMmaStages], (uint32_t)(q / kMmaStages) & 1u))
@@ -666,6 +673,7 @@ __global__ void __launch_bounds__((kMmaWarps + 2) * 32, 1) router_mma_kernel(con
   // 8-column block (lane / 8) % 2.
   const uint32_t a_off = (uint32_t)((lane & 15) * kMmaRowStride + (lane >> 4) * 16 + warp * 512);
   const uint32_t b_base = smem_addr(s_w) + (uint32_t)((lane & 7) * w_stride + ((lane >> 3) & 1) * 16);
+  if (!__all_sync(0xffffffffu, bar_wait_bounded(wbar, 0, abort_flag))) return;
   int j = 0;
   for (int i = 0; i < my_groups; ++i) {
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -717,7 +725,7 @@ int run_router_mma(const RouterArgs& a, cudaStream_t s) {
   const int n_groups = (a.T + 15) / 16;
   const int grid = n_groups < 148 ? n_groups : 148;
   const size_t smem = (size_t)kMmaStages * kMmaStageBytes + (size_t)8 * (a.d * 2 + kMmaRowPad) +
-                      (size_t)2 * 16 * kMmaWarps * 8 * sizeof(float) + (2 * kMmaStages + 4) * sizeof(uint64_t) + 16;
+                      (size_t)2 * 16 * kMmaWarps * 8 * sizeof(float) + (2 * kMmaStages + 5) * sizeof(uint64_t) + 16;
   static PerDeviceOnce once;
   int dev = 0;
   DMOE_CUDA(cudaGetDevice(&dev));
