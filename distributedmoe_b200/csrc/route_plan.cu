@@ -312,6 +312,15 @@ __device__ __forceinline__ int field4(const uint64_t (&v)[4], int e) {
   return (int)((pick4(v, e >> 2) >> ((e & 3) * 16)) & 0xffffu);
 }
 
+// floor(f / T) for 0 <= f, T <= 32768 without a division: m = ceil(2^32 / T) makes
+// f * m / 2^32 = (f / T)(1 + eps) with eps < T / 2^32, so the error stays below 2^-17 while
+// the fractional part of f / T is at most 1 - 1/T <= 1 - 2^-15.
+// T = 1 (m would be 2^32) is marked by m = 0.
+__device__ __forceinline__ uint32_t div_magic(uint32_t T) {
+  return T <= 1 ? 0u : (uint32_t)((0x100000000ull + T - 1) / T);
+}
+__device__ __forceinline__ int div_small(int f, uint32_t m) { return m ? (int)__umulhi((uint32_t)f, m) : f; }
+
 size_t plan_few_smem(int64_t n) {
   const size_t na = (size_t)((n + 15) & ~int64_t(15));
   return 6 * na;  // expert and slot (int8), position and token (int16) per activation
@@ -331,6 +340,7 @@ __global__ void __launch_bounds__(kFewThreads, 1)
   int8_t* s_slot = s_ex + na;                                    // [n] slot of position p
   int16_t* s_pos = reinterpret_cast<int16_t*>(s_slot + na);      // [n] position of activation f (-1: none)
   int16_t* s_tok = s_pos + na;                                   // [n] token of position p
+  const uint32_t mT = div_magic((uint32_t)T), mk = div_magic((uint32_t)k);
   // 1. experts of all activations, coalesced over tokens (eight loads in flight per thread)
   for (int f0 = tid; f0 < n; f0 += 8 * kFewThreads) {
     int64_t v[8];
@@ -339,7 +349,7 @@ __global__ void __launch_bounds__(kFewThreads, 1)
       const int f = f0 + u * kFewThreads;
       v[u] = -1;
       if (f < n) {
-        const int s = f / T, t = f - s * T;
+        const int s = div_small(f, mT), t = f - s * T;
         v[u] = idx[(int64_t)t * k + s];
       }
     }
@@ -402,17 +412,21 @@ __global__ void __launch_bounds__(kFewThreads, 1)
   }
   if (tid == 0) offsets[E] = run;
   // 3. positions, in order within the chunk, into shared memory
+  int cs = div_small(lo, mT), ct = lo - cs * T;  // (slot, token) of activation f, stepped with f
   for (int f = lo; f < hi; ++f) {
     const int e = s_ex[f];
     int pos = -1;
     if (e >= 0) {
       pos = field4(base, e);
       add4(base, e, 1);
-      const int s = f / T;
-      s_tok[pos] = (int16_t)(f - s * T);
-      s_slot[pos] = (int8_t)s;
+      s_tok[pos] = (int16_t)ct;
+      s_slot[pos] = (int8_t)cs;
     }
     s_pos[f] = (int16_t)pos;
+    if (++ct == T) {
+      ct = 0;
+      ++cs;
+    }
   }
   __syncthreads();
   // 4. in-order (coalesced) stores: by position, then by (token, slot)
@@ -424,7 +438,7 @@ __global__ void __launch_bounds__(kFewThreads, 1)
   }
   if (inverse) {
     for (int i = tid; i < n; i += kFewThreads) {
-      const int t = i / k, s = i - t * k;
+      const int t = div_small(i, mk), s = i - t * k;
       inverse[i] = s_pos[s * T + t];
     }
   }

@@ -377,14 +377,16 @@ template <int EP>
 __device__ __forceinline__ void select_tile(const RouterArgs& a, const float* part, int nw, int t0, int nt,
                                             int lane) {
   // lane = token-in-chunk * EP + expert; groups of EP lanes hold one token's logits
+  const int e = lane % EP;
+  const float bias = (a.logit_bias && e < a.E) ? a.logit_bias[e] : 0.f;  // one load, before the tokens
   for (int r0 = 0; r0 < nt; r0 += 32 / EP) {
-    const int r = r0 + lane / EP, e = lane % EP;
+    const int r = r0 + lane / EP;
     const bool live = r < nt && e < a.E;
     float l = -INFINITY;
     if (live) {
       float v = 0.f;
       for (int w = 0; w < nw; ++w) v += part[(r * nw + w) * EP + e];
-      if (a.logit_bias) v += a.logit_bias[e];
+      if (a.logit_bias) v += bias;
       if (a.logits_out) a.logits_out[(int64_t)(t0 + r) * a.E + e] = v;
       l = v;
     }
