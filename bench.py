@@ -63,7 +63,7 @@ METRIC = "moe_layer_tokens_per_s"
 # DRAM bytes of the grouped MLP (both GEMMs of one launch) for the Mixtral workload, from
 # `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` over the layer's launches (one
 # pass): GEMM1 read + write, GEMM2 read + write.  None for workloads without a capture.
-MIXTRAL_MLP_TRAFFIC_BYTES = (1971 + 228 + 1409 + 58) * 10**6
+MIXTRAL_MLP_TRAFFIC_BYTES = (2018 + 228 + 1417 + 62) * 10**6
 
 
 class Workload:

@@ -359,7 +359,9 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
     if (lane == 0) a.ret[p] = code;
   }
   // Last CTA out raises the data flag on every rank: each thread's stores are made visible
-  // system-wide before its CTA counts itself done.
+  // system-wide before its CTA counts itself done.  One rank waits on no flag: the GEMM
+  // that reads the rows follows on the same stream.
+  if (a.peers.world == 1) return;
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {

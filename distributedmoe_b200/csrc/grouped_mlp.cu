@@ -1259,6 +1259,13 @@ int raster_mode(int dflt) {
   return dflt;
 }
 
+// Tile order of the down-projection GEMM alone (DMOE_GEMM2_RASTER), else raster_mode.
+int raster_mode2(int dflt) {
+  const char* v = getenv("DMOE_GEMM2_RASTER");
+  if (v && (v[0] == '0' || v[0] == '1' || v[0] == '2') && v[1] == 0) return v[0] - '0';
+  return raster_mode(dflt);
+}
+
 int prefetch_distance() {
   const char* v = getenv("DMOE_GEMM_PREFETCH");
   if (v && *v) return atoi(v);
@@ -1372,7 +1379,7 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
     int r = make_map(&td2, DT2, w_down, 3, dims, box);
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
-    GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
+    GemmArgs a2{Y, d, d, I, nt2, raster_mode2(2), act, prefetch_distance(), status};
     GemmArgs s1{H, I, I, d, nt1, 0, act, prefetch_distance(), status};
     GemmArgs s2{Y, d, d, I, nt2, 1, act, prefetch_distance(), status};
     apply_scatter(a2, sc);
@@ -1401,7 +1408,7 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
     int r = make_map(&td2, DT2, w_down, 3, dims, box);
     if (r) return r;
     GemmArgs a1{H, I, I, d, nt1, raster_mode(2), act, prefetch_distance(), status};
-    GemmArgs a2{Y, d, d, I, nt2, raster_mode(2), act, prefetch_distance(), status};
+    GemmArgs a2{Y, d, d, I, nt2, raster_mode2(2), act, prefetch_distance(), status};
     apply_scatter(a2, sc);
     apply_scales(a1, f8);
     // Pair tiles only.  With the segment-by-segment tile order a remainder's pair tile reads
