@@ -517,13 +517,18 @@ def _e2e_pipelined(moe, x_host, dev, stream, steps, dist) -> float:
         stream.wait_stream(copy_out)
 
     run(2)
-    _barrier(dist, dev)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    run(steps, t0)
-    t1.record(stream)
-    _barrier(dist, dev)
-    return _max_over_ranks(dist, t0.elapsed_time(t1) / steps, dev)
+    # Three timed repetitions, the median reported: the host links of these GPUs are shared
+    # with other jobs on the machine, and one repetition can catch another job's transfers.
+    reps = []
+    for _ in range(3):
+        _barrier(dist, dev)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        run(steps, t0)
+        t1.record(stream)
+        _barrier(dist, dev)
+        reps.append(_max_over_ranks(dist, t0.elapsed_time(t1) / steps, dev))
+    return sorted(reps)[1]
 
 
 def run_ours(args, dist, rank, world, local_rank):
@@ -689,7 +694,7 @@ def run_ours(args, dist, rank, world, local_rank):
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": total_tokens * D * 2, "d2h_bytes_per_step": total_tokens * D * 2,
                 "copies": "pinned host in/out every step; H2D of step i+1 and D2H of step i-1 on two copy "
-                          "streams overlapping step i",
+                          "streams overlapping step i; median of three timed repetitions",
                 "serial": {"value": total_tokens / (e2e_serial_ms * 1e-3), "ms_per_step": e2e_serial_ms,
                            "copies": "H2D, layer, D2H back to back on one stream"}},
         "gpu_launches": launches,

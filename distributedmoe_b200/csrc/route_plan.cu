@@ -297,19 +297,26 @@ constexpr int kFewMaxE = 16;
 constexpr int kFewMax = 32768;
 constexpr int kFewThreads = 1024;
 
-__device__ __forceinline__ uint64_t pick4(const uint64_t (&v)[4], int q) {
-  return q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
+// NW 64-bit words of four 16-bit fields each (experts 4q .. 4q+3 in word q).
+template <int NW>
+__device__ __forceinline__ uint64_t pick4(const uint64_t (&v)[NW], int q) {
+  uint64_t r = v[0];
+#pragma unroll
+  for (int i = 1; i < NW; ++i) r = (q == i) ? v[i] : r;
+  return r;
 }
 
-__device__ __forceinline__ void add4(uint64_t (&v)[4], int e, uint64_t amount) {
+template <int NW>
+__device__ __forceinline__ void add4(uint64_t (&v)[NW], int e, uint64_t amount) {
   const int q = e >> 2;
   const uint64_t inc = amount << ((e & 3) * 16);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] += (q == i) ? inc : 0ull;
+  for (int i = 0; i < NW; ++i) v[i] += (q == i) ? inc : 0ull;
 }
 
-__device__ __forceinline__ int field4(const uint64_t (&v)[4], int e) {
-  return (int)((pick4(v, e >> 2) >> ((e & 3) * 16)) & 0xffffu);
+template <int NW>
+__device__ __forceinline__ int field4(const uint64_t (&v)[NW], int e) {
+  return (int)((pick4<NW>(v, e >> 2) >> ((e & 3) * 16)) & 0xffffu);
 }
 
 // floor(f / T) for 0 <= f, T <= 32768 without a division: m = ceil(2^32 / T) makes
@@ -326,13 +333,14 @@ size_t plan_few_smem(int64_t n) {
   return 6 * na;  // expert and slot (int8), position and token (int16) per activation
 }
 
+template <int NW>
 __global__ void __launch_bounds__(kFewThreads, 1)
     plan_few_experts(const int64_t* __restrict__ idx, const void* __restrict__ w, int w_dtype, int T, int k, int E,
                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_token,
                      int32_t* __restrict__ perm_slot, int32_t* __restrict__ inverse, void* __restrict__ perm_weight) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
-  __shared__ uint64_t s_warp[32][4];
-  __shared__ uint64_t s_total[4];
+  __shared__ uint64_t s_warp[32][NW];
+  __shared__ uint64_t s_total[NW];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = T * k;
   const int na = (n + 15) & ~15;
@@ -363,14 +371,16 @@ __global__ void __launch_bounds__(kFewThreads, 1)
   // 2. counts of this thread's chunk, then a block-wide exclusive scan of the packed words
   const int c = (n + kFewThreads - 1) / kFewThreads;
   const int lo = min(n, tid * c), hi = min(n, lo + c);
-  uint64_t cnt[4] = {0, 0, 0, 0};
+  uint64_t cnt[NW];
+#pragma unroll
+  for (int q = 0; q < NW; ++q) cnt[q] = 0;
   for (int f = lo; f < hi; ++f) {
     const int e = s_ex[f];
-    if (e >= 0) add4(cnt, e, 1);
+    if (e >= 0) add4<NW>(cnt, e, 1);
   }
-  uint64_t incl[4];
+  uint64_t incl[NW];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < NW; ++q) {
     incl[q] = cnt[q];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -380,11 +390,11 @@ __global__ void __launch_bounds__(kFewThreads, 1)
   }
   if (lane == 31)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) s_warp[warp][q] = incl[q];
+    for (int q = 0; q < NW; ++q) s_warp[warp][q] = incl[q];
   __syncthreads();
   if (warp == 0) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NW; ++q) {
       uint64_t wv = s_warp[lane][q];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -396,14 +406,16 @@ __global__ void __launch_bounds__(kFewThreads, 1)
     }
   }
   __syncthreads();
-  uint64_t base[4];
+  uint64_t base[NW], tot[NW];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) base[q] = incl[q] - cnt[q] + (warp > 0 ? s_warp[warp - 1][q] : 0ull);
-  const uint64_t tot[4] = {s_total[0], s_total[1], s_total[2], s_total[3]};
+  for (int q = 0; q < NW; ++q) {
+    base[q] = incl[q] - cnt[q] + (warp > 0 ? s_warp[warp - 1][q] : 0ull);
+    tot[q] = s_total[q];
+  }
   int run = 0;
   for (int e = 0; e < E; ++e) {
-    const int ce = field4(tot, e);
-    add4(base, e, (uint64_t)run);  // base[e] = offsets[e] + earlier activations of e
+    const int ce = field4<NW>(tot, e);
+    add4<NW>(base, e, (uint64_t)run);  // base[e] = offsets[e] + earlier activations of e
     if (tid == e) {
       counts[e] = ce;
       offsets[e] = run;
@@ -417,8 +429,8 @@ __global__ void __launch_bounds__(kFewThreads, 1)
     const int e = s_ex[f];
     int pos = -1;
     if (e >= 0) {
-      pos = field4(base, e);
-      add4(base, e, 1);
+      pos = field4<NW>(base, e);
+      add4<NW>(base, e, 1);
       s_tok[pos] = (int16_t)ct;
       s_slot[pos] = (int8_t)cs;
     }
@@ -442,6 +454,25 @@ __global__ void __launch_bounds__(kFewThreads, 1)
       inverse[i] = s_pos[s * T + t];
     }
   }
+}
+
+template <int NW>
+int launch_plan_few(cudaStream_t s, const int64_t* idx, const void* w, int w_dtype, int T, int k, int E,
+                    int32_t* counts, int32_t* offsets, int32_t* perm_token, int32_t* perm_slot, int32_t* inverse,
+                    void* perm_weight) {
+  static PerDeviceOnce once;
+  int dev = 0;
+  DMOE_CUDA(cudaGetDevice(&dev));
+  const int r = once_per_device(once, dev, [] {
+    DMOE_CUDA(cudaFuncSetAttribute(plan_few_experts<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)plan_few_smem(kFewMax)));
+    return DMOE_OK;
+  });
+  if (r) return r;
+  plan_few_experts<NW><<<1, kFewThreads, plan_few_smem((int64_t)T * k), s>>>(idx, w, w_dtype, T, k, E, counts, offsets,
+                                                                              perm_token, perm_slot, inverse,
+                                                                              perm_weight);
+  return DMOE_OK;
 }
 
 bool plan_few_eligible(int T, int k, int E) {
@@ -512,17 +543,15 @@ extern "C" int dmoe_route_plan(const int64_t* idx, const void* w, int w_dtype, i
   cudaStream_t s = as_stream(stream);
   const int64_t n = (int64_t)T * k;
   if (n > 0 && plan_few_eligible(T, k, E)) {
-    static PerDeviceOnce once_few;
-    int dev = 0;
-    DMOE_CUDA(cudaGetDevice(&dev));
-    const int r = once_per_device(once_few, dev, [] {
-      DMOE_CUDA(cudaFuncSetAttribute(plan_few_experts, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)plan_few_smem(kFewMax)));
-      return DMOE_OK;
-    });
+    const int nw = (E + 3) / 4;
+    int r = DMOE_OK;
+    if (nw == 1) r = launch_plan_few<1>(s, idx, w, w_dtype, T, k, E, counts, offsets, perm_token, perm_slot, inverse,
+                                        perm_weight);
+    else if (nw == 2) r = launch_plan_few<2>(s, idx, w, w_dtype, T, k, E, counts, offsets, perm_token, perm_slot,
+                                             inverse, perm_weight);
+    else r = launch_plan_few<4>(s, idx, w, w_dtype, T, k, E, counts, offsets, perm_token, perm_slot, inverse,
+                                perm_weight);
     if (r) return r;
-    plan_few_experts<<<1, kFewThreads, plan_few_smem(n), s>>>(idx, w, w_dtype, T, k, E, counts, offsets, perm_token,
-                                                              perm_slot, inverse, perm_weight);
     DMOE_LAUNCH_CHECK();
     return DMOE_OK;
   }
