@@ -73,6 +73,8 @@ def _worker(rank, world, port, cfg, results):
         extra = {} if backend == B.NVLinkDirect else dict(io_buffer_size=cfg["io"], number_of_io_buffers=4)
         if backend == B.NVLinkDirect:
             extra["cuda_graphs"] = cfg.get("graphs", False)
+            if cfg.get("fp8"):
+                extra["expert_precision"] = "fp8"
         cl = ShardedCluster(E, k, d, torch.bfloat16, dev, stacked, activation="silu", renormalize=True,
                             forward_timeout=20000, backend=backend, max_tokens=T, blocks=blocks,
                             expert_block_policy=cfg.get("policy", "fifo"), **extra)
@@ -93,7 +95,13 @@ def _worker(rank, world, port, cfg, results):
                     assert y.shape == (0, d)
                     continue
                 _, _, logits = N.router(x.to(dev), inp.w_r.to(dev), k, want_logits=True)
-                ref = O.local_experts(x, logits.cpu(), inp.gate, inp.up, inp.down, k, act=O.ACT_SILU,
+                if cfg.get("fp8"):  # the oracle on the dequantised 8-bit operands
+                    xe = O.dequantize_rows_e4m3(*O.quantize_rows_e4m3(x))
+                    ge = O.dequantize_rows_e4m3(*O.quantize_rows_e4m3(inp.gate))
+                    ue = O.dequantize_rows_e4m3(*O.quantize_rows_e4m3(inp.up))
+                else:
+                    xe, ge, ue = x, inp.gate, inp.up
+                ref = O.local_experts(xe, logits.cpu(), ge, ue, inp.down, k, act=O.ACT_SILU,
                                       renormalize=True, compute_dtype=torch.float32)
                 yy = y.float().cpu()
                 errs.append(((yy - ref).norm() / ref.norm()).item())
@@ -154,6 +162,13 @@ def test_expert_parallel_two_gpus(backend):
 def test_expert_parallel_two_gpus_direct_cuda_graphs():
     """Decode-size batches replayed from CUDA graphs on both ranks (same step sequence)."""
     _run(2, dict(T=48, d=256, E=16, k=4, I=256, io=1024, seed=26, backend="direct", steps=6, graphs=True))
+
+
+@gpu
+def test_expert_parallel_two_gpus_direct_fp8():
+    """8-bit records cross NVLink (e4m3 codes + row scale) and the gate/up GEMMs run on e4m3
+    tensor cores on both ranks; against the oracle on the dequantised operands."""
+    _run(2, dict(T=640, d=256, E=8, k=2, I=384, io=1024, seed=27, backend="direct", fp8=True))
 
 
 @gpu
