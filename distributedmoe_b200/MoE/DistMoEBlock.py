@@ -265,7 +265,11 @@ class DistMoEBlock(nn.Module):
                         self.logger.error(f"health check: ping to EB #{experts_block_index} failed: {e}")
                         continue
                     try:
-                        packet = await asyncio.wait_for(pair.puller.recv(), timeout=1.0)
+                        # A pong may take as long as the configured P2P timeout (the sockets'
+                        # RCVTIMEO), as in the reference: a block busy in a long GPU call is late,
+                        # not dead.
+                        packet = await asyncio.wait_for(pair.puller.recv(),
+                                                        timeout=max(1.0, self.health_check_timeout / 1000.0))
                         header, _ = self.tensor_transfer_engine.deserialize_p2p_packet(packet)
                         if header != P2PHeaders.Pong.value:
                             raise RuntimeError(f"unexpected health check header {header}")

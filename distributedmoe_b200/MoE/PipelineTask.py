@@ -383,7 +383,7 @@ class ExpertsBlockPipelineTask(PipelineTask):
             await self.tensor_transfer_engine.async_send_metadata_to(
                 self.host_address, P2PHeaders.HostOutputBufferUnlocked.value, [(len(host_task_name), host_task_name)])
         except Exception as e:
-            self.logger.error(f"Experts block runtime error: {e}")
+            self.logger.error(f"Experts block runtime error: {type(e).__name__}: {e}")
         finally:
             if self.metrics_collector is not None:
                 self.metrics_collector.end_expert_run(task_id)

@@ -100,6 +100,9 @@ struct GemmArgs {
   int a_scale_ld;
   const float* b0_scale;
   const float* b1_scale;
+  // pair kernel only: a segment's last tile of at most 128 rows runs as an M=128 pair MMA
+  // (64 rows per CTA) at half the cost of a 256-row tile
+  int half_tiles;
 };
 
 // Destination of output row `row` of a plain GEMM with ESZ-byte elements (nullptr: not stored).
@@ -305,6 +308,86 @@ __device__ __forceinline__ float act_fn(float g, int act) {
 struct TileInfo {
   int row0, row_end, expert, nt;
 };
+
+// Epilogue of the gated GEMM for one row and 32 h columns from col0: gate and up accumulators
+// (fp32 bit patterns) -> act(gate) * up, scaled back first for e4m3 operands, stored as the
+// output type.  The row is valid.
+template <int DT>
+__device__ __forceinline__ void gated_store32(const GemmArgs& args, int row, int col0, int expert,
+                                              const uint32_t (&g)[32], const uint32_t (&u)[32]) {
+  if constexpr (DT == DMOE_F32) {
+    // fp32 operands (tf32 MMAs): h is stored in fp32, eight 16-byte vectors per 32 columns
+    float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      float h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        h[i] = act_fn(__uint_as_float(g[4 * v + i]), args.act) * __uint_as_float(u[4 * v + i]);
+      if (col0 + v * 4 < args.n_out) *reinterpret_cast<float4*>(dst + v * 4) = make_float4(h[0], h[1], h[2], h[3]);
+    }
+  } else {
+    uint32_t pk[16];
+    if constexpr (DT == DMOE_E4M3) {
+      // e4m3 operands: back to scale by the row's and each column's quantisation scale.
+      const float sa = args.a_scale[(int64_t)row * args.a_scale_ld];
+      const float* sg = args.b0_scale + (int64_t)expert * args.n_out;
+      const float* su = args.b1_scale + (int64_t)expert * args.n_out;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = col0 + 2 * i;
+        const float g0 = c < args.n_out ? __uint_as_float(g[2 * i]) * sa * sg[c] : 0.f;
+        const float u0 = c < args.n_out ? __uint_as_float(u[2 * i]) * sa * su[c] : 0.f;
+        const float g1 = c + 1 < args.n_out ? __uint_as_float(g[2 * i + 1]) * sa * sg[c + 1] : 0.f;
+        const float u1 = c + 1 < args.n_out ? __uint_as_float(u[2 * i + 1]) * sa * su[c + 1] : 0.f;
+        pk[i] = pack2<out_dtype<DT>()>(act_fn(g0, args.act) * u0, act_fn(g1, args.act) * u1);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
+        const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
+        pk[i] = pack2<DT>(h0, h1);
+      }
+    }
+    char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      if (col0 + v * 8 < args.n_out)
+        *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+  }
+}
+
+// Epilogue of the plain GEMM for one row and 32 output columns from col0: fp32 accumulators to
+// `out` (out_f32), else rounded to the output type at drow (the row's destination, local or
+// another GPU's return row; nullptr: not stored).
+template <int DT>
+__device__ __forceinline__ void plain_store32(const GemmArgs& args, char* drow, int row, bool valid, int col0,
+                                              const uint32_t (&y)[32]) {
+  if (valid && args.out_f32) {
+    float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      if (col0 + v * 4 < args.n_out)
+        *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+  } else if (drow != nullptr && DT == DMOE_F32) {
+    float* dst = reinterpret_cast<float*>(drow) + col0;
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      if (col0 + v * 4 < args.n_out)
+        *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+  } else if (drow != nullptr) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack2<DT == DMOE_F32 ? DMOE_BF16 : DT>(__uint_as_float(y[2 * i]),
+                                                                               __uint_as_float(y[2 * i + 1]));
+    char* dst = drow + (int64_t)col0 * 2;
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      if (col0 + v * 8 < args.n_out)
+        *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+  }
+}
 
 // The part of a segment [first, first + len) that a launch with split mode `split` computes
 // (see GemmSegs::split); updates len and returns the first row.
@@ -685,6 +768,7 @@ constexpr int A2_BYTES = 2 * SUB2_BYTES;
 constexpr int B2_BYTES = 2 * SUB2_BYTES;
 constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
 constexpr int kSmemBytes2 = 1024 + STAGES2 * STAGE2_BYTES + kBarBytes + kSegBytes;
+static_assert(kSmemBytes2 <= 227 * 1024, "pair kernel shared memory");
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -772,16 +856,17 @@ __device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
                : "memory");
 }
 
-template <int DT>
+template <int DT, int M = BM2>
 __host__ __device__ constexpr uint32_t make_idesc_pair() {
   return (1u << 4) | (operand_format<DT>() << 7) | (operand_format<DT>() << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM2 >> 4) << 24);
+         ((uint32_t)(M >> 4) << 24);
 }
 
 template <bool GATED, int DT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
-                            const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ GemmSegs segs,
+                            const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ CUtensorMap tm_b0h,
+                            const __grid_constant__ CUtensorMap tm_b1h, const __grid_constant__ GemmSegs segs,
                             const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -876,7 +961,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair; tile < total && ok; tile += n_pairs) {
         const TileInfo ti = decode_tile<BM2>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
                                         s_expert, s_tile);
-        const int arow = ti.row0 + (int)rank * 128;
+        // A segment's last tile of at most 128 rows is a half tile: 64 rows per CTA (the box
+        // still loads 128; the MMA reads the first 64).
+        const bool half = args.half_tiles && ti.row_end - ti.row0 <= 128;
+        const int arow = ti.row0 + (int)rank * (half ? 64 : 128);
         const int brow = GATED ? ti.nt * 128 : ti.nt * BN + (int)rank * 128;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_PRODUCER)) {
@@ -892,7 +980,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int h = 0; h < 2; ++h) {
             const int k0 = kb * 2 * RE + h * RE;  // a box past K reads zeros and still counts its bytes
             tma_load_2d_pair(sa + h * SUB2_BYTES, &tm_a, fbar, k0, arow);
-            tma_load_3d_pair(sb + h * SUB2_BYTES, tb, fbar, k0, brow, ti.expert);
+            if (GATED && half) {
+              // Half tile: each CTA takes 64 gate rows and the matching 64 up rows, so that both
+              // land in the same TMEM lanes (see the epilogue).
+              const int hrow = ti.nt * 128 + (int)rank * 64;
+              tma_load_3d_pair(sb + h * SUB2_BYTES, &tm_b0h, fbar, k0, hrow, ti.expert);
+              tma_load_3d_pair(sb + h * SUB2_BYTES + SUB2_BYTES / 2, &tm_b1h, fbar, k0, hrow, ti.expert);
+            } else {
+              tma_load_3d_pair(sb + h * SUB2_BYTES, tb, fbar, k0, brow, ti.expert);
+            }
           }
           const int kp = kb + args.prefetch;
           if (args.prefetch > 0 && kp < nk) {
@@ -925,7 +1021,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader CTA)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc_pair<DT>();
+      constexpr uint32_t idesc_full = make_idesc_pair<DT>();
+      constexpr uint32_t idesc_half = make_idesc_pair<DT, 128>();
       int stage = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -934,6 +1031,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair; tile < total && ok; tile += n_pairs) {
         if (!mbar_wait(&acce[acc], acc_ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) break;
         tc_fence_after();
+        const TileInfo ti = decode_tile<BM2>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
+                                        s_expert, s_tile);
+        const uint32_t idesc = (args.half_tiles && ti.row_end - ti.row0 <= 128) ? idesc_half : idesc_full;
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[stage], ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) {
@@ -984,87 +1084,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = mbar_wait(&accf[acc], acc_ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const int row = ti.row0 + (int)rank * 128 + q * 32 + lane;
-      const bool valid = row < ti.row_end;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if constexpr (GATED) {
+      if (args.half_tiles && ti.row_end - ti.row0 <= 128) {
+        // Half tile (M=128 pair MMA): this CTA's 64 rows sit in TMEM lanes 0-63 for output
+        // columns [0, 128) and again in lanes 64-127 for columns [128, 256) of the tile.
+        const int row = ti.row0 + (int)rank * 64 + (q & 1) * 32 + lane;
+        const bool valid = row < ti.row_end;
+        if constexpr (GATED) {
+          // The B tile of CTA c holds 64 gate rows, then the matching 64 up rows, for h columns
+          // nt*128 + 64c + [0, 64): warp q finds the gate values of h columns
+          // nt*128 + 64*(q >> 1) + [0, 64) at TMEM columns [0, 64) and the up values at [64, 128).
 #pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-          uint32_t g[32], u[32];
-          __syncwarp();
-          tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
-          const int col0 = ti.nt * (BN / 2) + j * 32;
-          if (valid && DT == DMOE_F32) {
-            // fp32 operands (tf32 MMAs): h is stored in fp32, eight 16-byte vectors per 32 columns
-            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              float h[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                h[i] = act_fn(__uint_as_float(g[4 * v + i]), args.act) * __uint_as_float(u[4 * v + i]);
-              if (col0 + v * 4 < args.n_out) *reinterpret_cast<float4*>(dst + v * 4) = make_float4(h[0], h[1], h[2], h[3]);
-            }
-          } else if (valid) {
-            uint32_t pk[16];
-            if constexpr (DT == DMOE_E4M3) {
-              // e4m3 operands: back to scale by the row's and each column's quantisation scale.
-              const float sa = args.a_scale[(int64_t)row * args.a_scale_ld];
-              const float* sg = args.b0_scale + (int64_t)ti.expert * args.n_out;
-              const float* su = args.b1_scale + (int64_t)ti.expert * args.n_out;
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int c = col0 + 2 * i;
-                const float g0 = c < args.n_out ? __uint_as_float(g[2 * i]) * sa * sg[c] : 0.f;
-                const float u0 = c < args.n_out ? __uint_as_float(u[2 * i]) * sa * su[c] : 0.f;
-                const float g1 = c + 1 < args.n_out ? __uint_as_float(g[2 * i + 1]) * sa * sg[c + 1] : 0.f;
-                const float u1 = c + 1 < args.n_out ? __uint_as_float(u[2 * i + 1]) * sa * su[c + 1] : 0.f;
-                pk[i] = pack2<out_dtype<DT>()>(act_fn(g0, args.act) * u0, act_fn(g1, args.act) * u1);
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
-                const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
-                pk[i] = pack2<DT>(h0, h1);
-              }
-            }
-            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (col0 + v * 8 < args.n_out)
-                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          for (int j = 0; j < 2; ++j) {
+            uint32_t g[32], u[32];
+            __syncwarp();
+            tmem_ld32x2(tbase + j * 32, tbase + 64 + j * 32, g, u);
+            if (valid) gated_store32<DT>(args, row, ti.nt * (BN / 2) + (q >> 1) * 64 + j * 32, ti.expert, g, u);
+          }
+        } else {
+          char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            uint32_t y[32];
+            __syncwarp();
+            tmem_ld32(tbase + j * 32, y);
+            plain_store32<DT>(args, drow, row, valid, ti.nt * BN + (q >> 1) * 128 + j * 32, y);
           }
         }
       } else {
-        char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
+        const int row = ti.row0 + (int)rank * 128 + q * 32 + lane;
+        const bool valid = row < ti.row_end;
+        if constexpr (GATED) {
 #pragma unroll 1
-        for (int j = 0; j < BN / 32; ++j) {
-          uint32_t y[32];
-          __syncwarp();
-          tmem_ld32(tbase + j * 32, y);
-          const int col0 = ti.nt * BN + j * 32;
-          if (valid && args.out_f32) {
-            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
-#pragma unroll
-            for (int v = 0; v < 8; ++v)
-              if (col0 + v * 4 < args.n_out)
-                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-          } else if (drow != nullptr && DT == DMOE_F32) {
-            float* dst = reinterpret_cast<float*>(drow) + col0;
-#pragma unroll
-            for (int v = 0; v < 8; ++v)
-              if (col0 + v * 4 < args.n_out)
-                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-          } else if (drow != nullptr) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
-            char* dst = drow + (int64_t)col0 * 2;
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (col0 + v * 8 < args.n_out)
-                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          for (int j = 0; j < 4; ++j) {
+            uint32_t g[32], u[32];
+            __syncwarp();
+            tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
+            if (valid) gated_store32<DT>(args, row, ti.nt * (BN / 2) + j * 32, ti.expert, g, u);
+          }
+        } else {
+          char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
+#pragma unroll 1
+          for (int j = 0; j < BN / 32; ++j) {
+            uint32_t y[32];
+            __syncwarp();
+            tmem_ld32(tbase + j * 32, y);
+            plain_store32<DT>(args, drow, row, valid, ti.nt * BN + j * 32, y);
           }
         }
       }
@@ -1209,7 +1274,8 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
 
 template <bool GATED, int DT>
 int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
-                    const GemmArgs& args, int max_pairs, cudaStream_t stream) {
+                    const GemmArgs& args, int max_pairs, cudaStream_t stream, const CUtensorMap* b0h = nullptr,
+                    const CUtensorMap* b1h = nullptr) {
   static PerDeviceOnce once;
   static int max_clusters[64];
   int dev = 0;
@@ -1243,7 +1309,9 @@ int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorM
   if (max_pairs >= 0 && max_pairs < pairs) pairs = max_pairs;
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs);
-  DMOE_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_2sm_kernel<GATED, DT>, a, b0, b1, segs, args));
+  DMOE_REQUIRE(!GATED || !args.half_tiles || (b0h && b1h), "grouped MLP: half tiles need the 64-row gate/up maps");
+  DMOE_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_2sm_kernel<GATED, DT>, a, b0, b1, b0h ? *b0h : b0, b1h ? *b1h : b1,
+                               segs, args));
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }
@@ -1257,6 +1325,12 @@ int raster_mode(int dflt) {
   const char* v = getenv("DMOE_GEMM_RASTER");
   if (v && (v[0] == '0' || v[0] == '1' || v[0] == '2') && v[1] == 0) return v[0] - '0';
   return dflt;
+}
+
+// Half-height pair tiles for segment remainders of at most 128 rows (DMOE_GEMM_HALF=0: off).
+int half_tiles_mode() {
+  const char* v = getenv("DMOE_GEMM_HALF");
+  return (v && v[0] == '0') ? 0 : 1;
 }
 
 // Tile order of the down-projection GEMM alone (DMOE_GEMM2_RASTER), else raster_mode.
@@ -1411,12 +1485,23 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
     GemmArgs a2{Y, d, d, I, nt2, raster_mode2(2), act, prefetch_distance(), status};
     apply_scatter(a2, sc);
     apply_scales(a1, f8);
-    // Pair tiles only.  With the segment-by-segment tile order a remainder's pair tile reads
+    a1.half_tiles = a2.half_tiles = half_tiles_mode();
+    CUtensorMap tgh, tuh;  // 64-row gate/up boxes for half tiles
+    if (a1.half_tiles) {
+      const uint64_t dims[3] = {(uint64_t)d, (uint64_t)I, (uint64_t)E_stack};
+      const uint32_t box[3] = {RE1, 64, 1};
+      r = make_map(&tgh, DT1, w_gate, 3, dims, box);
+      if (r) return r;
+      r = make_map(&tuh, DT1, w_up, 3, dims, box);
+      if (r) return r;
+    }
+    // Pair tiles only (a segment's last tile of at most 128 rows at half height).  With the segment-by-segment tile order a remainder's pair tile reads
     // the expert's weights from L2 next to the expert's other tiles, while a separate
     // single-SM launch re-reads them from DRAM after the pair launch (measured on the
     // Mixtral layer, about 1000 rows per expert: 2.22 ms for pair tiles only against 2.26 ms
     // split); the split pays off for ragged experts of a few hundred rows.
-    r = launch_gemm_2sm<true, DT1>(ta, tg, tu, segs, a1, -1, stream);
+    r = launch_gemm_2sm<true, DT1>(ta, tg, tu, segs, a1, -1, stream, a1.half_tiles ? &tgh : nullptr,
+                                   a1.half_tiles ? &tuh : nullptr);
     if (r) return r;
     return launch_gemm_2sm<false, DT2>(th, td2, td2, segs, a2, -1, stream);
   }

@@ -255,9 +255,9 @@ class _FakeTask:
 
 
 def test_health_checker_marks_a_silent_block_dead_then_alive_and_aborts_its_tasks():
-    """MoE/DistMoEBlock.py:312-414: a block that does not answer a ping within 1 s is marked
-    dead and the tasks dispatched to it are aborted (their activations go back to the
-    queues); when it answers again it is marked alive."""
+    """MoE/DistMoEBlock.py:312-414: a block that does not answer a ping within the P2P
+    timeout (1 s here) is marked dead and the tasks dispatched to it are aborted (their
+    activations go back to the queues); when it answers again it is marked alive."""
     import logging
     from distributedmoe_b200.MoE.DistMoEBlock import DistMoEBlock
 
@@ -265,6 +265,7 @@ def test_health_checker_marks_a_silent_block_dead_then_alive_and_aborts_its_task
     blk = object.__new__(DistMoEBlock)
     pair = _FakePair(eng)
     blk.monitoring_flag = True
+    blk.health_check_timeout = 1000  # ms
     blk.disabled_expert_blocks = set()
     blk.health_check_p2p_pairs = {"eb0": pair}
     blk.tensor_transfer_engine = eng
