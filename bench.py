@@ -724,6 +724,14 @@ def run_gemm_only(args):
     wd = _randn_bf16((Eg, D, w.I), w.w_std, gen, dev)
     Y = torch.empty(rows, D, dtype=torch.bfloat16, device=dev)
     ends = [rows * (e + 1) // Eg for e in range(Eg)]
+    if args.gemm_ragged:
+        # Ragged experts as top-k routing makes them: binomial-like sizes around rows / Eg.
+        gs = torch.Generator().manual_seed(w.seed + 5)
+        share = torch.full((Eg,), rows / Eg) + torch.randn(Eg, generator=gs) * (rows / Eg) ** 0.5
+        share = share.clamp_min(0)
+        cuts = (share.cumsum(0) * rows / share.sum()).round().long().tolist()
+        ends = [min(rows, max(0, c)) for c in cuts]
+        ends[-1] = rows
     fp8 = args.expert_precision == "fp8"
     if fp8:  # operands quantised once, outside the timed region: the GEMM pair alone is timed
         xq, xs = N.quantize_rows_e4m3(X)
@@ -747,6 +755,7 @@ def run_gemm_only(args):
     N.check_device_status(dev)
     ms = a.elapsed_time(b) / args.steps
     print(json.dumps({"mode": "gemm", "workload": w.name, "rows": rows, "experts": Eg, "ms_per_launch_pair": ms,
+                      "segment_rows": [b - a for a, b in zip([0] + ends[:-1], ends)] if args.gemm_ragged else None,
                       "precision": "e4m3 gate/up, bf16 down" if fp8 else "bf16",
                       "tflops": 6.0 * rows * D * w.I / (ms * 1e-3) / 1e12}), flush=True)
 
@@ -841,6 +850,8 @@ def main():
                          "precision: the headline line is bf16)")
     ap.add_argument("--gemm-rows", type=int, default=4096)
     ap.add_argument("--gemm-experts", type=int, default=2)
+    ap.add_argument("--gemm-ragged", action="store_true",
+                    help="--mode gemm: uneven expert segments (about rows/experts +- its square root)")
     args = ap.parse_args()
     if args.tokens is not None:
         if args.tokens < 1:
