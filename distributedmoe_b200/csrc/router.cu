@@ -803,9 +803,15 @@ int launch_router_small(int grid, int threads, size_t smem, cudaStream_t s, cons
   static PerDeviceOnce once;
   int dev = 0;
   DMOE_CUDA(cudaGetDevice(&dev));
+  // The attribute is set once per device, so to the most any call can ask for: the ring, and
+  // partials for tile_t * nw <= 64 (tile_t = 32 KB / row bytes, nw = row bytes / 512), plus
+  // the barriers.  A first call with a small row must not cap later calls with larger rows.
+  constexpr size_t kMaxSmem = (size_t)kSmallStages * kSmallStageBytes + 2 * 64 * 8 * sizeof(float) +
+                              (kSmallStages + 4) * sizeof(uint64_t) + 16;
+  DMOE_REQUIRE(smem <= kMaxSmem, "router: %zu bytes of shared memory exceed %zu", smem, kMaxSmem);
   const int r = once_per_device(once, dev, [&] {
     DMOE_CUDA(cudaFuncSetAttribute(router_small_kernel<DT, EP, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
+                                   (int)kMaxSmem));
     return DMOE_OK;
   });
   if (r) return r;
