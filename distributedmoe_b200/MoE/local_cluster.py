@@ -8,9 +8,12 @@ sit on any local GPUs (NVLink peers) or share the host's GPU.
 
 from __future__ import annotations
 
+import os
+import random
 import socket
 import threading
-from typing import List, Optional, Sequence
+import time
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 
@@ -23,15 +26,49 @@ from distributedmoe_b200.TensorTransferEngine.TensorTransferEngine import (
 from distributedmoe_b200.TensorTransferEngine.utils import HandshakeType, TransferProtocol
 
 
+def _ephemeral_range() -> Tuple[int, int]:
+    try:
+        with open("/proc/sys/net/ipv4/ip_local_port_range") as f:
+            lo, hi = (int(v) for v in f.read().split()[:2])
+        return lo, hi
+    except (OSError, ValueError):
+        return 32768, 60999
+
+
 def free_ports(n: int) -> List[int]:
+    """n distinct ports that are free now, to be bound as listeners soon after.  They are
+    taken below the kernel's ephemeral range when it leaves room: a port from that range can
+    be handed to an outgoing connection (the engines' own ZeroMQ connects, the process
+    group's sockets) between this pick and the bind, and a listener that then fails to bind
+    leaves its peers waiting for a hand-shake."""
+    lo, _ = _ephemeral_range()
+    base, top = 20000, min(lo, 32000)
     socks, ports = [], []
-    for _ in range(n):
-        s = socket.socket()
-        s.bind(("127.0.0.1", 0))
-        socks.append(s)
-        ports.append(s.getsockname()[1])
-    for s in socks:
-        s.close()
+    try:
+        if top - base >= 8 * n:
+            rng = random.Random(os.getpid() ^ int(time.time_ns()))
+            tried = 0
+            while len(ports) < n and tried < 64 * n:
+                tried += 1
+                port = rng.randrange(base, top)
+                if port in ports:
+                    continue
+                s = socket.socket()
+                try:
+                    s.bind(("127.0.0.1", port))
+                except OSError:
+                    s.close()
+                    continue
+                socks.append(s)
+                ports.append(port)
+        while len(ports) < n:  # no room below the ephemeral range: let the kernel choose
+            s = socket.socket()
+            s.bind(("127.0.0.1", 0))
+            socks.append(s)
+            ports.append(s.getsockname()[1])
+    finally:
+        for s in socks:
+            s.close()
     return ports
 
 

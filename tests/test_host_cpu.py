@@ -501,3 +501,20 @@ def test_window_descriptors_and_instance_tables_agree_over_two_gloo_ranks():
     assert out[0] == out[1]
     descs = out[0][0]
     assert [struct.unpack("!Q", d[:8])[0] for d in descs] == [1000, 1001]
+
+
+def test_free_ports_are_distinct_bindable_and_outside_the_ephemeral_range():
+    """Listener ports are picked below the kernel's ephemeral range (where outgoing
+    connections take their source ports), distinct, and free to bind."""
+    import socket
+    from distributedmoe_b200.MoE.local_cluster import _ephemeral_range, free_ports
+
+    ports = free_ports(41)
+    assert len(set(ports)) == 41
+    lo, _ = _ephemeral_range()
+    if min(lo, 32000) - 20000 >= 8 * 41:
+        assert all(20000 <= p < min(lo, 32000) for p in ports)
+    for p in ports[:5]:
+        s = socket.socket()
+        s.bind(("127.0.0.1", p))
+        s.close()
