@@ -672,16 +672,20 @@ class DistMoEBlock(nn.Module):
     def _direct_tile_policy(self, T: int) -> int:
         """Tile shape of the grouped MLP from the rows an expert instance can expect (every
         rank sending about T tokens): the segment table is on the device, so the host cannot
-        see the actual sizes.  A hundred rows per expert or more: 256-row pair tiles (a
-        segment's last tile of at most 128 rows runs swapped, its MMA work scaling with the
-        rows); fewer: single-SM tiles.  DMOE_TILE_POLICY (0 auto, 1 pair, 2 single, 3 pair +
-        single-SM remainders) overrides."""
+        see the actual sizes.  Hundreds of rows per expert or more: 256-row pair tiles; a few
+        hundred: pair tiles plus single-SM tiles for remainders of at most 128 rows (a
+        segment of 257-384 rows then costs three SM-tiles, not four); fewer: single-SM tiles.
+        DMOE_TILE_POLICY (0 auto, 1 pair, 2 single, 3 pair + single remainders) overrides."""
         forced = os.environ.get("DMOE_TILE_POLICY")
         if forced:
             return int(forced)
         ep = self._ep
         expected = ep["world"] * T * self.top_k / max(1, ep["inst"].n_inst)
-        return N.TILES_PAIR if expected >= 128 else N.TILES_SINGLE
+        if expected >= 768:
+            return N.TILES_PAIR
+        if expected >= 128:
+            return N.TILES_PAIR_SPLIT
+        return N.TILES_SINGLE
 
     def _direct_step(self, x: torch.Tensor) -> torch.Tensor:
         ep = self._ep

@@ -100,16 +100,7 @@ struct GemmArgs {
   int a_scale_ld;
   const float* b0_scale;
   const float* b1_scale;
-  // pair kernel only: how a segment's last tile of at most 128 rows runs -- 0 as a full
-  // tile, 1 as an M=128 pair MMA (64 rows per CTA), 2 swapped (the weights as the M=256
-  // operand, the tile's rows as N = rows rounded up to 16)
-  int small_mode;
 };
-
-// How the pair kernel runs tile `ti` (see GemmArgs::small_mode).
-__device__ __forceinline__ int small_kind(const GemmArgs& args, int row0, int row_end) {
-  return (args.small_mode != 0 && row_end - row0 <= 128) ? args.small_mode : 0;
-}
 
 // Destination of output row `row` of a plain GEMM with ESZ-byte elements (nullptr: not stored).
 template <int ESZ>
@@ -314,95 +305,6 @@ __device__ __forceinline__ float act_fn(float g, int act) {
 struct TileInfo {
   int row0, row_end, expert, nt;
 };
-
-// Epilogue of the gated GEMM for one row and 32 h columns from col0: gate and up accumulators
-// (fp32 bit patterns) -> act(gate) * up, scaled back first for e4m3 operands, stored as the
-// output type.  The row is valid.
-template <int DT>
-__device__ __forceinline__ void gated_store32(const GemmArgs& args, int row, int col0, int expert,
-                                              const uint32_t (&g)[32], const uint32_t (&u)[32]) {
-  if constexpr (DT == DMOE_F32) {
-    // fp32 operands (tf32 MMAs): h is stored in fp32, eight 16-byte vectors per 32 columns
-    float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
-#pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      float h[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        h[i] = act_fn(__uint_as_float(g[4 * v + i]), args.act) * __uint_as_float(u[4 * v + i]);
-      if (col0 + v * 4 < args.n_out) *reinterpret_cast<float4*>(dst + v * 4) = make_float4(h[0], h[1], h[2], h[3]);
-    }
-  } else {
-    uint32_t pk[16];
-    if constexpr (DT == DMOE_E4M3) {
-      // e4m3 operands: back to scale by the row's and each column's quantisation scale.
-      const float sa = args.a_scale[(int64_t)row * args.a_scale_ld];
-      const float* sg = args.b0_scale + (int64_t)expert * args.n_out;
-      const float* su = args.b1_scale + (int64_t)expert * args.n_out;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = col0 + 2 * i;
-        const float g0 = c < args.n_out ? __uint_as_float(g[2 * i]) * sa * sg[c] : 0.f;
-        const float u0 = c < args.n_out ? __uint_as_float(u[2 * i]) * sa * su[c] : 0.f;
-        const float g1 = c + 1 < args.n_out ? __uint_as_float(g[2 * i + 1]) * sa * sg[c + 1] : 0.f;
-        const float u1 = c + 1 < args.n_out ? __uint_as_float(u[2 * i + 1]) * sa * su[c + 1] : 0.f;
-        pk[i] = pack2<out_dtype<DT>()>(act_fn(g0, args.act) * u0, act_fn(g1, args.act) * u1);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
-        const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
-        pk[i] = pack2<DT>(h0, h1);
-      }
-    }
-    char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
-#pragma unroll
-    for (int v = 0; v < 4; ++v)
-      if (col0 + v * 8 < args.n_out)
-        *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-  }
-}
-
-// One element of type ODT (fp32 or a 16-bit type) at p.
-template <int ODT>
-__device__ __forceinline__ void store_elem(char* p, float v) {
-  if constexpr (ODT == DMOE_F32)
-    *reinterpret_cast<float*>(p) = v;
-  else
-    *reinterpret_cast<uint16_t*>(p) = (uint16_t)(pack2<ODT>(v, 0.f) & 0xFFFFu);
-}
-
-// Epilogue of the plain GEMM for one row and 32 output columns from col0: fp32 accumulators to
-// `out` (out_f32), else rounded to the output type at drow (the row's destination, local or
-// another GPU's return row; nullptr: not stored).
-template <int DT>
-__device__ __forceinline__ void plain_store32(const GemmArgs& args, char* drow, int row, bool valid, int col0,
-                                              const uint32_t (&y)[32]) {
-  if (valid && args.out_f32) {
-    float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
-#pragma unroll
-    for (int v = 0; v < 8; ++v)
-      if (col0 + v * 4 < args.n_out)
-        *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-  } else if (drow != nullptr && DT == DMOE_F32) {
-    float* dst = reinterpret_cast<float*>(drow) + col0;
-#pragma unroll
-    for (int v = 0; v < 8; ++v)
-      if (col0 + v * 4 < args.n_out)
-        *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-  } else if (drow != nullptr) {
-    uint32_t pk[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) pk[i] = pack2<DT == DMOE_F32 ? DMOE_BF16 : DT>(__uint_as_float(y[2 * i]),
-                                                                               __uint_as_float(y[2 * i + 1]));
-    char* dst = drow + (int64_t)col0 * 2;
-#pragma unroll
-    for (int v = 0; v < 4; ++v)
-      if (col0 + v * 8 < args.n_out)
-        *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-  }
-}
 
 // The part of a segment [first, first + len) that a launch with split mode `split` computes
 // (see GemmSegs::split); updates len and returns the first row.
@@ -782,9 +684,7 @@ constexpr int SUB2_BYTES = 128 * BK * 2;      // one box: 128 rows x 128 bytes
 constexpr int A2_BYTES = 2 * SUB2_BYTES;
 constexpr int B2_BYTES = 2 * SUB2_BYTES;
 constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
-constexpr int kXchBytes = 2 * 32 * 33 * 4;  // swapped gated tiles: up values from warps 2-3 to 0-1
-constexpr int kSmemBytes2 = 1024 + STAGES2 * STAGE2_BYTES + kBarBytes + kSegBytes + kXchBytes;
-static_assert(kSmemBytes2 <= 227 * 1024, "pair kernel shared memory");
+constexpr int kSmemBytes2 = 1024 + STAGES2 * STAGE2_BYTES + kBarBytes + kSegBytes;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -872,17 +772,16 @@ __device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
                : "memory");
 }
 
-template <int DT, int M = BM2>
+template <int DT>
 __host__ __device__ constexpr uint32_t make_idesc_pair() {
   return (1u << 4) | (operand_format<DT>() << 7) | (operand_format<DT>() << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
+         ((uint32_t)(BM2 >> 4) << 24);
 }
 
 template <bool GATED, int DT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
-                            const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ CUtensorMap tm_b0h,
-                            const __grid_constant__ CUtensorMap tm_b1h, const __grid_constant__ GemmSegs segs,
+                            const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ GemmSegs segs,
                             const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -892,15 +791,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acce = accf + 2;
   uint64_t* fin = acce + 2;
   uint64_t* bye = fin + 1;
-  uint64_t* xfull = bye + 1;    // [2] swapped gated tiles: up values written (per warp pair)
-  uint64_t* xempty = xfull + 2;  // [2] ... and read
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bye + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int32_t* s_start = reinterpret_cast<int32_t*>(smem + STAGES2 * STAGE2_BYTES + kBarBytes);
   int32_t* s_end = s_start + (kMaxSegDev + 1);
   int32_t* s_expert = s_end + (kMaxSegDev + 1);
   int32_t* s_tile = s_expert + (kMaxSegDev + 1);
-  float* s_xch = reinterpret_cast<float*>(s_tile + (kMaxSegDev + 1));  // [2][32][33]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -951,10 +847,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(fin, 1);
     mbar_init(bye, 1);
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(&xfull[x], 1);
-      mbar_init(&xempty[x], 1);
-    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -984,12 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair; tile < total && ok; tile += n_pairs) {
         const TileInfo ti = decode_tile<BM2>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
                                         s_expert, s_tile);
-        // A segment's last tile of at most 128 rows may run small: as a half tile (64 rows per
-        // CTA) or swapped (N = rows rounded up to 16, half of them from each CTA).  The box
-        // still loads 128 rows; the MMA reads the first ones.
-        const int kind = small_kind(args, ti.row0, ti.row_end);
-        const int n_pad = (ti.row_end - ti.row0 + 15) & ~15;
-        const int arow = ti.row0 + (int)rank * (kind == 1 ? 64 : (kind == 2 ? n_pad / 2 : 128));
+        const int arow = ti.row0 + (int)rank * 128;
         const int brow = GATED ? ti.nt * 128 : ti.nt * BN + (int)rank * 128;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_PRODUCER)) {
@@ -1005,15 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int h = 0; h < 2; ++h) {
             const int k0 = kb * 2 * RE + h * RE;  // a box past K reads zeros and still counts its bytes
             tma_load_2d_pair(sa + h * SUB2_BYTES, &tm_a, fbar, k0, arow);
-            if (GATED && kind != 0) {
-              // Small tile: each CTA takes 64 gate rows and the matching 64 up rows, so that both
-              // land in TMEM lanes of this CTA (see the epilogue).
-              const int hrow = ti.nt * 128 + (int)rank * 64;
-              tma_load_3d_pair(sb + h * SUB2_BYTES, &tm_b0h, fbar, k0, hrow, ti.expert);
-              tma_load_3d_pair(sb + h * SUB2_BYTES + SUB2_BYTES / 2, &tm_b1h, fbar, k0, hrow, ti.expert);
-            } else {
-              tma_load_3d_pair(sb + h * SUB2_BYTES, tb, fbar, k0, brow, ti.expert);
-            }
+            tma_load_3d_pair(sb + h * SUB2_BYTES, tb, fbar, k0, brow, ti.expert);
           }
           const int kp = kb + args.prefetch;
           if (args.prefetch > 0 && kp < nk) {
@@ -1046,8 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader CTA)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc_full = make_idesc_pair<DT>();
-      constexpr uint32_t idesc_half = make_idesc_pair<DT, 128>();
+      constexpr uint32_t idesc = make_idesc_pair<DT>();
       int stage = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -1056,14 +934,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair; tile < total && ok; tile += n_pairs) {
         if (!mbar_wait(&acce[acc], acc_ph ^ 1u, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const TileInfo ti = decode_tile<BM2>(tile, total_m, args.n_tiles_n, args.raster_n_fast, n_seg, s_start, s_end,
-                                        s_expert, s_tile);
-        const int kind = small_kind(args, ti.row0, ti.row_end);
-        // Swapped: M = 256 weight rows (128 per CTA), N = the tile's rows rounded up to 16.
-        const uint32_t n_pad = (uint32_t)((ti.row_end - ti.row0 + 15) & ~15);
-        const uint32_t idesc_swap = (idesc_full & ~(0x3Fu << 17)) | ((n_pad >> 3) << 17);
-        const uint32_t idesc = kind == 1 ? idesc_half : (kind == 2 ? idesc_swap : idesc_full);
-        const bool swap = kind == 2;
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[stage], ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_MMA)) {
@@ -1077,10 +947,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 8; ++k) {
             // sub-box k/4 (16 KB = 1024 in the descriptor's 16-byte units), then +32 bytes of K per MMA
             const uint64_t off = (uint64_t)((k >> 2) * (SUB2_BYTES >> 4) + 2 * (k & 3));
-            if (swap)
-              umma_f16_pair<DT>(d_tmem, bd + off, ad + off, idesc, (kb | k) != 0);
-            else
-              umma_f16_pair<DT>(d_tmem, ad + off, bd + off, idesc, (kb | k) != 0);
+            umma_f16_pair<DT>(d_tmem, ad + off, bd + off, idesc, (kb | k) != 0);
           }
           umma_commit_both(&empty[stage]);
           if (++stage == STAGES2) {
@@ -1109,7 +976,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;
     const uint32_t acce_leader0 = map_to_cta(smem_u32(&acce[0]), 0);
-    int xcount = 0;  // exchanges of this warp's pair so far (swapped gated tiles)
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int tile = pair; tile < total; tile += n_pairs) {
@@ -1118,135 +984,87 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = mbar_wait(&accf[acc], acc_ph, abort_flag, args.status, DMOE_DEVERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
+      const int row = ti.row0 + (int)rank * 128 + q * 32 + lane;
+      const bool valid = row < ti.row_end;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      const int kind = small_kind(args, ti.row0, ti.row_end);
-      if (kind == 2) {
-        // Swapped tile: TMEM lane 32q + lane of this CTA is weight row 128 * rank + 32q + lane of
-        // the tile, TMEM column i is the tile's row row0 + i.
-        constexpr int ODT = out_dtype<DT>();
-        constexpr int ESZ = ODT == DMOE_F32 ? 4 : 2;
-        const int n_tok = ti.row_end - ti.row0;
-        const int nch = (n_tok + 31) / 32;
-        if constexpr (GATED) {
-          // Lanes 0-63 hold the gate rows of h columns hc0 + [0, 64), lanes 64-127 the up rows of
-          // the same columns: warps 2-3 hand their up values to warps 0-1 through shared memory.
-          const int pr = q & 1;
-          const int hcol = ti.nt * (BN / 2) + (int)rank * 64 + pr * 32 + lane;
-          float* xch = s_xch + pr * 32 * 33;
-          bool alive = true;
+      if constexpr (GATED) {
 #pragma unroll 1
-          for (int c = 0; c < nch && alive; ++c) {
-            uint32_t v[32];
-            __syncwarp();
-            tmem_ld32(tbase + c * 32, v);
-            if (q >= 2) {
-              if (xcount > 0)
-                alive = __all_sync(0xffffffffu, mbar_wait(&xempty[pr], (uint32_t)(xcount - 1) & 1u, abort_flag,
-                                                          args.status, DMOE_DEVERR_TIMEOUT_EPILOGUE));
-              if (!alive) break;
+        for (int j = 0; j < 4; ++j) {
+          uint32_t g[32], u[32];
+          __syncwarp();
+          tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
+          const int col0 = ti.nt * (BN / 2) + j * 32;
+          if (valid && DT == DMOE_F32) {
+            // fp32 operands (tf32 MMAs): h is stored in fp32, eight 16-byte vectors per 32 columns
+            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) xch[lane * 33 + i] = __uint_as_float(v[i]);
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&xfull[pr]);
+            for (int v = 0; v < 8; ++v) {
+              float h[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                h[i] = act_fn(__uint_as_float(g[4 * v + i]), args.act) * __uint_as_float(u[4 * v + i]);
+              if (col0 + v * 4 < args.n_out) *reinterpret_cast<float4*>(dst + v * 4) = make_float4(h[0], h[1], h[2], h[3]);
+            }
+          } else if (valid) {
+            uint32_t pk[16];
+            if constexpr (DT == DMOE_E4M3) {
+              // e4m3 operands: back to scale by the row's and each column's quantisation scale.
+              const float sa = args.a_scale[(int64_t)row * args.a_scale_ld];
+              const float* sg = args.b0_scale + (int64_t)ti.expert * args.n_out;
+              const float* su = args.b1_scale + (int64_t)ti.expert * args.n_out;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int c = col0 + 2 * i;
+                const float g0 = c < args.n_out ? __uint_as_float(g[2 * i]) * sa * sg[c] : 0.f;
+                const float u0 = c < args.n_out ? __uint_as_float(u[2 * i]) * sa * su[c] : 0.f;
+                const float g1 = c + 1 < args.n_out ? __uint_as_float(g[2 * i + 1]) * sa * sg[c + 1] : 0.f;
+                const float u1 = c + 1 < args.n_out ? __uint_as_float(u[2 * i + 1]) * sa * su[c + 1] : 0.f;
+                pk[i] = pack2<out_dtype<DT>()>(act_fn(g0, args.act) * u0, act_fn(g1, args.act) * u1);
+              }
             } else {
-              alive = __all_sync(0xffffffffu, mbar_wait(&xfull[pr], (uint32_t)xcount & 1u, abort_flag, args.status,
-                                                        DMOE_DEVERR_TIMEOUT_EPILOGUE));
-              if (!alive) break;
-              float u[32];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) u[i] = xch[lane * 33 + i];
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&xempty[pr]);
-              if (hcol < args.n_out) {
-                float sg = 1.f, su = 1.f;
-                if constexpr (DT == DMOE_E4M3) {
-                  sg = args.b0_scale[(int64_t)ti.expert * args.n_out + hcol];
-                  su = args.b1_scale[(int64_t)ti.expert * args.n_out + hcol];
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  const int t = ti.row0 + c * 32 + i;
-                  if (t >= ti.row_end) continue;
-                  float g = __uint_as_float(v[i]), up = u[i];
-                  if constexpr (DT == DMOE_E4M3) {
-                    const float sa = args.a_scale[(int64_t)t * args.a_scale_ld];
-                    g *= sa * sg;
-                    up *= sa * su;
-                  }
-                  store_elem<ODT>(reinterpret_cast<char*>(args.out) + ((int64_t)t * args.ldo + hcol) * ESZ,
-                                  act_fn(g, args.act) * up);
-                }
+              for (int i = 0; i < 16; ++i) {
+                const float h0 = act_fn(__uint_as_float(g[2 * i]), args.act) * __uint_as_float(u[2 * i]);
+                const float h1 = act_fn(__uint_as_float(g[2 * i + 1]), args.act) * __uint_as_float(u[2 * i + 1]);
+                pk[i] = pack2<DT>(h0, h1);
               }
             }
-            ++xcount;
-          }
-        } else {
-          const int col = ti.nt * BN + (int)rank * 128 + q * 32 + lane;
-#pragma unroll 1
-          for (int c = 0; c < nch; ++c) {
-            uint32_t y[32];
-            __syncwarp();
-            tmem_ld32(tbase + c * 32, y);
-            if (col < args.n_out) {
+            char* dst = reinterpret_cast<char*>(args.out) + ((int64_t)row * args.ldo + col0) * 2;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int t = ti.row0 + c * 32 + i;
-                if (t >= ti.row_end) continue;
-                if (args.out_f32) {
-                  reinterpret_cast<float*>(args.out)[(int64_t)t * args.ldo + col] = __uint_as_float(y[i]);
-                } else {
-                  char* drow = out_row<ESZ>(args, t, true);
-                  if (drow != nullptr) store_elem<ODT>(drow + (int64_t)col * ESZ, __uint_as_float(y[i]));
-                }
-              }
-            }
-          }
-        }
-      } else if (kind == 1) {
-        // Half tile (M=128 pair MMA): this CTA's 64 rows sit in TMEM lanes 0-63 for output
-        // columns [0, 128) and again in lanes 64-127 for columns [128, 256) of the tile.
-        const int row = ti.row0 + (int)rank * 64 + (q & 1) * 32 + lane;
-        const bool valid = row < ti.row_end;
-        if constexpr (GATED) {
-          // The B tile of CTA c holds 64 gate rows, then the matching 64 up rows, for h columns
-          // nt*128 + 64c + [0, 64): warp q finds the gate values of h columns
-          // nt*128 + 64*(q >> 1) + [0, 64) at TMEM columns [0, 64) and the up values at [64, 128).
-#pragma unroll 1
-          for (int j = 0; j < 2; ++j) {
-            uint32_t g[32], u[32];
-            __syncwarp();
-            tmem_ld32x2(tbase + j * 32, tbase + 64 + j * 32, g, u);
-            if (valid) gated_store32<DT>(args, row, ti.nt * (BN / 2) + (q >> 1) * 64 + j * 32, ti.expert, g, u);
-          }
-        } else {
-          char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
-#pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-            uint32_t y[32];
-            __syncwarp();
-            tmem_ld32(tbase + j * 32, y);
-            plain_store32<DT>(args, drow, row, valid, ti.nt * BN + (q >> 1) * 128 + j * 32, y);
+            for (int v = 0; v < 4; ++v)
+              if (col0 + v * 8 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
           }
         }
       } else {
-        const int row = ti.row0 + (int)rank * 128 + q * 32 + lane;
-        const bool valid = row < ti.row_end;
-        if constexpr (GATED) {
+        char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
 #pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-            uint32_t g[32], u[32];
-            __syncwarp();
-            tmem_ld32x2(tbase + j * 32, tbase + BN / 2 + j * 32, g, u);
-            if (valid) gated_store32<DT>(args, row, ti.nt * (BN / 2) + j * 32, ti.expert, g, u);
-          }
-        } else {
-          char* const drow = args.out_f32 ? nullptr : out_row<DT == DMOE_F32 ? 4 : 2>(args, row, valid);
-#pragma unroll 1
-          for (int j = 0; j < BN / 32; ++j) {
-            uint32_t y[32];
-            __syncwarp();
-            tmem_ld32(tbase + j * 32, y);
-            plain_store32<DT>(args, drow, row, valid, ti.nt * BN + j * 32, y);
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t y[32];
+          __syncwarp();
+          tmem_ld32(tbase + j * 32, y);
+          const int col0 = ti.nt * BN + j * 32;
+          if (valid && args.out_f32) {
+            float* dst = reinterpret_cast<float*>(args.out) + (int64_t)row * args.ldo + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col0 + v * 4 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else if (drow != nullptr && DT == DMOE_F32) {
+            float* dst = reinterpret_cast<float*>(drow) + col0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col0 + v * 4 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 4) = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else if (drow != nullptr) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack2<DT>(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1]));
+            char* dst = drow + (int64_t)col0 * 2;
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col0 + v * 8 < args.n_out)
+                *reinterpret_cast<uint4*>(dst + v * 16) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
           }
         }
       }
@@ -1391,8 +1209,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
 
 template <bool GATED, int DT>
 int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmSegs& segs,
-                    const GemmArgs& args, int max_pairs, cudaStream_t stream, const CUtensorMap* b0h = nullptr,
-                    const CUtensorMap* b1h = nullptr) {
+                    const GemmArgs& args, int max_pairs, cudaStream_t stream) {
   static PerDeviceOnce once;
   static int max_clusters[64];
   int dev = 0;
@@ -1426,9 +1243,7 @@ int launch_gemm_2sm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorM
   if (max_pairs >= 0 && max_pairs < pairs) pairs = max_pairs;
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs);
-  DMOE_REQUIRE(!GATED || !args.small_mode || (b0h && b1h), "grouped MLP: small tiles need the 64-row gate/up maps");
-  DMOE_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_2sm_kernel<GATED, DT>, a, b0, b1, b0h ? *b0h : b0, b1h ? *b1h : b1,
-                               segs, args));
+  DMOE_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_2sm_kernel<GATED, DT>, a, b0, b1, segs, args));
   DMOE_LAUNCH_CHECK();
   return DMOE_OK;
 }
@@ -1442,15 +1257,6 @@ int raster_mode(int dflt) {
   const char* v = getenv("DMOE_GEMM_RASTER");
   if (v && (v[0] == '0' || v[0] == '1' || v[0] == '2') && v[1] == 0) return v[0] - '0';
   return dflt;
-}
-
-// How the pair kernel runs a segment's last tile of at most 128 rows (GemmArgs::small_mode):
-// DMOE_GEMM_SMALL=0 as a full tile, 1 at half height (an M=128 pair MMA drives 64 of each
-// SM's 128 TMEM lanes and took as long as a full tile), 2 swapped (default).
-int small_tiles_mode() {
-  const char* v = getenv("DMOE_GEMM_SMALL");
-  if (v && (v[0] == '0' || v[0] == '1' || v[0] == '2') && v[1] == 0) return v[0] - '0';
-  return 2;
 }
 
 // Tile order of the down-projection GEMM alone (DMOE_GEMM2_RASTER), else raster_mode.
@@ -1605,24 +1411,12 @@ int run_mlp2(const void* X, const void* w_gate, const void* w_up, const void* w_
     GemmArgs a2{Y, d, d, I, nt2, raster_mode2(2), act, prefetch_distance(), status};
     apply_scatter(a2, sc);
     apply_scales(a1, f8);
-    a1.small_mode = a2.small_mode = small_tiles_mode();
-    CUtensorMap tgh, tuh;  // 64-row gate/up boxes for small tiles
-    if (a1.small_mode) {
-      const uint64_t dims[3] = {(uint64_t)d, (uint64_t)I, (uint64_t)E_stack};
-      const uint32_t box[3] = {RE1, 64, 1};
-      r = make_map(&tgh, DT1, w_gate, 3, dims, box);
-      if (r) return r;
-      r = make_map(&tuh, DT1, w_up, 3, dims, box);
-      if (r) return r;
-    }
-    // Pair tiles only (a segment's last tile of at most 128 rows swapped, see
-    // small_tiles_mode).  With the segment-by-segment tile order a remainder's pair tile reads
+    // Pair tiles only.  With the segment-by-segment tile order a remainder's pair tile reads
     // the expert's weights from L2 next to the expert's other tiles, while a separate
     // single-SM launch re-reads them from DRAM after the pair launch (measured on the
     // Mixtral layer, about 1000 rows per expert: 2.22 ms for pair tiles only against 2.26 ms
     // split); the split pays off for ragged experts of a few hundred rows.
-    r = launch_gemm_2sm<true, DT1>(ta, tg, tu, segs, a1, -1, stream, a1.small_mode ? &tgh : nullptr,
-                                   a1.small_mode ? &tuh : nullptr);
+    r = launch_gemm_2sm<true, DT1>(ta, tg, tu, segs, a1, -1, stream);
     if (r) return r;
     return launch_gemm_2sm<false, DT2>(th, td2, td2, segs, a2, -1, stream);
   }

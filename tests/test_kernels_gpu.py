@@ -342,11 +342,10 @@ def test_grouped_mlp_matches_fp32_reference(dtype, act, E, d, I, sizes):
 @gpu
 @pytest.mark.parametrize("env", [{"DMOE_GEMM_HYBRID": "1"}, {"DMOE_GEMM_RASTER": "0"}, {"DMOE_GEMM_RASTER": "1"},
                                  {"DMOE_GEMM_VARIANT": "1sm"}, {"DMOE_GEMM_HYBRID": "1", "DMOE_GEMM_RASTER": "1"},
-                                 {"DMOE_GEMM_SMALL": "0"}, {"DMOE_GEMM_SMALL": "1"}, {"DMOE_GEMM2_RASTER": "1"}])
+                                 {"DMOE_GEMM2_RASTER": "1"}])
 def test_grouped_mlp_launch_variants(env, monkeypatch):
     """The non-default launch shapes (pair tiles with single-SM remainders, the other tile
-    orders, single-SM tiles only, a segment's last tile of at most 128 rows as a full or a
-    half-height pair tile instead of swapped) give the same results."""
+    orders, single-SM tiles only) give the same results."""
     for k, v in env.items():
         monkeypatch.setenv(k, v)
     N = _nat()
