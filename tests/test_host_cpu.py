@@ -146,8 +146,10 @@ def _port_worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_engine_port_exchange_over_two_gloo_ranks():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_engine_port_exchange_over_gloo_ranks(world):
+    """Every rank gets the same table of engine ports, with no port used twice (4 ranks pick
+    84 listener ports)."""
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
@@ -164,9 +166,9 @@ def test_engine_port_exchange_over_two_gloo_ranks():
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
-    assert sorted(out) == [0, 1]
-    t0, t1 = out[0][0], out[1][0]
-    assert t0 == t1  # every rank sees the same table
+    assert sorted(out) == list(range(world))
+    t0 = out[0][0]
+    assert all(out[r][0] == t0 for r in range(world))  # every rank sees the same table
     assert not out[0][1]
     for r, row in enumerate(t0):
         assert row["device"] == r and row["address"] == "127.0.0.1"
