@@ -121,7 +121,8 @@ class DistExpertsBlock(nn.Module):
         args = (self.tensor_transfer_engine, self.io_buffer_size, self.hidden_features, self.dtype, self.device)
         self.input_buffers_pool = BuffersPool(self.number_of_io_buffers, *args)
         self.output_buffers_pool = BuffersPool(self.number_of_io_buffers, *args)
-        assert self.tensor_transfer_engine.handshake()
+        if not self.tensor_transfer_engine.handshake():
+            raise RuntimeError(f"expert block {self.experts_block_index}: hand-shake with its host failed (see the log)")
 
     def parse_host_io_buffer_descriptors(self, metadata: List[Tuple[int, bytes]]) -> None:
         n = struct.unpack("!H", metadata[0][1])[0]

@@ -148,7 +148,8 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         with _ENGINES_LOCK:
             _ENGINES[self.host_name] = self
         self._init_transfer_engine()
-        assert self.handshake()
+        if not self.handshake():
+            raise RuntimeError(f"{self.host_name}: transfer-engine hand-shake failed (see the log)")
 
     def _init_transfer_engine(self) -> None:
         self.transfer_engine = "cuda-ipc"
@@ -158,18 +159,23 @@ class NVLinkTensorTransferEngine(TensorTransferEngine):
         dev = torch.cuda.current_device() if torch.cuda.is_available() else -1
         return struct.pack("!Ih", self.pid, dev) + socket.gethostname().encode()[:200]
 
+    HANDSHAKE_DEADLINE_S = 120.0
+
     def handshake_with_remote(self, remote_name: str) -> bool:
         """Exchange (pid, device, hostname); CLIENT speaks first, as the NIXL agents do
         (``NIXLTensorTransferEngine.py:87-108``)."""
+        # A peer that never answers (its process or listener failed during set-up) ends the
+        # hand-shake with an error after HANDSHAKE_DEADLINE_S instead of a retry loop forever.
+        dl = self.HANDSHAKE_DEADLINE_S
         try:
             if self.handshake_type == HandshakeType.CLIENT:
                 ident = self._identity()
-                self.send_metadata_to(remote_name, 0, (len(ident), ident))
-                header, body = self.get_metadata_from(remote_name)
+                self.send_metadata_to(remote_name, 0, (len(ident), ident), deadline_s=dl)
+                header, body = self.get_metadata_from(remote_name, deadline_s=dl)
             elif self.handshake_type == HandshakeType.SERVER:
-                header, body = self.get_metadata_from(remote_name)
+                header, body = self.get_metadata_from(remote_name, deadline_s=dl)
                 ident = self._identity()
-                self.send_metadata_to(remote_name, 0, (len(ident), ident))
+                self.send_metadata_to(remote_name, 0, (len(ident), ident), deadline_s=dl)
             else:
                 return True
             assert header == 0

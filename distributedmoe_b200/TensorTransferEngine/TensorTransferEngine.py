@@ -230,20 +230,29 @@ class TensorTransferEngine(ABC):
             return asyncio.run(coro_fn())
         return asyncio.run_coroutine_threadsafe(coro_fn(), loop).result()
 
-    def send_metadata_to(self, remote_name: str, header: int, body) -> None:
-        """Blocking send; retries on timeout (``TensorTransferEngine.py:258-275``)."""
+    def send_metadata_to(self, remote_name: str, header: int, body, deadline_s: Optional[float] = None) -> None:
+        """Blocking send; retries on timeout (``TensorTransferEngine.py:258-275``), for at most
+        deadline_s seconds when given (then TimeoutError)."""
+        t0 = timeit.default_timer()
         while True:
             try:
                 return self._run_blocking(lambda: self.async_send_metadata_to(remote_name, header, body))
             except (asyncio.TimeoutError, zmq.Again):
+                if deadline_s is not None and timeit.default_timer() - t0 > deadline_s:
+                    raise TimeoutError(f"no metadata could be sent to {remote_name} in {deadline_s:.0f} s") from None
                 self.logger.warning(f"Waiting to send metadata to {remote_name}, retrying...")
 
-    def get_metadata_from(self, remote_name: str) -> Tuple[int, List[Tuple[int, bytes]]]:
-        """Blocking receive; retries on timeout (``TensorTransferEngine.py:281-295``)."""
+    def get_metadata_from(self, remote_name: str,
+                          deadline_s: Optional[float] = None) -> Tuple[int, List[Tuple[int, bytes]]]:
+        """Blocking receive; retries on timeout (``TensorTransferEngine.py:281-295``), for at
+        most deadline_s seconds when given (then TimeoutError)."""
+        t0 = timeit.default_timer()
         while True:
             try:
                 return self._run_blocking(lambda: self.async_get_metadata_from(remote_name))
             except (asyncio.TimeoutError, zmq.Again):
+                if deadline_s is not None and timeit.default_timer() - t0 > deadline_s:
+                    raise TimeoutError(f"no metadata from {remote_name} in {deadline_s:.0f} s") from None
                 self.logger.warning(f"Waiting for metadata from {remote_name}, retrying...")
 
     # ------------------------------------------------------------------ completion

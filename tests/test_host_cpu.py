@@ -520,3 +520,25 @@ def test_free_ports_are_distinct_bindable_and_outside_the_ephemeral_range():
         s = socket.socket()
         s.bind(("127.0.0.1", p))
         s.close()
+
+
+def test_blocking_metadata_exchange_gives_up_after_its_deadline():
+    """The set-up hand-shake's blocking receive and send retry on socket timeouts, but for at
+    most deadline_s seconds: a peer that never answers ends in TimeoutError, not a hang."""
+    import asyncio
+    import logging
+    import time
+
+    eng = _bare_engine()
+    eng.logger = logging.getLogger("test.deadline")
+
+    def never(_coro_fn):
+        raise asyncio.TimeoutError
+
+    eng._run_blocking = never
+    t0 = time.monotonic()
+    with pytest.raises(TimeoutError, match="no metadata from peer"):
+        eng.get_metadata_from("peer", deadline_s=0.05)
+    with pytest.raises(TimeoutError, match="could be sent to peer"):
+        eng.send_metadata_to("peer", 0, (0, b""), deadline_s=0.05)
+    assert time.monotonic() - t0 < 10
